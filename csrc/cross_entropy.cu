@@ -1,0 +1,123 @@
+// Cross-entropy over (vocabulary-sharded) bf16 logits, in two small kernels
+// around the LM-head GEMM, whose kEpiCE epilogue already produced, per row and
+// per 256-column tile, the tile max and the sum of exp(z - tile max), plus the
+// target logit when the target falls in this shard.
+//
+//   md_ce_stats    : combine the column tiles of each row into (max, sumexp)
+//                    and, for an unsharded vocabulary, finish with
+//                    lse = max + log(sumexp) and loss = lse - z_target.
+//   md_ce_backward : dlogits = (exp(z - lse) - onehot(target)) * g / rows,
+//                    recomputed from the stored bf16 logits, so the fp32
+//                    softmax ([rows, V] floats) is never materialised.
+//
+// With tensor parallelism the per-row (max, sumexp, z_target) of each rank are
+// combined across the group (MAX, rescaled SUM, SUM) before lse is formed —
+// the decomposition of the reference's _VocabParallelCrossEntropy
+// (tensor_parallel.py:451-492) with [rows]-sized instead of [rows, V]-sized
+// intermediates.
+#include "md_sm100.cuh"
+
+namespace md {
+namespace ce {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+__global__ void stats_kernel(const float* __restrict__ tmax, const float* __restrict__ tsum, int tiles, int M,
+                             float* __restrict__ row_max, float* __restrict__ row_sum,
+                             const float* __restrict__ tgt_logit, float* __restrict__ lse_out,
+                             float* __restrict__ loss_out) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  float mx = -INFINITY;
+  for (int t = 0; t < tiles; ++t) mx = fmaxf(mx, tmax[static_cast<long long>(t) * M + m]);
+  float s = 0.f;
+  for (int t = 0; t < tiles; ++t) {
+    const float tm = tmax[static_cast<long long>(t) * M + m];
+    if (tm != -INFINITY) s += tsum[static_cast<long long>(t) * M + m] * exp2f((tm - mx) * kLog2e);
+  }
+  if (row_max) row_max[m] = mx;
+  if (row_sum) row_sum[m] = s;
+  if (lse_out) {
+    const float lse = mx + log2f(s) * kLn2;
+    lse_out[m] = lse;
+    if (loss_out) loss_out[m] = lse - tgt_logit[m];
+  }
+}
+
+// One CTA per row block; each thread handles 8 consecutive logits per step.
+__global__ void backward_kernel(const __nv_bfloat16* __restrict__ logits, long long ldl,
+                                const float* __restrict__ lse, const long long* __restrict__ target,
+                                long long col_offset, const float* __restrict__ grad_out, float scale,
+                                __nv_bfloat16* __restrict__ dlogits, long long ldd, int M, int V) {
+  const float g = scale * (grad_out != nullptr ? grad_out[0] : 1.f);
+  const int nvec = (V + 7) / 8;
+  for (int m = blockIdx.x; m < M; m += gridDim.x) {
+    const float l = lse[m];
+    const long long t = target[m] - col_offset;
+    const __nv_bfloat16* zr = logits + m * ldl;
+    __nv_bfloat16* dr = dlogits + m * ldd;
+    for (int j = threadIdx.x; j < nvec; j += blockDim.x) {
+      const int c0 = j * 8;
+      float z[8];
+      if (c0 + 8 <= V) {
+        const uint4 w = reinterpret_cast<const uint4*>(zr)[j];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(ws[q]);
+          z[2 * q] = f.x;
+          z[2 * q + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) z[e] = (c0 + e < V) ? __bfloat162float(zr[c0 + e]) : -INFINITY;
+      }
+      float d[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float p = exp2f((z[e] - l) * kLog2e);
+        d[e] = (p - ((c0 + e) == t ? 1.f : 0.f)) * g;
+      }
+      if (c0 + 8 <= V) {
+        uint4 o;
+        o.x = pack_bf16x2(d[0], d[1]);
+        o.y = pack_bf16x2(d[2], d[3]);
+        o.z = pack_bf16x2(d[4], d[5]);
+        o.w = pack_bf16x2(d[6], d[7]);
+        reinterpret_cast<uint4*>(dr)[j] = o;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (c0 + e < V) dr[c0 + e] = __float2bfloat16_rn(d[e]);
+      }
+    }
+  }
+}
+
+}  // namespace ce
+}  // namespace md
+
+extern "C" {
+
+int md_ce_stats(const float* tmax, const float* tsum, int tiles, int M, float* row_max, float* row_sum,
+                const float* tgt_logit, float* lse_out, float* loss_out, cudaStream_t s) {
+  if (M <= 0 || tiles <= 0) return -1;
+  md::ce::stats_kernel<<<(M + 255) / 256, 256, 0, s>>>(tmax, tsum, tiles, M, row_max, row_sum, tgt_logit, lse_out,
+                                                       loss_out);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int md_ce_backward(const void* logits, long long ldl, const float* lse, const long long* target, long long col_offset,
+                   const float* grad_out, float scale, void* dlogits, long long ldd, int M, int V, cudaStream_t s) {
+  if (M <= 0 || V <= 0 || (ldl % 8) || (ldd % 8) || (reinterpret_cast<uintptr_t>(logits) & 15u) ||
+      (reinterpret_cast<uintptr_t>(dlogits) & 15u))
+    return -1;
+  int grid = M < 148 * 16 ? M : 148 * 16;
+  md::ce::backward_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(logits), ldl, lse, target,
+                                               col_offset, grad_out, scale, reinterpret_cast<__nv_bfloat16*>(dlogits),
+                                               ldd, M, V);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // extern "C"

@@ -1,0 +1,209 @@
+// Token + position embedding, forward and backward, for bf16 activations.
+//
+// forward : out[m, :] = wte[ids[m] - vocab_start, :] (0 if the id is outside
+//           this rank's vocabulary shard) + (add_pos ? wpe[m % S, :] : 0)
+// backward: d_wte[id - vocab_start] += dx[m]   (fp32 vector atomics; rows are
+//           rarely hit twice in one warp-step, so contention is low)
+//           d_wpe[s] (+)= sum_b dx[b*S + s]    (fixed-order, deterministic)
+//
+// Reads the bf16 shadow of the tables; gradients land in fp32.
+// Replaces VocabParallelEmbedding.forward (reference tensor_parallel.py:409-416)
+// and Embedding.forward (models/gpt.py:183-185).
+#include "md_sm100.cuh"
+
+namespace md {
+namespace emb {
+
+// One warp per token row; each lane moves 8 bf16 (16 B) per step.
+__global__ void embed_fwd_kernel(const long long* __restrict__ ids, const __nv_bfloat16* __restrict__ wte,
+                                 long long ldw, const __nv_bfloat16* __restrict__ wpe, long long ldp,
+                                 __nv_bfloat16* __restrict__ out, long long ldo, int M, int S, int C,
+                                 long long vocab_start, long long vocab_rows, int add_pos) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nvec = C / 8;
+  for (int m = blockIdx.x * warps + (threadIdx.x >> 5); m < M; m += gridDim.x * warps) {
+    const long long id = ids[m] - vocab_start;
+    const bool own = id >= 0 && id < vocab_rows;
+    const int s = m % S;
+    for (int j = lane; j < nvec; j += 32) {
+      float v[8];
+      if (own) {
+        const uint4 w = reinterpret_cast<const uint4*>(wte + id * ldw)[j];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(ws[q]);
+          v[2 * q] = f.x;
+          v[2 * q + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      }
+      if (add_pos) {
+        const uint4 w = reinterpret_cast<const uint4*>(wpe + s * ldp)[j];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(ws[q]);
+          v[2 * q] += f.x;
+          v[2 * q + 1] += f.y;
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16x2(v[0], v[1]);
+      o.y = pack_bf16x2(v[2], v[3]);
+      o.z = pack_bf16x2(v[4], v[5]);
+      o.w = pack_bf16x2(v[6], v[7]);
+      reinterpret_cast<uint4*>(out + m * ldo)[j] = o;
+    }
+  }
+}
+
+__global__ void embed_bwd_wte_kernel(const long long* __restrict__ ids, const __nv_bfloat16* __restrict__ dx,
+                                     long long ldx, float* __restrict__ dwte, long long ldg, int M, int C,
+                                     long long vocab_start, long long vocab_rows) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nvec = C / 8;
+  for (int m = blockIdx.x * warps + (threadIdx.x >> 5); m < M; m += gridDim.x * warps) {
+    const long long id = ids[m] - vocab_start;
+    if (id < 0 || id >= vocab_rows) continue;
+    for (int j = lane; j < nvec; j += 32) {
+      const uint4 w = reinterpret_cast<const uint4*>(dx + m * ldx)[j];
+      const float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), c = unpack_bf16x2(w.z), d = unpack_bf16x2(w.w);
+      float4* dst = reinterpret_cast<float4*>(dwte + id * ldg + j * 8);
+      atomicAdd(dst, make_float4(a.x, a.y, b.x, b.y));
+      atomicAdd(dst + 1, make_float4(c.x, c.y, d.x, d.y));
+    }
+  }
+}
+
+// d_wpe[s, c] (+)= sum_b dx[b*S + s, c]; one thread per (s, pair of columns).
+__global__ void embed_bwd_wpe_kernel(const __nv_bfloat16* __restrict__ dx, long long ldx, float* __restrict__ dwpe,
+                                     long long ldg, int B, int S, int C, int accumulate) {
+  const int pairs = C / 2;
+  const long long total = static_cast<long long>(S) * pairs;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int s = static_cast<int>(i / pairs);
+    const int c2 = static_cast<int>(i - static_cast<long long>(s) * pairs);
+    float ax = 0.f, ay = 0.f;
+    for (int b = 0; b < B; ++b) {
+      const uint32_t w = reinterpret_cast<const uint32_t*>(dx + (static_cast<long long>(b) * S + s) * ldx)[c2];
+      const float2 f = unpack_bf16x2(w);
+      ax += f.x;
+      ay += f.y;
+    }
+    float2* dst = reinterpret_cast<float2*>(dwpe + s * ldg) + c2;
+    if (accumulate) {
+      float2 o = *dst;
+      ax += o.x;
+      ay += o.y;
+    }
+    *dst = make_float2(ax, ay);
+  }
+}
+
+// Column sums of a bf16 matrix into fp32: out[n] (+)= sum_m x[m, n].
+// Stage 1 writes one partial row per row-chunk, stage 2 adds them in order.
+__global__ void colsum_partial_kernel(const __nv_bfloat16* __restrict__ x, long long ldx, int M, int N,
+                                      int rows_per_chunk, float* __restrict__ partial) {
+  const int c2 = blockIdx.x * blockDim.x + threadIdx.x;  // column pair
+  const int chunk = blockIdx.y;
+  if (2 * c2 >= N) return;
+  const int r0 = chunk * rows_per_chunk;
+  const int r1 = min(M, r0 + rows_per_chunk);
+  float ax = 0.f, ay = 0.f;
+  const bool pair = 2 * c2 + 1 < N;
+  for (int r = r0; r < r1; ++r) {
+    if (pair) {
+      const float2 f = unpack_bf16x2(reinterpret_cast<const uint32_t*>(x + r * ldx)[c2]);
+      ax += f.x;
+      ay += f.y;
+    } else {
+      ax += __bfloat162float(x[r * ldx + 2 * c2]);
+    }
+  }
+  partial[static_cast<long long>(chunk) * N + 2 * c2] = ax;
+  if (pair) partial[static_cast<long long>(chunk) * N + 2 * c2 + 1] = ay;
+}
+
+__global__ void colsum_final_kernel(const float* __restrict__ partial, int chunks, int N, float* __restrict__ out,
+                                    int accumulate) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float s = 0.f;
+  for (int c = 0; c < chunks; ++c) s += partial[static_cast<long long>(c) * N + n];
+  out[n] = accumulate ? out[n] + s : s;
+}
+
+}  // namespace emb
+}  // namespace md
+
+namespace {
+bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+
+extern "C" {
+
+int md_embed_fwd(const long long* ids, const void* wte, long long ldw, const void* wpe, long long ldp, void* out,
+                 long long ldo, int M, int S, int C, long long vocab_start, long long vocab_rows, int add_pos,
+                 cudaStream_t s) {
+  if (M <= 0 || (C % 8) || (ldw % 8) || (ldo % 8) || !a16(wte) || !a16(out)) return -1;
+  if (add_pos && ((ldp % 8) || !a16(wpe))) return -1;
+  const int warps = 8;
+  int grid = (M + warps - 1) / warps;
+  if (grid > 148 * 16) grid = 148 * 16;
+  md::emb::embed_fwd_kernel<<<grid, warps * 32, 0, s>>>(
+      ids, reinterpret_cast<const __nv_bfloat16*>(wte), ldw, reinterpret_cast<const __nv_bfloat16*>(wpe), ldp,
+      reinterpret_cast<__nv_bfloat16*>(out), ldo, M, S, C, vocab_start, vocab_rows, add_pos);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// d_wte must already hold the values to accumulate onto (zero it for a fresh gradient).
+int md_embed_bwd_wte(const long long* ids, const void* dx, long long ldx, float* dwte, long long ldg, int M, int C,
+                     long long vocab_start, long long vocab_rows, cudaStream_t s) {
+  if (M <= 0 || (C % 8) || (ldx % 8) || (ldg % 4) || !a16(dx) || !a16(dwte)) return -1;
+  const int warps = 8;
+  int grid = (M + warps - 1) / warps;
+  if (grid > 148 * 16) grid = 148 * 16;
+  md::emb::embed_bwd_wte_kernel<<<grid, warps * 32, 0, s>>>(ids, reinterpret_cast<const __nv_bfloat16*>(dx), ldx,
+                                                            dwte, ldg, M, C, vocab_start, vocab_rows);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int md_embed_bwd_wpe(const void* dx, long long ldx, float* dwpe, long long ldg, int B, int S, int C, int accumulate,
+                     cudaStream_t s) {
+  if (B <= 0 || S <= 0 || (C % 2) || (ldx % 2) || (ldg % 2)) return -1;
+  const long long total = static_cast<long long>(S) * (C / 2);
+  int grid = static_cast<int>((total + 255) / 256);
+  if (grid > 148 * 16) grid = 148 * 16;
+  md::emb::embed_bwd_wpe_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(dx), ldx, dwpe, ldg, B, S,
+                                                     C, accumulate);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// Number of row chunks (partial rows) md_colsum uses; the caller provides
+// partial scratch of md_colsum_chunks(M, N) * N floats.
+int md_colsum_chunks(int M, int N) {
+  const int col_blocks = (N / 2 + 255) / 256 + 1;
+  int chunks = (148 * 8) / col_blocks;
+  if (chunks < 1) chunks = 1;
+  const int max_chunks = (M + 63) / 64;
+  return chunks < max_chunks ? chunks : max_chunks;
+}
+
+int md_colsum(const void* x, long long ldx, int M, int N, float* partial, float* out, int accumulate, cudaStream_t s) {
+  if (M <= 0 || N <= 0 || (ldx % 2) || (reinterpret_cast<uintptr_t>(x) & 3u)) return -1;
+  const int chunks = md_colsum_chunks(M, N);
+  const int rows_per_chunk = (M + chunks - 1) / chunks;
+  dim3 grid((N / 2 + 1 + 255) / 256, chunks);
+  md::emb::colsum_partial_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, N,
+                                                       rows_per_chunk, partial);
+  md::emb::colsum_final_kernel<<<(N + 255) / 256, 256, 0, s>>>(partial, chunks, N, out, accumulate);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // extern "C"

@@ -1,0 +1,393 @@
+// LayerNorm forward/backward for bf16 activations with fp32 statistics and
+// fp32 affine parameters (the model keeps fp32 master weights).
+//
+// A row of C elements (C % 8 == 0) is handled by a "team" of T threads; every
+// thread holds up to V 16-byte vectors (8 bf16 each) in registers, so the row
+// is read once.  T scales with C so the per-thread footprint stays at <= 32
+// values: T=32 up to C=1024, 64 up to 2048, 128 up to 4096, 256 up to 8192.
+//
+// Backward accumulates dgamma/dbeta per thread over the rows its team
+// processes, then reduces across teams in shared memory in a fixed order and
+// writes one partial row per CTA; md_ln_reduce_partials sums the CTA partials
+// in a fixed order too.  The result is bit-reproducible, which keeps
+// LayerNorm gradients of tensor-parallel replicas identical on every rank.
+//
+// The backward optionally fuses two column sums the transformer block needs
+// anyway (the bias gradients of the row-parallel projections on either side of
+// the norm): the column sum of the incoming residual gradient and of the
+// produced input gradient.
+//
+// Replaces nn.LayerNorm (reference models/gpt.py:158,160,199) and the ATen
+// layer_norm kernels it dispatches to.
+#include "md_sm100.cuh"
+
+namespace md {
+namespace ln {
+
+constexpr int kThreads = 256;
+
+template <int T>
+__device__ __forceinline__ float team_sum(float v, float* scratch) {
+  // scratch: [kThreads / 32] floats per CTA (used only when T > 32)
+#pragma unroll
+  for (int o = (T < 32 ? T : 32) / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if constexpr (T > 32) {
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int team_first_warp = (threadIdx.x / T) * (T / 32);
+    __syncwarp();
+    if (lane == 0) scratch[warp] = v;
+    // All warps of a team must publish before any reads.  Teams are aligned to
+    // warps, so a named barrier per team is not needed: the whole CTA syncs.
+    __syncthreads();
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < T / 32; ++w) s += scratch[team_first_warp + w];
+    __syncthreads();
+    v = s;
+  }
+  return v;
+}
+
+template <int T, int V>
+__global__ void __launch_bounds__(kThreads) ln_fwd_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                         const float* __restrict__ gamma,
+                                                         const float* __restrict__ beta,
+                                                         __nv_bfloat16* __restrict__ y, long long ldy,
+                                                         float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                                                         int M, int C, float eps) {
+  __shared__ float scratch[kThreads / 32];
+  const int teams_per_cta = kThreads / T;
+  const int team = threadIdx.x / T;
+  const int t = threadIdx.x % T;
+  const int nvec = C / 8;
+  const float inv_c = 1.0f / static_cast<float>(C);
+  // Every team runs the same number of iterations so the CTA-wide barriers in
+  // team_sum (T > 32) line up; rows past M are computed on a clamped row and
+  // not stored.
+  const int rows_per_pass = gridDim.x * teams_per_cta;
+  const int passes = (M + rows_per_pass - 1) / rows_per_pass;
+  for (int pass = 0; pass < passes; ++pass) {
+    const int row = pass * rows_per_pass + blockIdx.x * teams_per_cta + team;
+    const bool valid = row < M;
+    const int r = valid ? row : M - 1;
+    float v[V][8];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int j = t + i * T;
+      if (j < nvec) {
+        uint4 w = reinterpret_cast<const uint4*>(x + r * ldx)[j];
+        float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), c = unpack_bf16x2(w.z), d = unpack_bf16x2(w.w);
+        v[i][0] = a.x; v[i][1] = a.y; v[i][2] = b.x; v[i][3] = b.y;
+        v[i][4] = c.x; v[i][5] = c.y; v[i][6] = d.x; v[i][7] = d.y;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s += v[i][e];
+      }
+    }
+    const float mean = team_sum<T>(s, scratch) * inv_c;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int j = t + i * T;
+      if (j < nvec) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = v[i][e] - mean;
+          q += d * d;
+        }
+      }
+    }
+    const float rstd = rsqrtf(team_sum<T>(q, scratch) * inv_c + eps);
+    if (!valid) continue;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int j = t + i * T;
+      if (j < nvec) {
+        const float4 g0 = reinterpret_cast<const float4*>(gamma)[2 * j];
+        const float4 g1 = reinterpret_cast<const float4*>(gamma)[2 * j + 1];
+        const float4 b0 = reinterpret_cast<const float4*>(beta)[2 * j];
+        const float4 b1 = reinterpret_cast<const float4*>(beta)[2 * j + 1];
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = (v[i][e] - mean) * rstd * g[e] + b[e];
+        uint4 w;
+        w.x = pack_bf16x2(o[0], o[1]);
+        w.y = pack_bf16x2(o[2], o[3]);
+        w.z = pack_bf16x2(o[4], o[5]);
+        w.w = pack_bf16x2(o[6], o[7]);
+        reinterpret_cast<uint4*>(y + row * ldy)[j] = w;
+      }
+    }
+    if (t == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+  }
+}
+
+// NACC = 2 (dgamma, dbeta) or 4 (+ colsum(resid_grad), colsum(dx)).
+template <int T, int V, int NACC>
+__global__ void __launch_bounds__(kThreads) ln_bwd_kernel(
+    const __nv_bfloat16* __restrict__ dy, long long lddy, const __nv_bfloat16* __restrict__ x, long long ldx,
+    const float* __restrict__ mean_in, const float* __restrict__ rstd_in, const float* __restrict__ gamma,
+    const __nv_bfloat16* __restrict__ resid_grad, long long ldr, __nv_bfloat16* __restrict__ dx, long long lddx,
+    float* __restrict__ partials, int M, int C) {
+  extern __shared__ float smem_f[];  // [teams][NACC][C] then scratch
+  const int teams_per_cta = kThreads / T;
+  const int team = threadIdx.x / T;
+  const int t = threadIdx.x % T;
+  const int nvec = C / 8;
+  const float inv_c = 1.0f / static_cast<float>(C);
+  float* scratch = smem_f + teams_per_cta * NACC * C;
+
+  float acc[NACC][V][8];
+#pragma unroll
+  for (int a = 0; a < NACC; ++a)
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[a][i][e] = 0.f;
+
+  const int rows_per_pass = gridDim.x * teams_per_cta;
+  const int passes = (M + rows_per_pass - 1) / rows_per_pass;
+  for (int pass = 0; pass < passes; ++pass) {
+    const int row = pass * rows_per_pass + blockIdx.x * teams_per_cta + team;
+    const bool valid = row < M;
+    const int r = valid ? row : M - 1;
+    const float mean = mean_in[r], rstd = rstd_in[r];
+    float xh[V][8], gy[V][8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int j = t + i * T;
+      if (j < nvec) {
+        uint4 wx = reinterpret_cast<const uint4*>(x + r * ldx)[j];
+        uint4 wd = reinterpret_cast<const uint4*>(dy + r * lddy)[j];
+        const float4 g0 = reinterpret_cast<const float4*>(gamma)[2 * j];
+        const float4 g1 = reinterpret_cast<const float4*>(gamma)[2 * j + 1];
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const uint32_t xs[4] = {wx.x, wx.y, wx.z, wx.w};
+        const uint32_t ds[4] = {wd.x, wd.y, wd.z, wd.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 xv = unpack_bf16x2(xs[q]);
+          const float2 dv = unpack_bf16x2(ds[q]);
+          xh[i][2 * q] = (xv.x - mean) * rstd;
+          xh[i][2 * q + 1] = (xv.y - mean) * rstd;
+          if (valid) {
+            acc[0][i][2 * q] += dv.x * xh[i][2 * q];
+            acc[0][i][2 * q + 1] += dv.y * xh[i][2 * q + 1];
+            acc[1][i][2 * q] += dv.x;
+            acc[1][i][2 * q + 1] += dv.y;
+          }
+          gy[i][2 * q] = dv.x * g[2 * q];
+          gy[i][2 * q + 1] = dv.y * g[2 * q + 1];
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          s1 += gy[i][e];
+          s2 += gy[i][e] * xh[i][e];
+        }
+      }
+    }
+    const float a1 = team_sum<T>(s1, scratch) * inv_c;
+    const float a2 = team_sum<T>(s2, scratch) * inv_c;
+    if (!valid) continue;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int j = t + i * T;
+      if (j < nvec) {
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = rstd * (gy[i][e] - a1 - xh[i][e] * a2);
+        if (resid_grad != nullptr) {
+          uint4 wr = reinterpret_cast<const uint4*>(resid_grad + row * ldr)[j];
+          const uint32_t rs[4] = {wr.x, wr.y, wr.z, wr.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 rv = unpack_bf16x2(rs[q]);
+            o[2 * q] += rv.x;
+            o[2 * q + 1] += rv.y;
+            if constexpr (NACC == 4) {
+              acc[2][i][2 * q] += rv.x;
+              acc[2][i][2 * q + 1] += rv.y;
+            }
+          }
+        }
+        uint4 w;
+        w.x = pack_bf16x2(o[0], o[1]);
+        w.y = pack_bf16x2(o[2], o[3]);
+        w.z = pack_bf16x2(o[4], o[5]);
+        w.w = pack_bf16x2(o[6], o[7]);
+        reinterpret_cast<uint4*>(dx + row * lddx)[j] = w;
+        if constexpr (NACC == 4) {
+          // Column sum of the *stored* (bf16-rounded) gradient, as the next
+          // GEMM will see it.
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 ov = unpack_bf16x2(ws[q]);
+            acc[3][i][2 * q] += ov.x;
+            acc[3][i][2 * q + 1] += ov.y;
+          }
+        }
+      }
+    }
+  }
+
+  // Fixed-order cross-team reduction, then one partial row per CTA.
+#pragma unroll
+  for (int a = 0; a < NACC; ++a)
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int j = t + i * T;
+      if (j < nvec)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) smem_f[(team * NACC + a) * C + j * 8 + e] = acc[a][i][e];
+    }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < NACC * C; idx += kThreads) {
+    float s = 0.f;
+    for (int tm = 0; tm < teams_per_cta; ++tm) s += smem_f[tm * NACC * C + idx];
+    partials[static_cast<long long>(blockIdx.x) * NACC * C + idx] = s;
+  }
+}
+
+// out_a[c] (+)= sum_b partials[b][a][c] for each accumulator a with a non-null destination.
+__global__ void reduce_partials_kernel(const float* __restrict__ partials, int nblocks, int nacc, int C,
+                                       float* d0, float* d1, float* d2, float* d3, int accumulate_mask) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= nacc * C) return;
+  const int a = idx / C, c = idx - a * C;
+  float* dst = a == 0 ? d0 : a == 1 ? d1 : a == 2 ? d2 : d3;
+  if (dst == nullptr) return;
+  float s = 0.f;
+  for (int b = 0; b < nblocks; ++b) s += partials[(static_cast<long long>(b) * nacc + a) * C + c];
+  dst[c] = ((accumulate_mask >> a) & 1) ? dst[c] + s : s;
+}
+
+}  // namespace ln
+}  // namespace md
+
+namespace {
+int g_sms = 0;
+int sms() {
+  if (g_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return g_sms;
+}
+
+template <int T, int V>
+cudaError_t ln_fwd_launch(const void* x, long long ldx, const float* g, const float* b, void* y, long long ldy,
+                          float* mean, float* rstd, int M, int C, float eps, cudaStream_t s) {
+  const int teams = md::ln::kThreads / T;
+  int grid = (M + teams - 1) / teams;
+  const int cap = sms() * 8;
+  if (grid > cap) grid = cap;
+  md::ln::ln_fwd_kernel<T, V><<<grid, md::ln::kThreads, 0, s>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), ldx, g, b, reinterpret_cast<__nv_bfloat16*>(y), ldy, mean, rstd, M,
+      C, eps);
+  return cudaGetLastError();
+}
+
+template <int T, int V, int NACC>
+cudaError_t ln_bwd_launch(const void* dy, long long lddy, const void* x, long long ldx, const float* mean,
+                          const float* rstd, const float* g, const void* rg, long long ldr, void* dx, long long lddx,
+                          float* partials, int grid, int M, int C, cudaStream_t s) {
+  const int teams = md::ln::kThreads / T;
+  const size_t smem = (static_cast<size_t>(teams) * NACC * C + md::ln::kThreads / 32) * sizeof(float);
+  auto kern = md::ln::ln_bwd_kernel<T, V, NACC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  kern<<<grid, md::ln::kThreads, smem, s>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dy), lddy, reinterpret_cast<const __nv_bfloat16*>(x), ldx, mean, rstd, g,
+      reinterpret_cast<const __nv_bfloat16*>(rg), ldr, reinterpret_cast<__nv_bfloat16*>(dx), lddx, partials, M, C);
+  return cudaGetLastError();
+}
+
+bool ok16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+
+extern "C" {
+
+// Number of CTAs (= partial rows) md_ln_bwd uses for M rows of width C.
+int md_ln_bwd_grid(int M, int C) {
+  (void)C;
+  int g = sms() * 2;
+  return g < M ? g : (M > 0 ? M : 1);
+}
+
+int md_ln_fwd(const void* x, long long ldx, const float* gamma, const float* beta, void* y, long long ldy, float* mean,
+              float* rstd, int M, int C, float eps, cudaStream_t s) {
+  if (M <= 0 || C <= 0 || (C % 8) || (ldx % 8) || (ldy % 8) || !ok16(x) || !ok16(y) || !ok16(gamma) || !ok16(beta))
+    return -1;
+  cudaError_t e;
+  const int nvec = C / 8;
+#define MD_LN_FWD_T(TT)                                                                  \
+  {                                                                                      \
+    const int v = (nvec + TT - 1) / TT;                                                  \
+    if (v <= 1) e = ln_fwd_launch<TT, 1>(x, ldx, gamma, beta, y, ldy, mean, rstd, M, C, eps, s); \
+    else if (v == 2) e = ln_fwd_launch<TT, 2>(x, ldx, gamma, beta, y, ldy, mean, rstd, M, C, eps, s); \
+    else if (v == 3) e = ln_fwd_launch<TT, 3>(x, ldx, gamma, beta, y, ldy, mean, rstd, M, C, eps, s); \
+    else e = ln_fwd_launch<TT, 4>(x, ldx, gamma, beta, y, ldy, mean, rstd, M, C, eps, s); \
+  }
+  if (C <= 1024)      MD_LN_FWD_T(32)
+  else if (C <= 2048) MD_LN_FWD_T(64)
+  else if (C <= 4096) MD_LN_FWD_T(128)
+  else if (C <= 8192) MD_LN_FWD_T(256)
+  else return -2;
+#undef MD_LN_FWD_T
+  return static_cast<int>(e);
+}
+
+// dx = LN'(dy) (+ resid_grad); partials [grid, nacc, C] (grid from md_ln_bwd_grid).
+int md_ln_bwd(const void* dy, long long lddy, const void* x, long long ldx, const float* mean, const float* rstd,
+              const float* gamma, const void* resid_grad, long long ldr, void* dx, long long lddx, float* partials,
+              int nacc, int M, int C, cudaStream_t s) {
+  if (M <= 0 || C <= 0 || (C % 8) || (lddy % 8) || (ldx % 8) || (lddx % 8) || !ok16(dy) || !ok16(x) || !ok16(dx) ||
+      !ok16(gamma))
+    return -1;
+  if (resid_grad != nullptr && ((ldr % 8) || !ok16(resid_grad))) return -1;
+  if (nacc != 2 && nacc != 4) return -3;
+  if (nacc == 4 && resid_grad == nullptr) return -4;
+  const int grid = md_ln_bwd_grid(M, C);
+  cudaError_t e;
+  const int nvec = C / 8;
+#define MD_LN_BWD_TV(TT, VV)                                                                                      \
+  (nacc == 2 ? ln_bwd_launch<TT, VV, 2>(dy, lddy, x, ldx, mean, rstd, gamma, resid_grad, ldr, dx, lddx, partials, \
+                                        grid, M, C, s)                                                            \
+             : ln_bwd_launch<TT, VV, 4>(dy, lddy, x, ldx, mean, rstd, gamma, resid_grad, ldr, dx, lddx, partials, \
+                                        grid, M, C, s))
+#define MD_LN_BWD_T(TT)                         \
+  {                                             \
+    const int v = (nvec + TT - 1) / TT;         \
+    if (v <= 1) e = MD_LN_BWD_TV(TT, 1);        \
+    else if (v == 2) e = MD_LN_BWD_TV(TT, 2);   \
+    else if (v == 3) e = MD_LN_BWD_TV(TT, 3);   \
+    else e = MD_LN_BWD_TV(TT, 4);               \
+  }
+  if (C <= 1024)      MD_LN_BWD_T(32)
+  else if (C <= 2048) MD_LN_BWD_T(64)
+  else if (C <= 4096) MD_LN_BWD_T(128)
+  else if (C <= 8192) MD_LN_BWD_T(256)
+  else return -2;
+#undef MD_LN_BWD_T
+#undef MD_LN_BWD_TV
+  return static_cast<int>(e);
+}
+
+int md_ln_reduce(const float* partials, int nblocks, int nacc, int C, float* d0, float* d1, float* d2, float* d3,
+                 int accumulate_mask, cudaStream_t s) {
+  const int total = nacc * C;
+  md::ln::reduce_partials_kernel<<<(total + 255) / 256, 256, 0, s>>>(partials, nblocks, nacc, C, d0, d1, d2, d3,
+                                                                     accumulate_mask);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // extern "C"
