@@ -9,6 +9,7 @@
 // Reads the bf16 shadow of the tables; gradients land in fp32.
 // Replaces VocabParallelEmbedding.forward (reference tensor_parallel.py:409-416)
 // and Embedding.forward (models/gpt.py:183-185).
+#include "md_noalloc.h"
 #include "md_sm100.cuh"
 
 namespace md {
@@ -207,3 +208,46 @@ int md_colsum(const void* x, long long ldx, int M, int N, float* partial, float*
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of md_colsum (declared in md_noalloc.h).
+//
+// For callers that cannot allocate device memory themselves — for example a
+// host program whose device memory is entirely owned by another allocator's
+// pool, or code that must not call cudaMalloc because it may synchronise the
+// device.  The partial-sum scratch of the two-stage column sum lives in the
+// static array below, which every GPU that loads this library holds until the
+// process exits.  Nothing in it needs clearing between calls: the first stage
+// writes every scratch entry the second stage reads.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float md_colsum_scratch[MD_NOALLOC_SCRATCH_FLOATS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+void* g_colsum_scratch[kMaxDevices] = {};
+}  // namespace
+
+extern "C" int md_colsum_scratch_floats(int M, int N) {
+  if (M <= 0 || N <= 0) return 0;
+  return md_colsum_chunks(M, N) * N;
+}
+
+extern "C" int md_colsum_noalloc(const void* x, long long ldx, int M, int N, float* out, int accumulate,
+                                 cudaStream_t s) {
+  if (M <= 0 || N <= 0 || out == nullptr || x == nullptr) return -1;
+  const long long need = static_cast<long long>(md_colsum_chunks(M, N)) * N;
+  if (need > MD_NOALLOC_SCRATCH_FLOATS) return MD_NOALLOC_TOO_LARGE;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev < 0 || dev >= kMaxDevices) return -2;
+  if (g_colsum_scratch[dev] == nullptr) {
+    // Device address of the static array for the current device; the host
+    // symbol itself is only a stand-in and must never reach a kernel.
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, md_colsum_scratch);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    g_colsum_scratch[dev] = ptr;
+  }
+  return md_colsum(x, ldx, M, N, static_cast<float*>(g_colsum_scratch[dev]), out, accumulate, s);
+}
