@@ -185,9 +185,12 @@ def build(impl: str, world: int, seed: int):
     cfg = GPTConfig(vocab_size=MODEL["vocab"], block_size=MODEL["seq"], n_layer=MODEL["layers"],
                     n_head=MODEL["heads"], n_embd=MODEL["embd"], seed=seed)
     torch.manual_seed(seed)
-    model = GPT(cfg, device=torch.device("cuda"))
+    # Pure data parallelism, as the reference trainer builds it: a (tp=1, pp=1)
+    # mesh whose size-1 TP group keeps the whole model on every rank.
+    mesh = md.ParallelMesh(tp_size=1, pp_size=1)
+    model = GPT(cfg, tp_group=mesh.tp_group, device=torch.device("cuda"))
     if world > 1:
-        model = md.DistributedDataParallel(model, bucket_cap_mb=25.0)
+        model = md.DistributedDataParallel(model, process_group=mesh.dp_group, bucket_cap_mb=25.0)
     opt = make_opt(model.parameters())
 
     def step(ids, tgt):
@@ -327,6 +330,10 @@ def main() -> int:
     if world > 1:
         import torch.distributed as dist
 
+        if args.impl == "ours":
+            from minidist.parallel import symm
+
+            symm.release_all()
         dist.barrier()
         dist.destroy_process_group()
     return 0

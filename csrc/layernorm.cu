@@ -257,16 +257,32 @@ __global__ void __launch_bounds__(kThreads) ln_bwd_kernel(
 }
 
 // out_a[c] (+)= sum_b partials[b][a][c] for each accumulator a with a non-null destination.
-__global__ void reduce_partials_kernel(const float* __restrict__ partials, int nblocks, int nacc, int C,
-                                       float* d0, float* d1, float* d2, float* d3, int accumulate_mask) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= nacc * C) return;
-  const int a = idx / C, c = idx - a * C;
-  float* dst = a == 0 ? d0 : a == 1 ? d1 : a == 2 ? d2 : d3;
-  if (dst == nullptr) return;
+// Block = 32 columns x 8 row groups; each group sums a contiguous range of
+// partial rows, then the 8 group sums are added in a fixed order.
+__global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ partials, int nblocks,
+                                                              int nacc, int C, float* d0, float* d1, float* d2,
+                                                              float* d3, int accumulate_mask) {
+  __shared__ float red[8][33];
+  const int col = threadIdx.x & 31, grp = threadIdx.x >> 5;
+  const int idx = blockIdx.x * 32 + col;
+  const bool ok = idx < nacc * C;
+  const int a = ok ? idx / C : 0, c = ok ? idx - a * C : 0;
+  const int per = (nblocks + 7) / 8;
+  const int b0 = grp * per, b1 = min(nblocks, b0 + per);
   float s = 0.f;
-  for (int b = 0; b < nblocks; ++b) s += partials[(static_cast<long long>(b) * nacc + a) * C + c];
-  dst[c] = ((accumulate_mask >> a) & 1) ? dst[c] + s : s;
+  if (ok)
+    for (int b = b0; b < b1; ++b) s += partials[(static_cast<long long>(b) * nacc + a) * C + c];
+  red[grp][col] = s;
+  __syncthreads();
+  if (grp == 0 && ok) {
+    float* dst = a == 0 ? d0 : a == 1 ? d1 : a == 2 ? d2 : d3;
+    if (dst != nullptr) {
+      float t = 0.f;
+#pragma unroll
+      for (int g = 0; g < 8; ++g) t += red[g][col];
+      dst[c] = ((accumulate_mask >> a) & 1) ? dst[c] + t : t;
+    }
+  }
 }
 
 }  // namespace ln
@@ -385,7 +401,7 @@ int md_ln_bwd(const void* dy, long long lddy, const void* x, long long ldx, cons
 int md_ln_reduce(const float* partials, int nblocks, int nacc, int C, float* d0, float* d1, float* d2, float* d3,
                  int accumulate_mask, cudaStream_t s) {
   const int total = nacc * C;
-  md::ln::reduce_partials_kernel<<<(total + 255) / 256, 256, 0, s>>>(partials, nblocks, nacc, C, d0, d1, d2, d3,
+  md::ln::reduce_partials_kernel<<<(total + 31) / 32, 256, 0, s>>>(partials, nblocks, nacc, C, d0, d1, d2, d3,
                                                                      accumulate_mask);
   return static_cast<int>(cudaGetLastError());
 }

@@ -112,7 +112,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, Status
 
 // ---------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor) — plain tile loads into this CTA's shared memory.
-// No .multicast::cluster anywhere in this library.
+// Every copy lands only in the issuing CTA's own shared memory.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -103,6 +103,10 @@ class DistributedDataParallel(nn.Module):
         }
         self._next_to_launch = 0
         self._callback_queued = False
+        # Parameters already counted in this backward: a parameter whose
+        # gradient a fused kernel wrote reports through ops/grads.py, and
+        # autograd may still run its post-accumulate hook afterwards.
+        self._ready: set[int] = set()
         self._handles: list = []
         self._reducer = None
         if self.world_size > 1:
@@ -161,6 +165,9 @@ class DistributedDataParallel(nn.Module):
     def _on_grad_ready(self, param: torch.Tensor) -> None:
         if not self.require_backward_grad_sync:
             return
+        if id(param) in self._ready:
+            return
+        self._ready.add(id(param))
         if not self._callback_queued:
             self._callback_queued = True
             try:
@@ -212,6 +219,7 @@ class DistributedDataParallel(nn.Module):
                 self._reducer.wait(b)
             b.reset()
         self._next_to_launch = 0
+        self._ready.clear()
 
     # -- public API --------------------------------------------------------------
 

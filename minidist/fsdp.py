@@ -138,8 +138,16 @@ class _FSDPUnit:
 
     def arm_gradient_reduction(self) -> None:
         self._pending = sum(1 for p in self.params if p.requires_grad)
+        self._ready: set[int] = set()
 
-    def on_param_grad_ready(self, sync: bool) -> None:
+    def on_param_grad_ready(self, param: torch.Tensor, sync: bool) -> None:
+        # Count each parameter once per backward (a fused-kernel gradient may
+        # be reported both through ops/grads.py and by autograd's hook).
+        ready = getattr(self, "_ready", None)
+        if ready is not None:
+            if id(param) in ready:
+                return
+            ready.add(id(param))
         self._pending -= 1
         if self._pending > 0:
             return
@@ -290,7 +298,7 @@ class FullyShardedDataParallel(nn.Module):
 
     def _grad_ready(self, unit):
         def hook(param):
-            unit.on_param_grad_ready(sync=self.require_backward_grad_sync)
+            unit.on_param_grad_ready(param, sync=self.require_backward_grad_sync)
         return hook
 
     # -- public API ----------------------------------------------------------------

@@ -338,6 +338,9 @@ class _HeadFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, head, targets, ln_w, ln_b, w):
         B, S, C = x.shape
+        # An unused output (usually the logits) must arrive as None, not as a
+        # materialised zero tensor of [tokens, vocab] that would then be added.
+        ctx.set_materialize_grads(False)
         xin = _as_bf16_2d(x)
         lnw, lnb = fp32_param(head.ln_f.weight), fp32_param(head.ln_f.bias)
         h, mu, r = K.layernorm_fwd(xin, lnw, lnb, head.ln_f.eps)
@@ -381,13 +384,15 @@ class _HeadFn(torch.autograd.Function):
         xin, h, mu, r, lnw, logits = ctx.saved
         ctx.saved = None
         group = head.tp_group
-        if ctx.has_loss:
+        if ctx.has_loss and g_loss is not None:
             dlogits = K.ce_backward(logits, ctx.lse, ctx.targets, g_loss.float().reshape(1), 1.0 / M, V,
                                     col_offset=ctx.col0)
             if g_logits is not None:
                 dlogits += g_logits.reshape(M, V).to(dlogits.dtype)
-        else:
+        elif g_logits is not None:
             dlogits = _as_bf16_2d(g_logits.reshape(M, V))
+        else:
+            return None, None, None, None, None, None
         wb = bf16_weight(head.head.weight)
         (t_w,) = _targets(head.head.weight)
         if t_w is not None:
