@@ -131,6 +131,44 @@ __global__ void colsum_partial_kernel(const __nv_bfloat16* __restrict__ x, long 
   if (pair) partial[static_cast<long long>(chunk) * N + 2 * c2 + 1] = ay;
 }
 
+// Wide variant (N % 8 == 0, 16-byte aligned rows): a CTA covers 256 columns
+// (32 groups of 8) x 8 row groups; the 8 row-group sums are added in a fixed
+// order in shared memory, giving one partial row per (chunk, column block).
+__global__ void __launch_bounds__(256) colsum_partial8_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                              int M, int N, int rows_per_chunk,
+                                                              float* __restrict__ partial) {
+  __shared__ float red[8][256 + 4];
+  const int cgp = threadIdx.x & 31, rg = threadIdx.x >> 5;
+  const int col = blockIdx.x * 256 + cgp * 8;
+  const int chunk = blockIdx.y;
+  const int r0 = chunk * rows_per_chunk;
+  const int r1 = min(M, r0 + rows_per_chunk);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (col < N) {
+    for (int r = r0 + rg; r < r1; r += 8) {
+      const uint4 w = *reinterpret_cast<const uint4*>(x + r * ldx + col);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = unpack_bf16x2(ws[q]);
+        acc[2 * q] += f.x;
+        acc[2 * q + 1] += f.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) red[rg][cgp * 8 + e] = acc[e];
+  __syncthreads();
+  const int c = threadIdx.x;  // one output column per thread
+  const int gc = blockIdx.x * 256 + c;
+  if (gc < N) {
+    float t = 0.f;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) t += red[g][c];
+    partial[static_cast<long long>(chunk) * N + gc] = t;
+  }
+}
+
 __global__ void colsum_final_kernel(const float* __restrict__ partial, int chunks, int N, float* __restrict__ out,
                                     int accumulate) {
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
@@ -189,20 +227,26 @@ int md_embed_bwd_wpe(const void* dx, long long ldx, float* dwpe, long long ldg, 
 // Number of row chunks (partial rows) md_colsum uses; the caller provides
 // partial scratch of md_colsum_chunks(M, N) * N floats.
 int md_colsum_chunks(int M, int N) {
-  const int col_blocks = (N / 2 + 255) / 256 + 1;
-  int chunks = (148 * 8) / col_blocks;
-  if (chunks < 1) chunks = 1;
+  (void)N;
+  int chunks = 148;
   const int max_chunks = (M + 63) / 64;
-  return chunks < max_chunks ? chunks : max_chunks;
+  if (chunks > max_chunks) chunks = max_chunks;
+  return chunks < 1 ? 1 : chunks;
 }
 
 int md_colsum(const void* x, long long ldx, int M, int N, float* partial, float* out, int accumulate, cudaStream_t s) {
   if (M <= 0 || N <= 0 || (ldx % 2) || (reinterpret_cast<uintptr_t>(x) & 3u)) return -1;
   const int chunks = md_colsum_chunks(M, N);
   const int rows_per_chunk = (M + chunks - 1) / chunks;
-  dim3 grid((N / 2 + 1 + 255) / 256, chunks);
-  md::emb::colsum_partial_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, N,
-                                                       rows_per_chunk, partial);
+  if ((N % 8) == 0 && (ldx % 8) == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    dim3 grid((N + 255) / 256, chunks);
+    md::emb::colsum_partial8_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, N,
+                                                          rows_per_chunk, partial);
+  } else {
+    dim3 grid((N / 2 + 1 + 255) / 256, chunks);
+    md::emb::colsum_partial_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, N,
+                                                         rows_per_chunk, partial);
+  }
   md::emb::colsum_final_kernel<<<(N + 255) / 256, 256, 0, s>>>(partial, chunks, N, out, accumulate);
   return static_cast<int>(cudaGetLastError());
 }

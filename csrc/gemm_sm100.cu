@@ -9,24 +9,39 @@
 //   dgrad    dx = dy W   : A = dy (K-major),  B = W (MN-major)
 //   wgrad    dW = dy^T x : A = dy (MN-major), B = x (MN-major)
 //
-// CTA layout (192 threads, one CTA per SM, grid = min(#SMs, #work units)):
-//   warp 0     : TMA producer (one thread) filling a 4-stage smem ring
-//   warp 1     : TMEM allocator + MMA issuer (one thread)
-//   warps 2..5 : epilogue; warp w reads TMEM lanes 32*(w%4) .. +31
-// The 512 TMEM columns hold two 128x256 fp32 accumulators, so the epilogue of
+// Two tile configurations share one kernel template:
+//   CG = 1: one CTA per SM computes 128 x 256 output tiles (tcgen05 cta_group::1).
+//   CG = 2: a cluster of two CTAs on two SMs computes 256 x 256 tiles with
+//           cta_group::2 MMAs: each CTA stages its own 128 rows of A and half
+//           (128 columns) of B, so per-SM operand traffic drops by a third;
+//           the leader CTA issues the MMAs, each CTA's TMEM holds its 128 rows
+//           of the accumulator.  Both CTAs' loads complete on the leader's
+//           mbarrier; the leader's MMA completion is signalled to both CTAs'
+//           barriers with one masked tcgen05.commit.
+//
+// Warp roles (64 + 32*EW threads):
+//   warp 0       : TMA producer (one thread), 6-stage ring (CG=2) / 4 (CG=1)
+//   warp 1       : TMEM allocator + MMA issuer (one thread, leader CTA only)
+//   warps 2..    : EW epilogue warps; warp w reads TMEM lanes 32*(w%4)..+31;
+//                  with EW = 8 two warps share a lane quarter and split the
+//                  256 accumulator columns.
+// 512 TMEM columns hold two 256-column fp32 accumulators, so the epilogue of
 // tile i overlaps the main loop of tile i+1.
 //
 // Epilogues (EpiMode):
 //   kEpiBF16  : (+bias) (-> store pre-activation, GELU) (+residual) -> bf16
 //   kEpiF32   : fp32 store, optionally D += acc (gradient accumulation); with
 //               k_splits > 1 each split writes a partial slab of `workspace`
-//               and md_splitk_reduce sums them in a fixed order
+//               and a fixed-order reduce kernel sums them
 //   kEpiDGELU : acc * gelu'(pre-activation) -> bf16   (MLP backward)
-//   kEpiCE    : bf16 logits plus per-(row, column-tile) max / sum-exp and the
-//               target logit, for the fused cross-entropy
+//   kEpiCE    : bf16 logits plus per-(row, 128-column slab) max / sum-exp and
+//               the target logit, for the fused cross-entropy
 //
-// This replaces the reference's F.linear calls (tensor_parallel.py:291,354
-// via models/gpt.py) and, through kEpiCE, the logits half of
+// Every mbarrier wait is bounded (md_sm100.cuh); on expiry the kernel records a
+// status word, drains its own copies and MMAs, frees TMEM and returns.
+//
+// Replaces the reference's F.linear calls (tensor_parallel.py:291,354 via
+// models/gpt.py) and, through kEpiCE, the logits half of
 // _VocabParallelCrossEntropy (tensor_parallel.py:451-479).
 #include <cudaTypedefs.h>
 
@@ -35,18 +50,22 @@
 namespace md {
 namespace gemm {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
+constexpr int BM = 128;  // rows per CTA
+constexpr int BN = 256;  // columns per tile
 constexpr int BK = 64;
-constexpr int kStages = 4;
-constexpr int kThreads = 192;
-constexpr int kABytes = BM * BK * 2;   // 16 KB
-constexpr int kBBytes = BN * BK * 2;   // 32 KB
-constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kABytes = BM * BK * 2;  // 16 KB
 constexpr int kTmemCols = 512;
-constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + 256 /*barriers*/;
+constexpr int kCeSlab = 128;  // CE statistics are kept per 128-column slab
 
 enum EpiMode : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiDGELU = 2, kEpiCE = 3 };
+
+template <int CG>
+struct Cfg {
+  static constexpr int kBBytes = (BN / CG) * BK * 2;  // B rows staged by this CTA
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = CG == 2 ? 6 : 4;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+};
 
 }  // namespace gemm
 }  // namespace md
@@ -73,12 +92,14 @@ struct MdGemmParams {
   long long ldws;
   int k_splits;
   const long long* ce_target;  // int64 [M] (kEpiCE)
-  float* ce_max;               // [tiles_n, M]
-  float* ce_sum;               // [tiles_n, M]
+  float* ce_max;               // [ceil(N/128), M]
+  float* ce_sum;               // [ceil(N/128), M]
   float* ce_tgt;               // [M]
   long long ce_col_offset;     // global column id of this shard's column 0
   int num_sms;                 // grid cap (0 -> all SMs)
   md::Status* status;
+  int cta_group;               // 0 = choose, 1 or 2
+  int epi_warps;               // 0 = choose, 4 or 8
 };
 
 namespace md {
@@ -86,7 +107,8 @@ namespace gemm {
 
 struct KParams {
   MdGemmParams p;
-  int tiles_m, tiles_n, units, k_blocks, kb_per_split;
+  int tiles_m;  // in units of CG*128 rows
+  int tiles_n, units, k_blocks, kb_per_split;
 };
 
 __device__ __forceinline__ void decode_unit(const KParams& kp, int u, int& tm, int& tn, int& split) {
@@ -97,26 +119,298 @@ __device__ __forceinline__ void decode_unit(const KParams& kp, int u, int& tm, i
   tn = rem - tm * kp.tiles_n;
 }
 
-template <bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+// ---------------------------------------------------------------------------
+// Cluster helpers (CG = 2)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t smem_addr, uint32_t cta) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr), "r"(cta));
+  return out;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA tile load into this CTA's shared memory whose transaction bytes are
+// counted on the pair leader's mbarrier (cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t leader_bar, void* smem_dst, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void umma_bf16_ss_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the mbarrier at this shared-memory offset in both CTAs of the pair
+// once the issuing thread's MMAs complete (commit with a CTA mask; this is a
+// completion signal, not a data copy).
+__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ---------------------------------------------------------------------------
+// Epilogue of one thread's row over the 32-column chunks [c_begin, c_end) of
+// the 256-column accumulator (TMEM address t_row: this warp's lane quarter,
+// accumulator base column).  Every thread of the warp calls this (tcgen05.ld
+// is warp-collective); rows past M only skip the stores.
+// ---------------------------------------------------------------------------
+template <int EPI>
+__device__ __forceinline__ void epilogue_row(const MdGemmParams& p, int row, int tn, int split, uint32_t t_row,
+                                             int c_begin, int c_end) {
+  const bool row_ok = row < p.M;
+  long long tgt = -1;
+  if (EPI == kEpiCE && row_ok) tgt = p.ce_target[row] - p.ce_col_offset;
+#pragma unroll 1
+  for (int slab = c_begin / 4; slab < c_end / 4; ++slab) {
+    float ce_m = -INFINITY, ce_s = 0.f;
+    bool ce_any = false;
+#pragma unroll 1
+    for (int c = slab * 4; c < slab * 4 + 4; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + c * 32, r);
+      tmem_ld_wait();
+      const int n0 = tn * BN + c * 32;
+      if (!row_ok || n0 >= p.N) continue;
+      const bool full = (n0 + 32 <= p.N);
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+
+      if (EPI == kEpiBF16) {
+        if (p.bias != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += (n0 + j < p.N) ? p.bias[n0 + j] : 0.f;
+        }
+        if (p.gelu) {
+          __nv_bfloat16* aux = reinterpret_cast<__nv_bfloat16*>(p.aux) + row * p.ldaux + n0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
+          if (full) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w;
+              w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+              w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+              w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+              w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+              reinterpret_cast<uint4*>(aux)[q] = w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) aux[j] = __float2bfloat16_rn(v[j]);
+          }
+          // GELU of the bf16-rounded pre-activation: exactly what backward differentiates.
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+        }
+        if (p.resid != nullptr) {
+          const __nv_bfloat16* rs = reinterpret_cast<const __nv_bfloat16*>(p.resid) + row * p.ldres + n0;
+          if (full) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w = reinterpret_cast<const uint4*>(rs)[q];
+              float2 f0 = unpack_bf16x2(w.x), f1 = unpack_bf16x2(w.y), f2 = unpack_bf16x2(w.z),
+                     f3 = unpack_bf16x2(w.w);
+              v[q * 8 + 0] += f0.x; v[q * 8 + 1] += f0.y; v[q * 8 + 2] += f1.x; v[q * 8 + 3] += f1.y;
+              v[q * 8 + 4] += f2.x; v[q * 8 + 5] += f2.y; v[q * 8 + 6] += f3.x; v[q * 8 + 7] += f3.y;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) v[j] += __bfloat162float(rs[j]);
+          }
+        }
+      } else if (EPI == kEpiDGELU) {
+        const __nv_bfloat16* hx = reinterpret_cast<const __nv_bfloat16*>(p.aux) + row * p.ldaux + n0;
+        if (full) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w = reinterpret_cast<const uint4*>(hx)[q];
+            float2 f0 = unpack_bf16x2(w.x), f1 = unpack_bf16x2(w.y), f2 = unpack_bf16x2(w.z),
+                   f3 = unpack_bf16x2(w.w);
+            v[q * 8 + 0] *= gelu_tanh_grad(f0.x); v[q * 8 + 1] *= gelu_tanh_grad(f0.y);
+            v[q * 8 + 2] *= gelu_tanh_grad(f1.x); v[q * 8 + 3] *= gelu_tanh_grad(f1.y);
+            v[q * 8 + 4] *= gelu_tanh_grad(f2.x); v[q * 8 + 5] *= gelu_tanh_grad(f2.y);
+            v[q * 8 + 6] *= gelu_tanh_grad(f3.x); v[q * 8 + 7] *= gelu_tanh_grad(f3.y);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) v[j] *= gelu_tanh_grad(__bfloat162float(hx[j]));
+        }
+      }
+
+      if (EPI == kEpiF32) {
+        float* dst;
+        bool add = false;
+        if (p.k_splits > 1 && p.workspace == nullptr) {
+          // Split-K by fp32 atomic accumulation straight into D (D was zeroed
+          // by the host unless accumulating).  Summation order varies run to
+          // run; the workspace path below is the deterministic alternative.
+          float* dd = reinterpret_cast<float*>(p.D) + row * p.ldd + n0;
+          if (full) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dd + 4 * q), "f"(v[q * 4 + 0]),
+                           "f"(v[q * 4 + 1]), "f"(v[q * 4 + 2]), "f"(v[q * 4 + 3])
+                           : "memory");
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) atomicAdd(dd + j, v[j]);
+          }
+          continue;
+        }
+        if (p.k_splits > 1) {
+          dst = p.workspace + (static_cast<long long>(split) * p.M + row) * p.ldws + n0;
+        } else {
+          dst = reinterpret_cast<float*>(p.D) + row * p.ldd + n0;
+          add = p.beta != 0;
+        }
+        if (full) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float4 w = make_float4(v[q * 4 + 0], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+            if (add) {
+              float4 o = reinterpret_cast<const float4*>(dst)[q];
+              w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
+            }
+            reinterpret_cast<float4*>(dst)[q] = w;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) dst[j] = add ? dst[j] + v[j] : v[j];
+        }
+      } else {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + n0;
+        if (EPI == kEpiCE) {
+          // Statistics use the bf16-rounded logits the backward pass reads back.
+          constexpr float kLog2e = 1.4426950408889634f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
+          float cm = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) cm = fmaxf(cm, v[j]);
+          if (cm > ce_m) {
+            ce_s = ce_any ? ce_s * ex2_approx((ce_m - cm) * kLog2e) : 0.f;
+            ce_m = cm;
+          }
+          ce_any = true;
+          const float mb = ce_m * kLog2e;
+          float s = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) s += ex2_approx(fmaf(v[j], kLog2e, -mb));
+          ce_s += s;
+          if (tgt >= n0 && tgt < n0 + 32) {
+            float tv = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j == tgt) tv = v[j];
+            p.ce_tgt[row] = tv;
+          }
+        }
+        if (full) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+            w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+            w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+            w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+            reinterpret_cast<uint4*>(dst)[q] = w;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) dst[j] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
+    if (EPI == kEpiCE && row_ok) {
+      const long long sl = static_cast<long long>(tn) * (BN / kCeSlab) + slab;
+      if (sl * kCeSlab < p.N) {
+        p.ce_max[sl * p.M + row] = ce_m;
+        p.ce_sum[sl * p.M + row] = ce_s;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------
+template <int CG, int EW, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ KParams kp) {
+  using C = Cfg<CG>;
+  constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-  uint64_t* full_bar = bars;                  // [kStages]
-  uint64_t* empty_bar = bars + kStages;       // [kStages]
-  uint64_t* tfull_bar = bars + 2 * kStages;   // [2]
-  uint64_t* tempty_bar = bars + 2 * kStages + 2;  // [2]
-  uint64_t* drain_bar = bars + 2 * kStages + 4;   // [1]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * C::kStageBytes);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + kStages;
+  uint64_t* tfull_bar = bars + 2 * kStages;
+  uint64_t* tempty_bar = bars + 2 * kStages + 2;
+  uint64_t* drain_bar = bars + 2 * kStages + 4;
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * kStages + 6);
 
   const MdGemmParams& p = kp.p;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t crank = CG == 2 ? cluster_ctarank() : 0u;
+  const bool leader = crank == 0;
+  const int cluster_id = CG == 2 ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int nclusters = CG == 2 ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -125,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], CG * EW);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -134,11 +428,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_base_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_base_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_base_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // peer barriers exist before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
 
@@ -146,55 +446,75 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     int stage = 0;
     uint32_t phase = 0;
+    long long fills = 0;
     int armed_phase[kStages];
     for (int s = 0; s < kStages; ++s) armed_phase[s] = -1;
     bool ok = true;
-    for (int u = blockIdx.x; u < kp.units && ok; u += gridDim.x) {
+    for (int u = cluster_id; u < kp.units && ok; u += nclusters) {
       int tm, tn, split;
       decode_unit(kp, u, tm, tn, split);
       const int kb0 = split * kp.kb_per_split;
       const int kb1 = min(kp.k_blocks, kb0 + kp.kb_per_split);
+      const int row_base = tm * (CG * BM) + static_cast<int>(crank) * BM;
+      const int col_base = tn * BN + static_cast<int>(crank) * (BN / CG);
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.status, 10, abort_flag)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+        uint32_t bar_addr = smem_u32(&full_bar[stage]);
+        if constexpr (CG == 2) {
+          bar_addr = map_to_cta(bar_addr, 0);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], CG * C::kStageBytes);
+        } else {
+          mbar_arrive_expect_tx(&full_bar[stage], C::kStageBytes);
+        }
         armed_phase[stage] = static_cast<int>(phase);
         uint8_t* a_dst = sA + stage * kABytes;
-        uint8_t* b_dst = sB + stage * kBBytes;
+        uint8_t* b_dst = sB + stage * C::kBBytes;
         if (!A_MN) {
-          tma_load_2d(&tmA, &full_bar[stage], a_dst, kb * BK, tm * BM);
+          if (CG == 2) tma_load_2d_pair(&tmA, bar_addr, a_dst, kb * BK, row_base);
+          else tma_load_2d(&tmA, &full_bar[stage], a_dst, kb * BK, row_base);
         } else {
 #pragma unroll
-          for (int c = 0; c < BM / 64; ++c)
-            tma_load_2d(&tmA, &full_bar[stage], a_dst + c * (64 * BK * 2), tm * BM + c * 64, kb * BK);
+          for (int c = 0; c < BM / 64; ++c) {
+            if (CG == 2) tma_load_2d_pair(&tmA, bar_addr, a_dst + c * (64 * BK * 2), row_base + c * 64, kb * BK);
+            else tma_load_2d(&tmA, &full_bar[stage], a_dst + c * (64 * BK * 2), row_base + c * 64, kb * BK);
+          }
         }
         if (!B_MN) {
-          tma_load_2d(&tmB, &full_bar[stage], b_dst, kb * BK, tn * BN);
+          if (CG == 2) tma_load_2d_pair(&tmB, bar_addr, b_dst, kb * BK, col_base);
+          else tma_load_2d(&tmB, &full_bar[stage], b_dst, kb * BK, col_base);
         } else {
 #pragma unroll
-          for (int c = 0; c < BN / 64; ++c)
-            tma_load_2d(&tmB, &full_bar[stage], b_dst + c * (64 * BK * 2), tn * BN + c * 64, kb * BK);
+          for (int c = 0; c < (BN / CG) / 64; ++c) {
+            if (CG == 2) tma_load_2d_pair(&tmB, bar_addr, b_dst + c * (64 * BK * 2), col_base + c * 64, kb * BK);
+            else tma_load_2d(&tmB, &full_bar[stage], b_dst + c * (64 * BK * 2), col_base + c * 64, kb * BK);
+          }
         }
+        ++fills;
         if (++stage == kStages) {
           stage = 0;
           phase ^= 1u;
         }
       }
     }
-    // Make sure no bulk copy into our shared memory is still in flight.
-    for (int s = 0; s < kStages; ++s)
-      if (armed_phase[s] >= 0) mbar_wait(&full_bar[s], static_cast<uint32_t>(armed_phase[s]), p.status, 11, nullptr);
-  } else if (warp == 1 && lane == 0) {
+    // No bulk copy into shared memory may still be in flight at exit.  (The
+    // follower's copies complete on the leader's barriers, which the leader's
+    // MMA has consumed before the final cluster barrier.)
+    if (CG == 1 || leader)
+      for (int s = 0; s < kStages; ++s)
+        if (armed_phase[s] >= 0) mbar_wait(&full_bar[s], static_cast<uint32_t>(armed_phase[s]), p.status, 11, nullptr);
+  } else if (warp == 1 && lane == 0 && leader) {
     // ------------------------------------------------------------ MMA issuer
-    constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+    constexpr uint32_t idesc = idesc_bf16_f32(CG * BM, BN, A_MN, B_MN);
+    constexpr uint32_t kBChunkStride = 64 * BK * 2;
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < kp.units && ok; u += gridDim.x) {
+    for (int u = cluster_id; u < kp.units && ok; u += nclusters) {
       int tm, tn, split;
       decode_unit(kp, u, tm, tn, split);
       const int kb0 = split * kp.kb_per_split;
@@ -209,204 +529,64 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t a_addr = smem_u32(sA + stage * kABytes);
-        const uint32_t b_addr = smem_u32(sB + stage * kBBytes);
+        const uint32_t b_addr = smem_u32(sB + stage * C::kBBytes);
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k) {
-          uint64_t adesc, bdesc;
-          if (!A_MN) adesc = sdesc_sw128(a_addr + k * 32, 16, 1024);
-          else       adesc = sdesc_sw128(a_addr + k * 2048, 64 * BK * 2, 1024);
-          if (!B_MN) bdesc = sdesc_sw128(b_addr + k * 32, 16, 1024);
-          else       bdesc = sdesc_sw128(b_addr + k * 2048, 64 * BK * 2, 1024);
-          umma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          const uint64_t adesc = A_MN ? sdesc_sw128(a_addr + k * 2048, kBChunkStride, 1024)
+                                      : sdesc_sw128(a_addr + k * 32, 16, 1024);
+          const uint64_t bdesc = B_MN ? sdesc_sw128(b_addr + k * 2048, kBChunkStride, 1024)
+                                      : sdesc_sw128(b_addr + k * 32, 16, 1024);
+          const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
+          if constexpr (CG == 2) umma_bf16_ss_pair(d_tmem, adesc, bdesc, idesc, accum);
+          else umma_bf16_ss(d_tmem, adesc, bdesc, idesc, accum);
         }
-        umma_commit(&empty_bar[stage]);
+        if constexpr (CG == 2) umma_commit_pair_both(&empty_bar[stage]);
+        else umma_commit(&empty_bar[stage]);
         if (++stage == kStages) {
           stage = 0;
           phase ^= 1u;
         }
       }
       if (!ok) break;
-      umma_commit(&tfull_bar[acc]);
+      if constexpr (CG == 2) umma_commit_pair_both(&tfull_bar[acc]);
+      else umma_commit(&tfull_bar[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
-    // Drain: wait for every MMA this thread issued before TMEM is released.
-    umma_commit(drain_bar);
+    // Drain: every MMA this thread issued completes before TMEM is released.
+    if constexpr (CG == 2) umma_commit_pair(drain_bar);
+    else umma_commit(drain_bar);
     mbar_wait(drain_bar, 0, p.status, 22, nullptr);
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int c_begin = EW == 8 ? (ew / 4) * 4 : 0;
+    const int c_end = EW == 8 ? c_begin + 4 : 8;
+    uint32_t tempty_addr[2] = {smem_u32(&tempty_bar[0]), smem_u32(&tempty_bar[1])};
+    if constexpr (CG == 2) {
+      tempty_addr[0] = map_to_cta(tempty_addr[0], 0);
+      tempty_addr[1] = map_to_cta(tempty_addr[1], 0);
+    }
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < kp.units; u += gridDim.x) {
+    for (int u = cluster_id; u < kp.units; u += nclusters) {
       int tm, tn, split;
       decode_unit(kp, u, tm, tn, split);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, p.status, 30, abort_flag)) break;
       tc_fence_after();
-      const int row = tm * BM + quarter * 32 + lane;
-      const bool row_ok = row < p.M;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-
-      float ce_m = -INFINITY, ce_s = 0.f, ce_t = 0.f;
-      bool ce_hit = false;
-      long long tgt = -1;
-      if (EPI == kEpiCE && row_ok) tgt = p.ce_target[row] - p.ce_col_offset;
-
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        tmem_ld_wait();
-        const int n0 = tn * BN + c * 32;
-        if (!row_ok || n0 >= p.N) continue;
-        const bool full = (n0 + 32 <= p.N);
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
-
-        if (EPI == kEpiBF16) {
-          if (p.bias != nullptr) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += (n0 + j < p.N) ? p.bias[n0 + j] : 0.f;
-          }
-          if (p.gelu) {
-            __nv_bfloat16* aux = reinterpret_cast<__nv_bfloat16*>(p.aux) + row * p.ldaux + n0;
-            if (full) {
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                uint4 w;
-                w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-                w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-                w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-                w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-                reinterpret_cast<uint4*>(aux)[q] = w;
-              }
-            } else {
-              #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n0 + j < p.N) aux[j] = __float2bfloat16_rn(v[j]);
-            }
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              // GELU of the bf16-rounded pre-activation, exactly what the
-              // backward pass will differentiate.
-              float h = __bfloat162float(__float2bfloat16_rn(v[j]));
-              v[j] = gelu_tanh(h);
-            }
-          }
-          if (p.resid != nullptr) {
-            const __nv_bfloat16* rs = reinterpret_cast<const __nv_bfloat16*>(p.resid) + row * p.ldres + n0;
-            if (full) {
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                uint4 w = reinterpret_cast<const uint4*>(rs)[q];
-                float2 f0 = unpack_bf16x2(w.x), f1 = unpack_bf16x2(w.y), f2 = unpack_bf16x2(w.z),
-                       f3 = unpack_bf16x2(w.w);
-                v[q * 8 + 0] += f0.x; v[q * 8 + 1] += f0.y; v[q * 8 + 2] += f1.x; v[q * 8 + 3] += f1.y;
-                v[q * 8 + 4] += f2.x; v[q * 8 + 5] += f2.y; v[q * 8 + 6] += f3.x; v[q * 8 + 7] += f3.y;
-              }
-            } else {
-              #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n0 + j < p.N) v[j] += __bfloat162float(rs[j]);
-            }
-          }
-        } else if (EPI == kEpiDGELU) {
-          const __nv_bfloat16* hx = reinterpret_cast<const __nv_bfloat16*>(p.aux) + row * p.ldaux + n0;
-          if (full) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 w = reinterpret_cast<const uint4*>(hx)[q];
-              float2 f0 = unpack_bf16x2(w.x), f1 = unpack_bf16x2(w.y), f2 = unpack_bf16x2(w.z),
-                     f3 = unpack_bf16x2(w.w);
-              v[q * 8 + 0] *= gelu_tanh_grad(f0.x); v[q * 8 + 1] *= gelu_tanh_grad(f0.y);
-              v[q * 8 + 2] *= gelu_tanh_grad(f1.x); v[q * 8 + 3] *= gelu_tanh_grad(f1.y);
-              v[q * 8 + 4] *= gelu_tanh_grad(f2.x); v[q * 8 + 5] *= gelu_tanh_grad(f2.y);
-              v[q * 8 + 6] *= gelu_tanh_grad(f3.x); v[q * 8 + 7] *= gelu_tanh_grad(f3.y);
-            }
-          } else {
-            #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) v[j] *= gelu_tanh_grad(__bfloat162float(hx[j]));
-          }
-        }
-
-        if (EPI == kEpiF32) {
-          float* dst;
-          bool add = false;
-          if (p.k_splits > 1) {
-            dst = p.workspace + (static_cast<long long>(split) * p.M + row) * p.ldws + n0;
-          } else {
-            dst = reinterpret_cast<float*>(p.D) + row * p.ldd + n0;
-            add = p.beta != 0;
-          }
-          if (full) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              float4 w = make_float4(v[q * 4 + 0], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
-              if (add) {
-                float4 o = reinterpret_cast<const float4*>(dst)[q];
-                w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
-              }
-              reinterpret_cast<float4*>(dst)[q] = w;
-            }
-          } else {
-            #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) dst[j] = add ? dst[j] + v[j] : v[j];
-          }
-        } else {
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + n0;
-          if (EPI == kEpiCE) {
-            // Round once; statistics use the same bf16 values the backward reads.
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
-            float cm = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) cm = fmaxf(cm, v[j]);
-            if (cm > ce_m) {
-              ce_s = (ce_m == -INFINITY) ? 0.f : ce_s * exp2f((ce_m - cm) * 1.4426950408889634f);
-              ce_m = cm;
-            }
-            float s = 0.f;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) s += exp2f((v[j] - ce_m) * 1.4426950408889634f);
-            ce_s += s;
-            if (tgt >= n0 && tgt < n0 + 32) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n0 + j == tgt) ce_t = v[j];
-              ce_hit = true;
-            }
-          }
-          if (full) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 w;
-              w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-              w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-              w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-              w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-              reinterpret_cast<uint4*>(dst)[q] = w;
-            }
-          } else {
-            #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) dst[j] = __float2bfloat16_rn(v[j]);
-          }
-        }
-      }
-      if (EPI == kEpiCE && row_ok) {
-        p.ce_max[static_cast<long long>(tn) * p.M + row] = ce_m;
-        p.ce_sum[static_cast<long long>(tn) * p.M + row] = ce_s;
-        if (ce_hit) p.ce_tgt[row] = ce_t;
-      }
+      const int row = tm * (CG * BM) + static_cast<int>(crank) * BM + quarter * 32 + lane;
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      epilogue_row<EPI>(p, row, tn, split, t_row, c_begin, c_end);
       tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (CG == 2) mbar_arrive_remote(tempty_addr[acc]);
+        else mbar_arrive(&tempty_bar[acc]);
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -416,8 +596,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+  if (warp == 1) {
+    if constexpr (CG == 2) tmem_dealloc_pair(tmem_base, kTmemCols);
+    else tmem_dealloc(tmem_base, kTmemCols);
+  }
 }
 
 // Fixed-order sum of split-K partials: D (+)= sum_s ws[s].  Deterministic, so
@@ -470,18 +654,63 @@ bool make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
 
 int g_num_sms = 0;
 
-template <bool A_MN, bool B_MN, int EPI>
+template <int CG, int kEW, bool A_MN, bool B_MN, int EPI>
 cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const md::gemm::KParams& kp, int grid,
                    cudaStream_t stream) {
-  auto kern = md::gemm::gemm_kernel<A_MN, B_MN, EPI>;
-  static bool attr_set = false;  // per instantiation
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, md::gemm::kSmemBytes);
+  auto kern = md::gemm::gemm_kernel<CG, kEW, A_MN, B_MN, EPI>;
+  constexpr int smem = md::gemm::Cfg<CG>::kSmemBytes;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    if (CG == 2) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+      (void)e;
+    }
+    attr_done[dev] = 1;
   }
-  kern<<<grid, md::gemm::kThreads, md::gemm::kSmemBytes, stream>>>(ta, tb, kp);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(64 + 32 * kEW);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  cfg.numAttrs = 0;
+  if (CG == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, kp);
+}
+
+template <int CG, int EW>
+cudaError_t dispatch(bool amn, bool bmn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+                     const md::gemm::KParams& kp, int grid, cudaStream_t s, bool* bad) {
+  using namespace md::gemm;
+  *bad = false;
+  if (!amn && !bmn) {
+    if (epi == kEpiBF16) return launch<CG, EW, false, false, kEpiBF16>(ta, tb, kp, grid, s);
+    if (epi == kEpiF32) return launch<CG, EW, false, false, kEpiF32>(ta, tb, kp, grid, s);
+    if (epi == kEpiCE) return launch<CG, EW, false, false, kEpiCE>(ta, tb, kp, grid, s);
+  } else if (!amn && bmn) {
+    if (epi == kEpiBF16) return launch<CG, EW, false, true, kEpiBF16>(ta, tb, kp, grid, s);
+    if (epi == kEpiF32) return launch<CG, EW, false, true, kEpiF32>(ta, tb, kp, grid, s);
+    if (epi == kEpiDGELU) return launch<CG, EW, false, true, kEpiDGELU>(ta, tb, kp, grid, s);
+  } else if (amn && bmn) {
+    if (epi == kEpiF32) return launch<CG, EW, true, true, kEpiF32>(ta, tb, kp, grid, s);
+    if (epi == kEpiBF16) return launch<CG, EW, true, true, kEpiBF16>(ta, tb, kp, grid, s);
+  } else {
+    if (epi == kEpiF32) return launch<CG, EW, true, false, kEpiF32>(ta, tb, kp, grid, s);
+    if (epi == kEpiBF16) return launch<CG, EW, true, false, kEpiBF16>(ta, tb, kp, grid, s);
+  }
+  *bad = true;
+  return cudaSuccess;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -499,7 +728,7 @@ extern "C" int md_gemm(const MdGemmParams* prm, cudaStream_t stream) {
   if (!aligned16(p.A) || !aligned16(p.B) || (p.lda % 8) || (p.ldb % 8)) return -4;
   if (p.epi == kEpiF32) {
     if (!aligned16(p.D) || (p.ldd % 4)) return -5;
-    if (p.k_splits > 1 && (p.workspace == nullptr || !aligned16(p.workspace) || (p.ldws % 4))) return -6;
+    if (p.k_splits > 1 && p.workspace != nullptr && (!aligned16(p.workspace) || (p.ldws % 4))) return -6;
   } else {
     if (!aligned16(p.D) || (p.ldd % 8)) return -5;
     if (p.k_splits != 1) return -6;
@@ -511,70 +740,71 @@ extern "C" int md_gemm(const MdGemmParams* prm, cudaStream_t stream) {
     return -9;
   if (p.k_splits < 1) p.k_splits = 1;
 
-  CUtensorMap ta, tb;
-  bool ok;
-  if (!p.a_mn_major) ok = make_map(&ta, p.A, p.K, p.M, p.lda, BM);
-  else               ok = make_map(&ta, p.A, p.M, p.K, p.lda, 64);
-  if (!ok) return -10;
-  if (!p.b_mn_major) ok = make_map(&tb, p.B, p.K, p.N, p.ldb, BN);
-  else               ok = make_map(&tb, p.B, p.N, p.K, p.ldb, 64);
-  if (!ok) return -11;
-
-  KParams kp;
-  kp.p = p;
-  kp.tiles_m = (p.M + BM - 1) / BM;
-  kp.tiles_n = (p.N + BN - 1) / BN;
-  kp.k_blocks = (p.K + BK - 1) / BK;
-  if (p.k_splits > kp.k_blocks) p.k_splits = kp.k_blocks;
-  kp.p.k_splits = p.k_splits;
-  kp.kb_per_split = (kp.k_blocks + p.k_splits - 1) / p.k_splits;
-  // Recompute the split count so that no split is empty.
-  kp.p.k_splits = (kp.k_blocks + kp.kb_per_split - 1) / kp.kb_per_split;
-  kp.units = kp.tiles_m * kp.tiles_n * kp.p.k_splits;
-
   if (g_num_sms == 0) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
   }
-  int cap = p.num_sms > 0 ? p.num_sms : g_num_sms;
-  int grid = kp.units < cap ? kp.units : cap;
+  // Tile configuration: the 2-CTA 256x256 tiles win whenever there are enough
+  // rows; weight-gradient products with few output rows keep 128-row tiles
+  // (more tiles to spread over the SMs).
+  int cg = p.cta_group;
+  if (cg != 1 && cg != 2) cg = p.a_mn_major ? (p.M >= 2304 ? 2 : 1) : (p.M >= 512 ? 2 : 1);
+  // Four epilogue warps measured best across the GPT shapes (eight only
+  // matched it for the GELU / cross-entropy epilogues).
+  if (p.epi_warps != 4 && p.epi_warps != 8)
+    p.epi_warps = (p.epi == kEpiCE || p.epi == kEpiDGELU || (p.epi == kEpiBF16 && p.gelu)) ? 8 : 4;
 
-  cudaError_t e;
-  const bool amn = p.a_mn_major != 0, bmn = p.b_mn_major != 0;
-  if (!amn && !bmn) {
-    switch (p.epi) {
-      case kEpiBF16: e = launch<false, false, kEpiBF16>(ta, tb, kp, grid, stream); break;
-      case kEpiF32: e = launch<false, false, kEpiF32>(ta, tb, kp, grid, stream); break;
-      case kEpiCE: e = launch<false, false, kEpiCE>(ta, tb, kp, grid, stream); break;
-      default: return -12;
-    }
-  } else if (!amn && bmn) {
-    switch (p.epi) {
-      case kEpiBF16: e = launch<false, true, kEpiBF16>(ta, tb, kp, grid, stream); break;
-      case kEpiF32: e = launch<false, true, kEpiF32>(ta, tb, kp, grid, stream); break;
-      case kEpiDGELU: e = launch<false, true, kEpiDGELU>(ta, tb, kp, grid, stream); break;
-      default: return -12;
-    }
-  } else if (amn && bmn) {
-    switch (p.epi) {
-      case kEpiF32: e = launch<true, true, kEpiF32>(ta, tb, kp, grid, stream); break;
-      case kEpiBF16: e = launch<true, true, kEpiBF16>(ta, tb, kp, grid, stream); break;
-      default: return -12;
-    }
+  CUtensorMap ta, tb;
+  bool ok;
+  if (!p.a_mn_major) ok = make_map(&ta, p.A, p.K, p.M, p.lda, BM);
+  else               ok = make_map(&ta, p.A, p.M, p.K, p.lda, 64);
+  if (!ok) return -10;
+  if (!p.b_mn_major) ok = make_map(&tb, p.B, p.K, p.N, p.ldb, BN / cg);
+  else               ok = make_map(&tb, p.B, p.N, p.K, p.ldb, 64);
+  if (!ok) return -11;
+
+  KParams kp;
+  kp.p = p;
+  kp.tiles_m = (p.M + cg * BM - 1) / (cg * BM);
+  kp.tiles_n = (p.N + BN - 1) / BN;
+  kp.k_blocks = (p.K + BK - 1) / BK;
+  if (p.k_splits > kp.k_blocks) p.k_splits = kp.k_blocks;
+  kp.kb_per_split = (kp.k_blocks + p.k_splits - 1) / p.k_splits;
+  kp.p.k_splits = (kp.k_blocks + kp.kb_per_split - 1) / kp.kb_per_split;  // no empty split
+  kp.units = kp.tiles_m * kp.tiles_n * kp.p.k_splits;
+
+  int cap = p.num_sms > 0 ? p.num_sms : g_num_sms;
+  int grid;
+  if (cg == 2) {
+    const int clusters = kp.units < cap / 2 ? kp.units : cap / 2;
+    grid = 2 * (clusters > 0 ? clusters : 1);
   } else {
-    switch (p.epi) {
-      case kEpiF32: e = launch<true, false, kEpiF32>(ta, tb, kp, grid, stream); break;
-      case kEpiBF16: e = launch<true, false, kEpiBF16>(ta, tb, kp, grid, stream); break;
-      default: return -12;
-    }
+    grid = kp.units < cap ? kp.units : cap;
   }
+
+  if (p.epi == kEpiF32 && kp.p.k_splits > 1 && p.workspace == nullptr && !p.beta) {
+    cudaError_t ez = cudaMemset2DAsync(p.D, static_cast<size_t>(p.ldd) * 4, 0, static_cast<size_t>(p.N) * 4,
+                                       static_cast<size_t>(p.M), stream);
+    if (ez != cudaSuccess) return static_cast<int>(ez);
+  }
+  bool bad = false;
+  const int ew = p.epi_warps == 4 ? 4 : 8;
+  cudaError_t e;
+  if (cg == 2) {
+    e = ew == 4 ? dispatch<2, 4>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, kp, grid, stream, &bad)
+                : dispatch<2, 8>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, kp, grid, stream, &bad);
+  } else {
+    e = ew == 4 ? dispatch<1, 4>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, kp, grid, stream, &bad)
+                : dispatch<1, 8>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, kp, grid, stream, &bad);
+  }
+  if (bad) return -12;
   if (e != cudaSuccess) return static_cast<int>(e);
 
-  if (p.epi == kEpiF32 && kp.p.k_splits > 1) {
+  if (p.epi == kEpiF32 && kp.p.k_splits > 1 && p.workspace != nullptr) {
     const long long total = static_cast<long long>(p.M) * p.N;
     int blocks = static_cast<int>((total + 255) / 256);
-    if (blocks > 4 * g_num_sms * 8) blocks = 4 * g_num_sms * 8;
+    if (blocks > 32 * g_num_sms) blocks = 32 * g_num_sms;
     md::gemm::splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p.workspace, reinterpret_cast<float*>(p.D), p.ldd,
                                                                p.ldws, p.M, p.N, kp.p.k_splits, p.beta);
     e = cudaGetLastError();
@@ -583,5 +813,5 @@ extern "C" int md_gemm(const MdGemmParams* prm, cudaStream_t stream) {
   return 0;
 }
 
-// Number of CE partial column tiles the kEpiCE epilogue writes for N columns.
-extern "C" int md_gemm_tile_n() { return md::gemm::BN; }
+// Width of the column slabs the kEpiCE epilogue keeps statistics for.
+extern "C" int md_gemm_ce_slab() { return md::gemm::kCeSlab; }

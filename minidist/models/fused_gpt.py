@@ -355,7 +355,7 @@ class _HeadFn(torch.autograd.Function):
             loss = None
         else:
             tgt_flat = targets.reshape(-1).contiguous()
-            tiles = -(-V // G.TILE_N)
+            tiles = -(-V // G.CE_SLAB)
             tmax = torch.empty(tiles, M, dtype=torch.float32, device=x.device)
             tsum = torch.empty_like(tmax)
             ttgt = torch.zeros(M, dtype=torch.float32, device=x.device)

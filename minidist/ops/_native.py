@@ -63,8 +63,8 @@ def _declare(h: ctypes.CDLL) -> None:
     vp, i32, i64, f32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_float
     h.md_gemm.argtypes = [ctypes.POINTER(GemmParams), vp]
     h.md_gemm.restype = i32
-    h.md_gemm_tile_n.argtypes = []
-    h.md_gemm_tile_n.restype = i32
+    h.md_gemm_ce_slab.argtypes = []
+    h.md_gemm_ce_slab.restype = i32
     for name, args in _EXTRA_DECLS.items():
         fn = getattr(h, name, None)
         if fn is None:
@@ -131,6 +131,8 @@ class GemmParams(ctypes.Structure):
         ("ce_col_offset", ctypes.c_longlong),
         ("num_sms", ctypes.c_int),
         ("status", ctypes.c_void_p),
+        ("cta_group", ctypes.c_int),
+        ("epi_warps", ctypes.c_int),
     ]
 
 

@@ -15,6 +15,7 @@ wgrad      dW[N,K] = dy^T x      dy MN-major x MN-major
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -22,6 +23,15 @@ from . import _native as nat
 
 EPI_BF16, EPI_F32, EPI_DGELU, EPI_CE = 0, 1, 2, 3
 TILE_M, TILE_N = 128, 256
+CE_SLAB = 128  # the kEpiCE epilogue keeps statistics per 128-column slab
+
+# Optional overrides of the kernel's own tile choices (0 = let the kernel choose).
+_ENV_CG = int(os.environ.get("MINIDIST_GEMM_CTA_GROUP", "0"))
+_ENV_EW = int(os.environ.get("MINIDIST_GEMM_EPI_WARPS", "0"))
+# Split-K weight gradients: fixed-order workspace reduction when set, fp32
+# atomic accumulation into the gradient otherwise (faster; none of the
+# split-K outputs is a replicated tensor-parallel parameter).
+_DETERMINISTIC = os.environ.get("MINIDIST_DETERMINISTIC", "0") not in ("0", "", "false", "no")
 
 
 def _vp(t):
@@ -54,6 +64,8 @@ def gemm(
     ce: tuple | None = None,
     ce_col_offset: int = 0,
     num_sms: int = 0,
+    cta_group: int = 0,
+    epi_warps: int = 0,
     stream: torch.cuda.Stream | None = None,
 ) -> None:
     """Raw launcher; see ``struct MdGemmParams`` for the meaning of each field."""
@@ -72,7 +84,7 @@ def gemm(
     p.resid = None if resid is None else resid.data_ptr()
     p.ldres = ldres
     ws = None
-    if epi == EPI_F32 and k_splits > 1:
+    if epi == EPI_F32 and k_splits > 1 and _DETERMINISTIC:
         ldws = (N + 3) // 4 * 4
         ws = torch.empty(k_splits * M * ldws, dtype=torch.float32, device=D.device)
         p.workspace = ws.data_ptr()
@@ -84,6 +96,8 @@ def gemm(
             target.data_ptr(), cmax.data_ptr(), csum.data_ptr(), ctgt.data_ptr())
     p.ce_col_offset = ce_col_offset
     p.num_sms = num_sms
+    p.cta_group = cta_group or _ENV_CG
+    p.epi_warps = epi_warps or _ENV_EW
     p.status = nat.status_ptr(D.device)
     rc = nat.lib().md_gemm(ctypes.byref(p), ctypes.c_void_p(nat.stream_ptr(stream)))
     nat.check(rc, f"md_gemm(M={M},N={N},K={K},a_mn={a_mn},b_mn={b_mn},epi={epi})")
@@ -175,7 +189,7 @@ def linear_wgrad(
     M, N = dy.shape
     K = x.shape[1]
     if k_splits is None:
-        units = -(-N // TILE_M) * -(-K // TILE_N)
+        units = -(-N // (2 * TILE_M if N >= 2304 else TILE_M)) * -(-K // TILE_N)
         k_splits = pick_k_splits(units, -(-M // 64), nat.num_sms(dy.device))
     gemm(dy, x, out, M=N, N=K, K=M, lda=_ld(dy), ldb=_ld(x), ldd=_ld(out), a_mn=True, b_mn=True,
          epi=EPI_F32, beta=accumulate, k_splits=k_splits)

@@ -15,6 +15,7 @@ import math
 import torch
 
 from .ops import _native as nat
+from .ops import grads as gradsink
 
 __all__ = ["FusedAdamW"]
 
@@ -62,6 +63,7 @@ class FusedAdamW(torch.optim.Optimizer):
             rest = [p for p, c in zip(params, cuda) if not c]
             if fused:
                 self._fused_update(gi, fused, lr, b1, b2, eps, wd, bc1, bc2_sqrt)
+                self._ensure_grad_buffers()
             for p in rest:
                 st = self.state[p]
                 g = p.grad.to(p.dtype)
@@ -71,6 +73,34 @@ class FusedAdamW(torch.optim.Optimizer):
                 denom = st["exp_avg_sq"].sqrt().div_(bc2_sqrt).add_(eps)
                 p.addcdiv_(st["exp_avg"], denom, value=-lr / bc1)
         return loss
+
+    def _ensure_grad_buffers(self) -> None:
+        """Give every CUDA fp32 parameter without one a persistent gradient buffer.
+
+        Fused kernels write gradients into these views (ops/grads.py), so the
+        gradient pointers stay fixed from step to step and the device-side
+        parameter table is built once.  Parameters that a wrapper (DDP) has
+        already given a buffer keep it.
+        """
+        if getattr(self, "_grad_buffers_done", False):
+            return
+        self._grad_buffers_done = True
+        todo = [p for g in self.param_groups for p in g["params"]
+                if p.is_cuda and p.dtype == torch.float32 and gradsink.main_grad(p) is None]
+        if not todo:
+            return
+        align = 64
+        sizes = [(p.numel() + align - 1) // align * align for p in todo]
+        flat = torch.zeros(sum(sizes), dtype=torch.float32, device=todo[0].device)
+        off = 0
+        for p, n in zip(todo, sizes):
+            view = flat[off: off + p.numel()].view_as(p)
+            if p.grad is not None:
+                view.copy_(p.grad)
+                p.grad = view
+            gradsink.set_main_grad(p, view)
+            off += n
+        self._grad_flat = flat
 
     def _fused_update(self, gi, params, lr, b1, b2, eps, wd, bc1, bc2_sqrt) -> None:
         from .models.fused_gpt import _SHADOW, _SHADOW_VER

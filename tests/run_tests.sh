@@ -1,0 +1,13 @@
+#!/usr/bin/env bash
+# CPU correctness suite (Gloo) plus a torchrun smoke test of the trainer; on a
+# CUDA machine also the GPU tier (`-m gpu`).
+set -euo pipefail
+cd "$(dirname "$0")/.."
+python -m pytest tests -q -m "not gpu" "$@"
+python -m torch.distributed.run --nnodes=1 --nproc-per-node=4 --master-addr=127.0.0.1 --master-port=29562 \
+  examples/train_gpt.py --tp 2 --pp 2 --strategy none --microbatches 4 --layers 4 --embd 128 --heads 4 \
+  --vocab 1024 --seq-len 64 --batch-size 8 --steps 4 --backend gloo
+if python -c 'import torch, sys; sys.exit(0 if torch.cuda.is_available() else 1)'; then
+  python -m pytest tests -q -m gpu
+fi
+echo "all green"

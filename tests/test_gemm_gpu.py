@@ -95,3 +95,20 @@ def test_wgrad_auto_split_large_reduction():
     G.linear_wgrad(dy, x, out)
     nat.check_status()
     assert _rel(out, dy.float().t() @ x.float()) < 1e-4
+
+
+@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
+def test_cta_group_variants(cg, a_mn, b_mn):
+    """Both tile configurations (1-CTA 128x256, 2-CTA 256x256) for every operand layout, ragged sizes."""
+    torch.manual_seed(6)
+    M, N, K = 1000, 700, 520
+    A = _bf16(K, M) if a_mn else _bf16(M, K)
+    B = _bf16(K, N) if b_mn else _bf16(N, K)
+    D = torch.zeros(M, (N + 3) // 4 * 4, device="cuda")[:, :N]
+    G.gemm(A, B, D, M=M, N=N, K=K, lda=A.stride(0), ldb=B.stride(0), ldd=D.stride(0), a_mn=a_mn, b_mn=b_mn,
+           epi=G.EPI_F32, cta_group=cg)
+    Af = A.float().t() if a_mn else A.float()
+    Bf = B.float() if b_mn else B.float().t()
+    nat.check_status()
+    assert _rel(D, Af @ Bf) < 1e-4
