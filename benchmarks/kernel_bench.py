@@ -10,7 +10,8 @@ Times are CUDA-event averages after warm-up on the launching stream.  GEMM
 rows report forward (y = x W^T), data-gradient (dx = dy W) and weight-gradient
 (dW = dy^T x) throughput next to cuBLAS (torch.matmul) for the same product.
 Attention rows compare with torch's scaled_dot_product_attention (cuDNN / flash
-backends).  Also the fixed small case used for ncu captures (``--iters``).
+backends).  ``--op gemm --shape M,N,K --which fwd --iters 3`` is the small case
+used for ncu captures of one GEMM launch.
 """
 
 from __future__ import annotations
@@ -45,18 +46,19 @@ def timed(fn, iters: int, warmup: int = 3) -> float:
 def bench_gemm(M, N, K, iters, cta_group=0, which="fwd,dgrad,wgrad"):
     x = torch.randn(M, K, device="cuda").bfloat16()
     w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
-    dy = torch.randn(M, N, device="cuda").bfloat16()
-    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    dy = G.empty_padded(M, N, device="cuda")  # row strides must be 16-byte multiples (N = 50257)
+    dy.copy_(torch.randn(M, N, device="cuda"))
+    out = G.empty_padded(M, N, device="cuda")
     dx = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
     dw = torch.empty(N, K, device="cuda")
     fl = 2.0 * M * N * K
     rows = []
     if "fwd" in which:
-        t = timed(lambda: G.gemm(x, w, out, M=M, N=N, K=K, lda=K, ldb=K, ldd=N, cta_group=cta_group), iters)
+        t = timed(lambda: G.gemm(x, w, out, M=M, N=N, K=K, lda=K, ldb=K, ldd=out.stride(0), cta_group=cta_group), iters)
         tc = timed(lambda: torch.matmul(x, w.t()), iters)
         rows.append(("fwd", t, tc))
     if "dgrad" in which:
-        t = timed(lambda: G.gemm(dy, w, dx, M=M, N=K, K=N, lda=N, ldb=K, ldd=K, b_mn=True, cta_group=cta_group), iters)
+        t = timed(lambda: G.gemm(dy, w, dx, M=M, N=K, K=N, lda=dy.stride(0), ldb=K, ldd=K, b_mn=True, cta_group=cta_group), iters)
         tc = timed(lambda: torch.matmul(dy, w), iters)
         rows.append(("dgrad", t, tc))
     if "wgrad" in which:
