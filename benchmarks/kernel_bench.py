@@ -75,6 +75,7 @@ def bench_attention(B, H, S, D, iters):
     qkv = torch.randn(B * S, 3 * H * D, device="cuda").bfloat16()
     fl_f = 4.0 * B * H * S * S * D / 2
     t = timed(lambda: K.attention_fwd(qkv, B, S, H, D), iters)
+    tm = timed(lambda: K.attention_fwd(qkv, B, S, H, D, impl="mma"), iters)
     y, lse = K.attention_fwd(qkv, B, S, H, D)
     dy = torch.randn_like(y)
     tb = timed(lambda: K.attention_bwd(qkv, y, dy, lse, B, S, H, D), iters)
@@ -86,7 +87,7 @@ def bench_attention(B, H, S, D, iters):
     trb = timed(lambda: torch.autograd.grad(o, (q, k, v), g, retain_graph=True), iters)
     nat.check_status()
     print(f"attention fwd B={B} H={H} S={S} D={D}: {t * 1e6:8.1f} us {fl_f / t / 1e12:6.1f} TFLOP/s | "
-          f"torch SDPA {tr * 1e6:8.1f} us {fl_f / tr / 1e12:6.1f} TFLOP/s")
+          f"torch SDPA {tr * 1e6:8.1f} us {fl_f / tr / 1e12:6.1f} TFLOP/s | mma.sync {tm * 1e6:8.1f} us")
     print(f"attention bwd B={B} H={H} S={S} D={D}: {tb * 1e6:8.1f} us {2.5 * fl_f / tb / 1e12:6.1f} TFLOP/s | "
           f"torch SDPA {trb * 1e6:8.1f} us {2.5 * fl_f / trb / 1e12:6.1f} TFLOP/s")
 
@@ -115,7 +116,7 @@ def main():
     p.add_argument("--which", default="fwd,dgrad,wgrad")
     a = p.parse_args()
     shp = [int(v) for v in a.shape.split(",")] if a.shape else None
-    if a.op in ("all", "gemm"):
+    if a.op in ("all", "gemm") and a.which != "none":
         for s in ([shp] if shp and a.op == "gemm" else
                   [(16384, 2304, 768), (16384, 768, 768), (16384, 3072, 768), (16384, 768, 3072),
                    (16384, 50257, 768), (8192, 8192, 8192)]):

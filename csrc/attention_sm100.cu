@@ -1,0 +1,481 @@
+// Causal flash attention forward on the 5th-generation tensor cores (tcgen05),
+// bf16 in / bf16 out, head_dim 64 or 128.
+//
+// Same contract as md_attn_fwd of attention.cu (which dispatches here for
+// these head sizes): Q, K, V are read in place from the QKV projection output
+// [B*S, ldq] whose columns are interleaved per head as [H, 3, D] (reference
+// models/gpt.py:92-99, 123-126: F.scaled_dot_product_attention(is_causal=True));
+// the output is [B*S, ldo] with head h at columns h*D; lse [B, H, S] holds the
+// natural-log log-sum-exp of every query row for the backward pass.
+//
+// Persistent kernel, one CTA per SM, warp-specialised:
+//   warp 0      TMA producer: Q tile (128 queries) and, per key block, K and V
+//               tiles (128 keys) through a 3-D tensor map [B, S, 3*H*D] whose
+//               sequence-end rows read as zero.
+//   warp 1      MMA issuer (one thread): S = Q K^T into one of two TMEM score
+//               buffers (128 x 128 fp32), then O += P V into a TMEM accumulator
+//               (128 x D fp32).  The score product of block g+1 is queued
+//               before the P V product of block g, so the tensor core computes
+//               scores while the softmax warps exponentiate.
+//   warps 2..5  softmax: thread t owns query row t (TMEM lane t, 32x32b loads),
+//               so row max and row sum need no shuffles.  Scores come out of
+//               TMEM, exp2 on the MUFU pipe, P goes to shared memory as bf16 in
+//               the 128-byte-swizzled K-major layout the P V product reads.
+//               The running max only moves when it grows by more than 2^8
+//               (factor kRescaleLog2), so the O rescale (TMEM load/scale/store)
+//               is rare after the first blocks; l and O stay consistent since
+//               both use the same stale max.  Final O / l and lse are written
+//               straight from TMEM.
+//
+// Work items are (query tile, batch*head) pairs ordered longest-first (the
+// causal tile qt has qt+1 key blocks) and dealt round-robin to the CTAs.
+//
+// Every mbarrier wait is bounded (md_sm100.cuh); a CTA that gives up records a
+// status, lets the other roles see the abort flag, drains its bulk copies and
+// MMAs, frees TMEM and exits.
+#include <cudaTypedefs.h>
+
+#include "md_sm100.cuh"
+
+namespace md {
+namespace attn_tc {
+
+constexpr int kBM = 128;   // queries per tile (TMEM lanes)
+constexpr int kBN = 128;   // keys per block
+constexpr float kRescaleLog2 = 8.0f;
+constexpr int kThreads = 192;
+
+template <int D>
+struct FwdCfg {
+  static constexpr int kChunks = D / 64;               // 64-column (128 B) swizzle atoms along head_dim
+  static constexpr int kTileBytes = kBM * D * 2;       // one Q/K/V tile
+  static constexpr int kQBufs = D == 64 ? 2 : 1;
+  static constexpr int kKvStages = D == 64 ? 3 : 2;
+  static constexpr int kPBytes = kBM * kBN * 2;        // P tile (bf16)
+  static constexpr int kSmemData = (kQBufs + 2 * kKvStages) * kTileBytes + kPBytes;
+  static constexpr int kSmemBytes = kSmemData + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+  static constexpr uint32_t kTmemCols = 512;           // S0 [0,128) S1 [128,256) O [256, 256+D)
+  static constexpr uint32_t kOCol = 256;
+};
+
+struct FwdParams {
+  void* out;
+  long long ldo;
+  float* lse;
+  int B, H, S;
+  int n_qt;       // query tiles per sequence
+  int items;      // n_qt * B * H
+  float scale_log2;
+  Status* status;
+};
+
+__device__ __forceinline__ void decode(const FwdParams& p, int w, int& qt, int& b, int& h) {
+  const int bh_count = p.B * p.H;
+  qt = p.n_qt - 1 - w / bh_count;
+  const int bh = w % bh_count;
+  b = bh / p.H;
+  h = bh % p.H;
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Byte offset of (row, 16-byte chunk) inside a 128-row, 128-byte-row tile with
+// the TMA 128B swizzle (chunk index XOR row % 8; 8-row groups 1024 B apart).
+__device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
+  return static_cast<uint32_t>((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ FwdParams p) {
+  using C = FwdCfg<D>;
+  constexpr int KST = C::kKvStages;
+  constexpr int QB = C::kQBufs;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + QB * C::kTileBytes;
+  uint8_t* sV = sK + KST * C::kTileBytes;
+  uint8_t* sP = sV + KST * C::kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::kPBytes);
+  uint64_t* q_full = bars;           // [2]
+  uint64_t* q_empty = bars + 2;      // [2]
+  uint64_t* k_full = bars + 4;       // [4]
+  uint64_t* k_empty = bars + 8;      // [4]
+  uint64_t* v_full = bars + 12;      // [4]
+  uint64_t* v_empty = bars + 16;     // [4]
+  uint64_t* s_full = bars + 20;      // [2]
+  uint64_t* s_free = bars + 22;      // [2]
+  uint64_t* p_full = bars + 24;
+  uint64_t* o_done = bars + 25;
+  uint64_t* drain = bars + 26;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 27);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 28);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < QB; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < KST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA producer
+    int q_armed[2] = {-1, -1};
+    int k_armed[4] = {-1, -1, -1, -1};
+    int v_armed[4] = {-1, -1, -1, -1};
+    int g = 0, t = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
+      int qt, b, h;
+      decode(p, w, qt, b, h);
+      const int qb = t % QB;
+      const uint32_t qph = static_cast<uint32_t>(t / QB) & 1u;
+      if (!mbar_wait(&q_empty[qb], qph ^ 1u, p.status, 40, abort_flag)) break;
+      mbar_arrive_expect_tx(&q_full[qb], C::kTileBytes);
+      q_armed[qb] = static_cast<int>(qph);
+      const int col0 = h * 3 * D;
+#pragma unroll
+      for (int c = 0; c < C::kChunks; ++c)
+        tma_load_3d(&tm, &q_full[qb], sQ + qb * C::kTileBytes + c * (kBM * 128), col0 + c * 64, qt * kBM, b);
+      for (int j = 0; j <= qt; ++j, ++g) {
+        const int st = g % KST;
+        const uint32_t ph = static_cast<uint32_t>(g / KST) & 1u;
+        if (!mbar_wait(&k_empty[st], ph ^ 1u, p.status, 41, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
+        k_armed[st] = static_cast<int>(ph);
+#pragma unroll
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_3d(&tm, &k_full[st], sK + st * C::kTileBytes + c * (kBN * 128), col0 + D + c * 64, j * kBN, b);
+        if (!mbar_wait(&v_empty[st], ph ^ 1u, p.status, 42, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
+        v_armed[st] = static_cast<int>(ph);
+#pragma unroll
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_3d(&tm, &v_full[st], sV + st * C::kTileBytes + c * (kBN * 128), col0 + 2 * D + c * 64,
+                      j * kBN, b);
+      }
+    }
+    // No bulk copy into shared memory may still be in flight at exit.
+    for (int i = 0; i < QB; ++i)
+      if (q_armed[i] >= 0) mbar_wait(&q_full[i], static_cast<uint32_t>(q_armed[i]), p.status, 43, nullptr);
+    for (int i = 0; i < KST; ++i) {
+      if (k_armed[i] >= 0) mbar_wait(&k_full[i], static_cast<uint32_t>(k_armed[i]), p.status, 44, nullptr);
+      if (v_armed[i] >= 0) mbar_wait(&v_full[i], static_cast<uint32_t>(v_armed[i]), p.status, 45, nullptr);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idS = idesc_bf16_f32(kBM, kBN, false, false);
+    constexpr uint32_t idO = idesc_bf16_f32(kBM, D, false, true);
+    const uint32_t sp = smem_u32(sP);
+    int pend = -1;
+    bool pend_first = false;
+    // O += P V for block gp (P from shared memory, V MN-major).
+    auto issue_pv = [&](int gp, bool first) -> bool {
+      if (!mbar_wait(p_full, static_cast<uint32_t>(gp) & 1u, p.status, 52, abort_flag)) return false;
+      const int st = gp % KST;
+      if (!mbar_wait(&v_full[st], static_cast<uint32_t>(gp / KST) & 1u, p.status, 53, abort_flag)) return false;
+      tc_fence_after();
+      const uint32_t va = smem_u32(sV + st * C::kTileBytes);
+#pragma unroll
+      for (int kk = 0; kk < kBN / 16; ++kk) {
+        const uint64_t ad = sdesc_sw128(sp + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024);
+        const uint64_t bd = sdesc_sw128(va + kk * 2048, kBN * 128, 1024);
+        umma_bf16_ss(tmem + C::kOCol, ad, bd, idO, (first && kk == 0) ? 0u : 1u);
+      }
+      umma_commit(o_done);
+      umma_commit(&v_empty[st]);
+      return true;
+    };
+    int g = 0, t = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
+      int qt, b, h;
+      decode(p, w, qt, b, h);
+      const int qb = t % QB;
+      if (!mbar_wait(&q_full[qb], static_cast<uint32_t>(t / QB) & 1u, p.status, 50, abort_flag)) break;
+      const uint32_t qa = smem_u32(sQ + qb * C::kTileBytes);
+      for (int j = 0; j <= qt; ++j, ++g) {
+        const int st = g % KST;
+        if (!mbar_wait(&k_full[st], static_cast<uint32_t>(g / KST) & 1u, p.status, 51, abort_flag) ||
+            !mbar_wait(&s_free[g & 1], (static_cast<uint32_t>(g >> 1) & 1u) ^ 1u, p.status, 54, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ka = smem_u32(sK + st * C::kTileBytes);
+        const uint32_t sd = tmem + static_cast<uint32_t>((g & 1) * kBN);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
+          umma_bf16_ss(sd, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[g & 1]);
+        umma_commit(&k_empty[st]);
+        if (j == qt) umma_commit(&q_empty[qb]);
+        if (pend >= 0 && !issue_pv(pend, pend_first)) {
+          ok = false;
+          break;
+        }
+        pend = g;
+        pend_first = (j == 0);
+      }
+    }
+    if (ok && pend >= 0) issue_pv(pend, pend_first);
+    // Every MMA this thread issued completes before TMEM is released.
+    umma_commit(drain);
+    mbar_wait(drain, 0, p.status, 55, nullptr);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const float sl2 = p.scale_log2;
+    int g = 0;
+    for (int w = blockIdx.x; w < p.items; w += gridDim.x) {
+      int qt, b, h;
+      decode(p, w, qt, b, h);
+      float m = -INFINITY, l = 0.f;
+      bool ok = true;
+      for (int j = 0; j <= qt; ++j, ++g) {
+        if (!mbar_wait(&s_full[g & 1], static_cast<uint32_t>(g >> 1) & 1u, p.status, 60, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t r[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_base + static_cast<uint32_t>((g & 1) * kBN + c * 32), r[c]);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[g & 1]);
+        if (j == qt) {  // diagonal block: key > query is masked
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i > row) r[c][i] = __float_as_uint(-INFINITY);
+        }
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            mx0 = fmaxf(mx0, __uint_as_float(r[c][i]));
+            mx1 = fmaxf(mx1, __uint_as_float(r[c][i + 1]));
+          }
+        const float mx = fmaxf(mx0, mx1) * sl2;
+        const float m_use = mx > m + kRescaleLog2 ? mx : m;
+        const float alpha = ex2(m - m_use);
+        float l0 = 0.f, l1 = 0.f;
+        uint32_t pk[64];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float e0 = ex2(fmaf(__uint_as_float(r[c][i]), sl2, -m_use));
+            const float e1 = ex2(fmaf(__uint_as_float(r[c][i + 1]), sl2, -m_use));
+            l0 += e0;
+            l1 += e1;
+            pk[(c * 32 + i) >> 1] = pack_bf16x2(e0, e1);
+          }
+        l = l * alpha + (l0 + l1);
+        if (j > 0) {
+          // P V of the previous block has finished reading P and writing O.
+          if (!mbar_wait(o_done, static_cast<uint32_t>(g - 1) & 1u, p.status, 61, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (__any_sync(0xFFFFFFFFu, m_use != m)) {
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t o[32];
+              const uint32_t ta = tmem + lane_base + C::kOCol + static_cast<uint32_t>(c * 32);
+              tmem_ld_32x32b_x32(ta, o);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st_32x32b_x32(ta, o);
+            }
+            tmem_st_wait();
+          }
+        }
+        m = m_use;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          uint8_t* dst = sP + (k >> 3) * (kBM * 128) + sw128_off(row, k & 7);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(dst)), "r"(pk[4 * k]),
+                       "r"(pk[4 * k + 1]), "r"(pk[4 * k + 2]), "r"(pk[4 * k + 3])
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+      }
+      if (!ok) break;
+      // Epilogue: O / l straight from TMEM, lse for the backward pass.
+      if (!mbar_wait(o_done, static_cast<uint32_t>(g - 1) & 1u, p.status, 62, abort_flag)) break;
+      tc_fence_after();
+      const int q = qt * kBM + row;
+      const float inv_l = 1.0f / l;
+      uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) +
+                      (static_cast<long long>(b) * p.S + q) * p.ldo * 2 + static_cast<long long>(h) * D * 2;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + C::kOCol + static_cast<uint32_t>(c * 32), o);
+        tmem_ld_wait();
+        if (q < p.S) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[8 * k + 0]) * inv_l, __uint_as_float(o[8 * k + 1]) * inv_l);
+            v.y = pack_bf16x2(__uint_as_float(o[8 * k + 2]) * inv_l, __uint_as_float(o[8 * k + 3]) * inv_l);
+            v.z = pack_bf16x2(__uint_as_float(o[8 * k + 4]) * inv_l, __uint_as_float(o[8 * k + 5]) * inv_l);
+            v.w = pack_bf16x2(__uint_as_float(o[8 * k + 6]) * inv_l, __uint_as_float(o[8 * k + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(orow + c * 64 + k * 16) = v;
+          }
+        }
+      }
+      if (q < p.S) p.lse[(static_cast<long long>(b) * p.H + h) * p.S + q] = (m + lg2(l)) * 0.6931471805599453f;
+      tc_fence_before();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+}  // namespace attn_tc
+}  // namespace md
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_attn = nullptr;
+
+bool get_encoder() {
+  if (g_encode_attn != nullptr) return true;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || fn == nullptr)
+    return false;
+  g_encode_attn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return true;
+}
+
+// [B, S, cols] view of a [B*S, ld] bf16 matrix; box {64 cols, 128 rows, 1}, 128B swizzle.
+bool make_map_bsc(CUtensorMap* map, const void* ptr, int B, int S, long long cols, long long ld) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(ld) * 2 * S};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode_attn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int g_sms = 0;
+
+template <int D>
+int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, float* lse, int B, int H, int S,
+                  float scale, void* status, cudaStream_t st) {
+  using C = md::attn_tc::FwdCfg<D>;
+  if (!get_encoder()) return -3;
+  CUtensorMap tm;
+  if (!make_map_bsc(&tm, qkv, B, S, 3LL * H * D, ldq)) return -4;
+  if (g_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  md::attn_tc::FwdParams p;
+  p.out = out;
+  p.ldo = ldo;
+  p.lse = lse;
+  p.B = B;
+  p.H = H;
+  p.S = S;
+  p.n_qt = (S + md::attn_tc::kBM - 1) / md::attn_tc::kBM;
+  p.items = p.n_qt * B * H;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.status = reinterpret_cast<md::Status*>(status);
+  auto k = md::attn_tc::fwd_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const int grid = p.items < g_sms ? p.items : g_sms;
+  k<<<grid, md::attn_tc::kThreads, C::kSmemBytes, st>>>(tm, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+extern "C" {
+
+// tcgen05 causal attention forward; same layouts as md_attn_fwd (attention.cu).
+// head_dim 64 or 128; status: md::Status word the kernel reports a timed-out
+// wait into (may be null).
+int md_attn_fwd_tc(const void* qkv, long long ldq, void* out, long long ldo, float* lse, int B, int H, int S, int D,
+                   float scale, void* status, cudaStream_t st) {
+  if (B <= 0 || H <= 0 || S <= 0 || (reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
+      (ldq % 8) || (ldo % 8))
+    return -1;
+  switch (D) {
+    case 64: return fwd_tc_launch<64>(qkv, ldq, out, ldo, lse, B, H, S, scale, status, st);
+    case 128: return fwd_tc_launch<128>(qkv, ldq, out, ldo, lse, B, H, S, scale, status, st);
+    default: return -2;
+  }
+}
+
+}  // extern "C"

@@ -2,13 +2,15 @@
 
 Each function validates shapes, allocates outputs with PyTorch's caching
 allocator and launches on the current stream.  Kernels: LayerNorm
-(csrc/layernorm.cu), flash attention (csrc/attention.cu), embedding and
+(csrc/layernorm.cu), flash attention (csrc/attention_sm100.cu on the tcgen05
+tensor cores for head_dim 64/128, csrc/attention.cu otherwise), embedding and
 column sums (csrc/embedding.cu), cross-entropy pieces (csrc/cross_entropy.cu).
 """
 
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -21,6 +23,7 @@ _SIGS = {
     "md_ln_bwd_grid": "i:ii",
     "md_ln_reduce": "i:piiippppip",
     "md_attn_fwd": "i:plplpiiiifp",
+    "md_attn_fwd_tc": "i:plplpiiiifpp",
     "md_attn_bwd": "i:plplplppppliiiifp",
     "md_embed_fwd": "i:pplplpliiillip",
     "md_embed_bwd_wte": "i:pplpliillp",
@@ -98,13 +101,24 @@ def layernorm_bwd(dy, x, mean, rstd, gamma, *, resid_grad=None, dgamma=None, dbe
 # ---------------------------------------------------------------------------
 
 
-def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int, D: int):
+# MINIDIST_ATTN_FWD=mma selects the warp-level mma.sync forward for every head
+# size (used by the tests to check the two kernels against each other).
+_ATTN_FWD = os.environ.get("MINIDIST_ATTN_FWD", "tc")
+
+
+def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int, D: int, impl: str | None = None):
     """Causal attention on the per-head interleaved ``qkv [B*S, 3*H*D]``; returns ``(out [B*S, H*D], lse)``."""
     out = empty_padded(B * S, H * D, device=qkv.device)
     lse = torch.empty(B, H, S, dtype=torch.float32, device=qkv.device)
-    rc = nat.lib().md_attn_fwd(qkv.data_ptr(), _ld(qkv), out.data_ptr(), _ld(out), lse.data_ptr(), B, H, S, D,
-                               1.0 / math.sqrt(D), _s())
-    nat.check(rc, f"md_attn_fwd(D={D})")
+    impl = impl or _ATTN_FWD
+    if impl == "tc" and D in (64, 128):
+        rc = nat.lib().md_attn_fwd_tc(qkv.data_ptr(), _ld(qkv), out.data_ptr(), _ld(out), lse.data_ptr(), B, H, S,
+                                      D, 1.0 / math.sqrt(D), nat.status_ptr(qkv.device), _s())
+        nat.check(rc, f"md_attn_fwd_tc(D={D})")
+    else:
+        rc = nat.lib().md_attn_fwd(qkv.data_ptr(), _ld(qkv), out.data_ptr(), _ld(out), lse.data_ptr(), B, H, S, D,
+                                   1.0 / math.sqrt(D), _s())
+        nat.check(rc, f"md_attn_fwd(D={D})")
     return out, lse
 
 

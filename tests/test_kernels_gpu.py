@@ -57,11 +57,13 @@ def _attn_ref(qkv, B, S, H, D):
     return y.transpose(1, 2).reshape(B * S, H * D)
 
 
-@pytest.mark.parametrize("B,S,H,D", [(2, 256, 3, 64), (1, 200, 2, 64), (1, 192, 2, 80), (2, 128, 2, 128), (1, 1024, 4, 64)])
-def test_attention(B, S, H, D):
+@pytest.mark.parametrize("impl", ["tc", "mma"])
+@pytest.mark.parametrize("B,S,H,D", [(2, 256, 3, 64), (1, 200, 2, 64), (1, 192, 2, 80), (2, 128, 2, 128),
+                                     (1, 1024, 4, 64), (2, 333, 2, 128)])
+def test_attention(B, S, H, D, impl):
     torch.manual_seed(1)
     qkv = torch.randn(B * S, 3 * H * D, device="cuda").bfloat16()
-    y, lse = K.attention_fwd(qkv, B, S, H, D)
+    y, lse = K.attention_fwd(qkv, B, S, H, D, impl=impl)
     qf = qkv.float().requires_grad_(True)
     ref = _attn_ref(qf, B, S, H, D)
     nat.check_status()
@@ -76,6 +78,21 @@ def test_attention(B, S, H, D):
     dqkv = K.attention_bwd(qkv, y, dy, lse, B, S, H, D)
     torch.cuda.synchronize()
     assert _rel(dqkv, qf.grad) < 3e-2
+
+
+def test_attention_fwd_tc_many_tiles():
+    """Persistent tcgen05 forward with several work items per CTA, padded row stride, large logits."""
+    torch.manual_seed(3)
+    B, S, H, D = 4, 1024, 12, 64  # 384 work items over 148 CTAs
+    buf = torch.randn(B * S, 3 * H * D + 64, device="cuda").bfloat16() * 3
+    qkv = buf[:, : 3 * H * D]
+    y, lse = K.attention_fwd(qkv, B, S, H, D, impl="tc")
+    y2, lse2 = K.attention_fwd(qkv, B, S, H, D, impl="mma")
+    nat.check_status()
+    ref = _attn_ref(qkv, B, S, H, D)
+    assert _rel(y, ref) < 2e-2
+    assert _rel(y, y2) < 2e-2
+    assert _rel(lse, lse2) < 1e-3
 
 
 def test_embedding_and_colsum():
