@@ -584,4 +584,37 @@ int md_attn_bwd(const void* qkv, long long ldq, const void* out, long long ldo, 
   }
 }
 
+// Backward through the tcgen05 main kernel of attention_sm100.cu (head_dim
+// 64): same contract as md_attn_bwd, plus the status word for timed-out waits.
+int md_attn_bwd_tc_main(const void* qkv, long long ldq, const void* dout, long long lddo, const float* lse,
+                        const float* delta, float* dqacc, long long ldacc, void* dqkv, long long lddq, int B, int H,
+                        int S, int D, float scale, void* status, cudaStream_t st);
+
+int md_attn_bwd_tc(const void* qkv, long long ldq, const void* out, long long ldo, const void* dout, long long lddo,
+                   const float* lse, float* delta, float* dqacc, void* dqkv, long long lddq, int B, int H, int S,
+                   int D, float scale, void* status, cudaStream_t st) {
+  if (B <= 0 || H <= 0 || S <= 0 || !al16(qkv) || !al16(out) || !al16(dout) || !al16(dqkv) || (ldq % 8) ||
+      (ldo % 8) || (lddo % 8) || (lddq % 8))
+    return -1;
+  if (D != 64) return -2;
+  const long long rows = static_cast<long long>(B) * S;
+  cudaError_t e = cudaMemsetAsync(dqacc, 0, rows * H * D * sizeof(float), st);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const long long nd = static_cast<long long>(B) * H * S;
+  int g1 = static_cast<int>((nd + 255) / 256);
+  if (g1 > 148 * 32) g1 = 148 * 32;
+  md::attn::delta_kernel<64><<<g1, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(out), ldo,
+                                                 reinterpret_cast<const __nv_bfloat16*>(dout), lddo, delta, B, H, S);
+  int rc = md_attn_bwd_tc_main(qkv, ldq, dout, lddo, lse, delta, dqacc, static_cast<long long>(H) * D, dqkv, lddq, B,
+                               H, S, D, scale, status, st);
+  if (rc != 0) return rc;
+  const long long nq = rows * H * (64 / 2);
+  int g2 = static_cast<int>((nq + 255) / 256);
+  if (g2 > 148 * 32) g2 = 148 * 32;
+  md::attn::dq_convert_kernel<64><<<g2, 256, 0, st>>>(dqacc, static_cast<long long>(H) * 64,
+                                                      reinterpret_cast<__nv_bfloat16*>(dqkv), lddq,
+                                                      static_cast<int>(rows), H, scale);
+  return static_cast<int>(cudaGetLastError());
+}
+
 }  // extern "C"

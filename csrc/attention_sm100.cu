@@ -394,6 +394,416 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
 
+
+// ===========================================================================
+// Backward
+//
+// One work item = (key tile kt of 128 keys, batch*head); items ordered
+// longest-first (tile kt meets nqt - kt query blocks).  Per query block i:
+//   S^T  = K Q_i^T          (TMEM, 128 keys x 128 queries)
+//   dP^T = V dO_i^T         (TMEM)
+//   P^T  = exp(S^T * scale - lse_i),  dS^T = P^T (dP^T - delta_i)   [compute warps, bf16 to smem]
+//   dV  += P^T dO_i,   dK += dS^T Q_i      (TMEM accumulators for the whole item)
+//   dQ_i = dS K_j                            (TMEM, drained by the dQ warps into an
+//                                             fp32 accumulator with red.global.add)
+// Roles: warp 0 TMA, warp 1 MMA, warps 2..5 compute (thread = key row), warps
+// 6..9 dQ drain (thread = query row).  The score products of block i+1 are
+// issued before the dV/dK/dQ products of block i so the compute warps start on
+// i+1 while the tensor core finishes i.
+// ===========================================================================
+constexpr int kBwdThreads = 320;
+
+template <int D>
+struct BwdCfg {
+  static constexpr int kChunks = D / 64;
+  static constexpr int kTileBytes = 128 * D * 2;
+  static constexpr int kQStages = 2;
+  static constexpr int kPBytes = 128 * 128 * 2;
+  // K, V | (Q, dO) x stages | P^T | dS^T | lse, delta x 2 parities
+  static constexpr int kSmemData = (2 + 2 * kQStages) * kTileBytes + 2 * kPBytes + 2 * 2 * 128 * 4;
+  static constexpr int kSmemBytes = kSmemData + 1024 + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 256 + D, kColDQ = 256 + 2 * D;
+  static_assert(256 + 3 * D <= 512, "TMEM budget");
+};
+
+struct BwdParams {
+  const float* lse;    // [B, H, S] natural log
+  const float* delta;  // [B, H, S]
+  float* dqacc;        // [B*S, ldacc] fp32, zeroed
+  long long ldacc;
+  void* dqkv;          // [B*S, lddq] bf16 interleaved [H, 3, D]
+  long long lddq;
+  int B, H, S;
+  int n_t;             // 128-row tiles per sequence
+  int items;
+  float scale, scale_log2;
+  Status* status;
+};
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    bwd_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
+               const __grid_constant__ BwdParams p) {
+  using C = BwdCfg<D>;
+  constexpr int QS = C::kQStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + C::kTileBytes;
+  uint8_t* sQ = sV + C::kTileBytes;               // [QS]
+  uint8_t* sdO = sQ + QS * C::kTileBytes;         // [QS]
+  uint8_t* sP = sdO + QS * C::kTileBytes;
+  uint8_t* sdS = sP + C::kPBytes;
+  float* sL = reinterpret_cast<float*>(sdS + C::kPBytes);  // [2][128] lse (log2 units)
+  float* sDel = sL + 2 * 128;                               // [2][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 2 * 128);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* kv_empty = bars + 1;
+  uint64_t* qd_full = bars + 2;    // [2]
+  uint64_t* qd_empty = bars + 4;   // [2]
+  uint64_t* sd_full = bars + 6;
+  uint64_t* sd_free = bars + 7;
+  uint64_t* pds_full = bars + 8;
+  uint64_t* mm_done = bars + 9;
+  uint64_t* dq_full = bars + 10;
+  uint64_t* dq_free = bars + 11;
+  uint64_t* dkv_free = bars + 12;
+  uint64_t* drain = bars + 13;
+  uint64_t* stage_bar = bars + 14;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int bhc = p.B * p.H;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
+    for (int i = 0; i < QS; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
+    mbar_init(sd_full, 1);
+    mbar_init(sd_free, 4);
+    mbar_init(pds_full, 4);
+    mbar_init(mm_done, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(dkv_free, 4);
+    mbar_init(drain, 1);
+    mbar_init(&stage_bar[0], 128);
+    mbar_init(&stage_bar[1], 128);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQKV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA producer
+    int kv_armed = -1;
+    int q_armed[2] = {-1, -1};
+    int g = 0, t = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
+      const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
+      const uint32_t tph = static_cast<uint32_t>(t) & 1u;
+      if (!mbar_wait(kv_empty, tph ^ 1u, p.status, 70, abort_flag)) break;
+      mbar_arrive_expect_tx(kv_full, 2 * C::kTileBytes);
+      kv_armed = static_cast<int>(tph);
+      const int col0 = h * 3 * D;
+#pragma unroll
+      for (int c = 0; c < C::kChunks; ++c) {
+        tma_load_3d(&tmQKV, kv_full, sK + c * 16384, col0 + D + c * 64, kt * 128, b);
+        tma_load_3d(&tmQKV, kv_full, sV + c * 16384, col0 + 2 * D + c * 64, kt * 128, b);
+      }
+      for (int i = kt; i < p.n_t; ++i, ++g) {
+        const int st = g % QS;
+        const uint32_t ph = static_cast<uint32_t>(g / QS) & 1u;
+        if (!mbar_wait(&qd_empty[st], ph ^ 1u, p.status, 71, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&qd_full[st], 2 * C::kTileBytes);
+        q_armed[st] = static_cast<int>(ph);
+#pragma unroll
+        for (int c = 0; c < C::kChunks; ++c) {
+          tma_load_3d(&tmQKV, &qd_full[st], sQ + st * C::kTileBytes + c * 16384, col0 + c * 64, i * 128, b);
+          tma_load_3d(&tmDO, &qd_full[st], sdO + st * C::kTileBytes + c * 16384, h * D + c * 64, i * 128, b);
+        }
+      }
+    }
+    if (kv_armed >= 0) mbar_wait(kv_full, static_cast<uint32_t>(kv_armed), p.status, 72, nullptr);
+    for (int i = 0; i < QS; ++i)
+      if (q_armed[i] >= 0) mbar_wait(&qd_full[i], static_cast<uint32_t>(q_armed[i]), p.status, 73, nullptr);
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idS = idesc_bf16_f32(128, 128, false, false);   // S^T, dP^T
+    constexpr uint32_t idKV = idesc_bf16_f32(128, D, false, true);     // dV, dK: B MN-major
+    constexpr uint32_t idQ = idesc_bf16_f32(128, D, true, true);       // dQ: A (dS) and B (K) MN-major
+    const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP), adS = smem_u32(sdS);
+    int g = 0, t = 0;
+    bool ok = true;
+    // Score products for block g (stage st).
+    auto issue_scores = [&](int gg) -> bool {
+      const int st = gg % QS;
+      if (!mbar_wait(&qd_full[st], static_cast<uint32_t>(gg / QS) & 1u, p.status, 80, abort_flag) ||
+          !mbar_wait(sd_free, (static_cast<uint32_t>(gg) & 1u) ^ 1u, p.status, 81, abort_flag))
+        return false;
+      tc_fence_after();
+      const uint32_t aQ = smem_u32(sQ + st * C::kTileBytes), adO = smem_u32(sdO + st * C::kTileBytes);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+        umma_bf16_ss(tmem + C::kColS, sdesc_sw128(aK + off, 16, 1024), sdesc_sw128(aQ + off, 16, 1024), idS,
+                     kk > 0 ? 1u : 0u);
+        umma_bf16_ss(tmem + C::kColDP, sdesc_sw128(aV + off, 16, 1024), sdesc_sw128(adO + off, 16, 1024), idS,
+                     kk > 0 ? 1u : 0u);
+      }
+      umma_commit(sd_full);
+      return true;
+    };
+    int next_scored = -1;  // last global block whose score products are issued
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
+      const int kt = w / bhc;
+      const int n = p.n_t - kt;
+      if (!mbar_wait(kv_full, static_cast<uint32_t>(t) & 1u, p.status, 82, abort_flag)) break;
+      if (next_scored < g) {
+        if (!issue_scores(g)) break;
+        next_scored = g;
+      }
+      for (int u = 0; u < n; ++u, ++g) {
+        const int st = g % QS;
+        if (!mbar_wait(pds_full, static_cast<uint32_t>(g) & 1u, p.status, 83, abort_flag)) {
+          ok = false;
+          break;
+        }
+        // Queue the next block's scores first (same item) so the compute warps
+        // can start on it while dV/dK/dQ of this block run.
+        if (u + 1 < n) {
+          if (!issue_scores(g + 1)) {
+            ok = false;
+            break;
+          }
+          next_scored = g + 1;
+        }
+        if (u == 0 && !mbar_wait(dkv_free, (static_cast<uint32_t>(t) & 1u) ^ 1u, p.status, 84, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t aQ = smem_u32(sQ + st * C::kTileBytes), adO = smem_u32(sdO + st * C::kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t offA = (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t acc = (u > 0 || kk > 0) ? 1u : 0u;
+          umma_bf16_ss(tmem + C::kColDV, sdesc_sw128(aP + offA, 16, 1024), sdesc_sw128(adO + kk * 2048, 16384, 1024),
+                       idKV, acc);
+          umma_bf16_ss(tmem + C::kColDK, sdesc_sw128(adS + offA, 16, 1024), sdesc_sw128(aQ + kk * 2048, 16384, 1024),
+                       idKV, acc);
+        }
+        umma_commit(&qd_empty[st]);
+        if (!mbar_wait(dq_free, (static_cast<uint32_t>(g) & 1u) ^ 1u, p.status, 85, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16_ss(tmem + C::kColDQ, sdesc_sw128(adS + kk * 2048, 16384, 1024),
+                       sdesc_sw128(aK + kk * 2048, 16384, 1024), idQ, kk > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+        umma_commit(mm_done);
+      }
+      if (!ok) break;
+      umma_commit(kv_empty);
+    }
+    umma_commit(drain);
+    mbar_wait(drain, 0, p.status, 86, nullptr);
+  } else if (warp >= 2 && warp < 6) {
+    // ------------------------------------------------------------ compute (thread = key row)
+    const int quarter = warp & 3;
+    const int krow = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int ct = threadIdx.x - 64;  // 0..127
+    int g = 0, t = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
+      const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
+      const int n = p.n_t - kt;
+      const long long lbase = static_cast<long long>(bh) * p.S;
+      for (int u = 0; u < n; ++u, ++g) {
+        const int i = kt + u;
+        // Stage lse (log2 units) and delta of this query block.
+        {
+          // Every compute thread writes one entry, then all 128 meet on an
+          // mbarrier (bounded wait).  Buffer g&1 is rewritten at block g+2,
+          // after every thread has passed block g+1's meeting point.
+          const int q = i * 128 + ct;
+          float* L = sL + (g & 1) * 128;
+          float* Dl = sDel + (g & 1) * 128;
+          L[ct] = q < p.S ? p.lse[lbase + q] * 1.4426950408889634f : INFINITY;
+          Dl[ct] = q < p.S ? p.delta[lbase + q] : 0.f;
+          mbar_arrive(&stage_bar[g & 1]);
+          if (!mbar_wait(&stage_bar[g & 1], static_cast<uint32_t>(g >> 1) & 1u, p.status, 89, abort_flag)) {
+            ok = false;
+            break;
+          }
+        }
+        const float* L = sL + (g & 1) * 128;
+        const float* Dl = sDel + (g & 1) * 128;
+        if (!mbar_wait(sd_full, static_cast<uint32_t>(g) & 1u, p.status, 90, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          uint32_t s0[32], s1[32], d0[32], d1[32];
+          tmem_ld_32x32b_x32(tmem + lane_base + C::kColS + half * 64, s0);
+          tmem_ld_32x32b_x32(tmem + lane_base + C::kColS + half * 64 + 32, s1);
+          tmem_ld_32x32b_x32(tmem + lane_base + C::kColDP + half * 64, d0);
+          tmem_ld_32x32b_x32(tmem + lane_base + C::kColDP + half * 64 + 32, d1);
+          tmem_ld_wait();
+          if (half == 1) {
+            // S^T and dP^T fully read: the next block's score products may overwrite them.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sd_free);
+          }
+          uint32_t pp[32], dd[32];
+#pragma unroll
+          for (int e = 0; e < 64; e += 2) {
+            const int qc = half * 64 + e;
+            const uint32_t sa = e < 32 ? s0[e] : s1[e - 32], sb = e < 32 ? s0[e + 1] : s1[e - 31];
+            const uint32_t da = e < 32 ? d0[e] : d1[e - 32], db = e < 32 ? d0[e + 1] : d1[e - 31];
+            float p0 = ex2(fmaf(__uint_as_float(sa), p.scale_log2, -L[qc]));
+            float p1 = ex2(fmaf(__uint_as_float(sb), p.scale_log2, -L[qc + 1]));
+            if (u == 0) {  // diagonal block: query < key is masked
+              if (qc < krow) p0 = 0.f;
+              if (qc + 1 < krow) p1 = 0.f;
+            }
+            const float g0 = p0 * (__uint_as_float(da) - Dl[qc]);
+            const float g1 = p1 * (__uint_as_float(db) - Dl[qc + 1]);
+            pp[e >> 1] = pack_bf16x2(p0, p1);
+            dd[e >> 1] = pack_bf16x2(g0, g1);
+          }
+          if (half == 0 && g > 0) {
+            // dV/dK/dQ of the previous block have finished reading P^T / dS^T.
+            if (!mbar_wait(mm_done, static_cast<uint32_t>(g - 1) & 1u, p.status, 91, abort_flag)) {
+              ok = false;
+              break;
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t off = half * 16384 + sw128_off(krow, k);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(sP + off)), "r"(pp[4 * k]),
+                         "r"(pp[4 * k + 1]), "r"(pp[4 * k + 2]), "r"(pp[4 * k + 3])
+                         : "memory");
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(sdS + off)), "r"(dd[4 * k]),
+                         "r"(dd[4 * k + 1]), "r"(dd[4 * k + 2]), "r"(dd[4 * k + 3])
+                         : "memory");
+          }
+        }
+        if (!ok) break;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pds_full);
+      }
+      if (!ok) break;
+      // dK (scaled) and dV of this key tile.
+      if (!mbar_wait(mm_done, static_cast<uint32_t>(g - 1) & 1u, p.status, 92, abort_flag)) break;
+      tc_fence_after();
+      const int key = kt * 128 + krow;
+      uint8_t* row = reinterpret_cast<uint8_t*>(p.dqkv) +
+                     ((static_cast<long long>(b) * p.S + key) * p.lddq + static_cast<long long>(h) * 3 * D) * 2;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const float sc = which == 0 ? p.scale : 1.f;
+        const uint32_t col = which == 0 ? C::kColDK : C::kColDV;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tmem + lane_base + col + c * 32, o);
+          tmem_ld_wait();
+          if (key < p.S) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              uint4 v;
+              v.x = pack_bf16x2(__uint_as_float(o[8 * k + 0]) * sc, __uint_as_float(o[8 * k + 1]) * sc);
+              v.y = pack_bf16x2(__uint_as_float(o[8 * k + 2]) * sc, __uint_as_float(o[8 * k + 3]) * sc);
+              v.z = pack_bf16x2(__uint_as_float(o[8 * k + 4]) * sc, __uint_as_float(o[8 * k + 5]) * sc);
+              v.w = pack_bf16x2(__uint_as_float(o[8 * k + 6]) * sc, __uint_as_float(o[8 * k + 7]) * sc);
+              *reinterpret_cast<uint4*>(row + (which + 1) * D * 2 + c * 64 + k * 16) = v;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dkv_free);
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------ dQ drain (thread = query row)
+    const int quarter = warp & 3;
+    const int qrow = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    int g = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x) {
+      const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
+      for (int i = kt; i < p.n_t; ++i, ++g) {
+        if (!mbar_wait(dq_full, static_cast<uint32_t>(g) & 1u, p.status, 95, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int q = i * 128 + qrow;
+        float* dst = p.dqacc + (static_cast<long long>(b) * p.S + q) * p.ldacc + static_cast<long long>(h) * D;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tmem + lane_base + C::kColDQ + c * 32, o);
+          tmem_ld_wait();
+          if (c == D / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(dq_free);
+          }
+          if (q < p.S) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              red_add_v4(dst + c * 32 + 4 * k, __uint_as_float(o[4 * k]), __uint_as_float(o[4 * k + 1]),
+                         __uint_as_float(o[4 * k + 2]), __uint_as_float(o[4 * k + 3]));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+}
+
 }  // namespace attn_tc
 }  // namespace md
 
@@ -459,9 +869,58 @@ int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, floa
   return static_cast<int>(cudaGetLastError());
 }
 
+
+template <int D>
+int bwd_tc_launch(const void* qkv, long long ldq, const void* dout, long long lddo, const float* lse,
+                  const float* delta, float* dqacc, long long ldacc, void* dqkv, long long lddq, int B, int H, int S,
+                  float scale, void* status, cudaStream_t st) {
+  using C = md::attn_tc::BwdCfg<D>;
+  if (!get_encoder()) return -3;
+  CUtensorMap tq, tdo;
+  if (!make_map_bsc(&tq, qkv, B, S, 3LL * H * D, ldq) || !make_map_bsc(&tdo, dout, B, S, 1LL * H * D, lddo))
+    return -4;
+  if (g_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  md::attn_tc::BwdParams p;
+  p.lse = lse;
+  p.delta = delta;
+  p.dqacc = dqacc;
+  p.ldacc = ldacc;
+  p.dqkv = dqkv;
+  p.lddq = lddq;
+  p.B = B;
+  p.H = H;
+  p.S = S;
+  p.n_t = (S + 127) / 128;
+  p.items = p.n_t * B * H;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.status = reinterpret_cast<md::Status*>(status);
+  auto k = md::attn_tc::bwd_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const int grid = p.items < g_sms ? p.items : g_sms;
+  k<<<grid, md::attn_tc::kBwdThreads, C::kSmemBytes, st>>>(tq, tdo, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
 }  // namespace
 
 extern "C" {
+
+// Main pass of the tcgen05 attention backward (head_dim 64): dK, dV into dqkv
+// and dQ (unscaled) added into the zeroed fp32 accumulator dqacc [B*S, ldacc].
+// delta [B, H, S] = rowsum(dO * O) must be ready.  attention.cu's
+// md_attn_bwd_tc wraps this with the delta and dQ conversion steps.
+int md_attn_bwd_tc_main(const void* qkv, long long ldq, const void* dout, long long lddo, const float* lse,
+                        const float* delta, float* dqacc, long long ldacc, void* dqkv, long long lddq, int B, int H,
+                        int S, int D, float scale, void* status, cudaStream_t st) {
+  if (D != 64) return -2;
+  return bwd_tc_launch<64>(qkv, ldq, dout, lddo, lse, delta, dqacc, ldacc, dqkv, lddq, B, H, S, scale, status, st);
+}
 
 // tcgen05 causal attention forward; same layouts as md_attn_fwd (attention.cu).
 // head_dim 64 or 128; status: md::Status word the kernel reports a timed-out

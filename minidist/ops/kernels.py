@@ -24,6 +24,7 @@ _SIGS = {
     "md_ln_reduce": "i:piiippppip",
     "md_attn_fwd": "i:plplpiiiifp",
     "md_attn_fwd_tc": "i:plplpiiiifpp",
+    "md_attn_bwd_tc": "i:plplplppppliiiifpp",
     "md_attn_bwd": "i:plplplppppliiiifp",
     "md_embed_fwd": "i:pplplpliiillip",
     "md_embed_bwd_wte": "i:pplpliillp",
@@ -101,9 +102,10 @@ def layernorm_bwd(dy, x, mean, rstd, gamma, *, resid_grad=None, dgamma=None, dbe
 # ---------------------------------------------------------------------------
 
 
-# MINIDIST_ATTN_FWD=mma selects the warp-level mma.sync forward for every head
-# size (used by the tests to check the two kernels against each other).
+# MINIDIST_ATTN_FWD=mma / MINIDIST_ATTN_BWD=mma select the warp-level mma.sync
+# kernels for every head size (the tests check the two against each other).
 _ATTN_FWD = os.environ.get("MINIDIST_ATTN_FWD", "tc")
+_ATTN_BWD = os.environ.get("MINIDIST_ATTN_BWD", "tc")
 
 
 def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int, D: int, impl: str | None = None):
@@ -122,16 +124,24 @@ def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int, D: int, impl: str |
     return out, lse
 
 
-def attention_bwd(qkv, out, dout, lse, B: int, S: int, H: int, D: int, dqkv: torch.Tensor | None = None):
+def attention_bwd(qkv, out, dout, lse, B: int, S: int, H: int, D: int, dqkv: torch.Tensor | None = None,
+                  impl: str | None = None):
     """Gradients w.r.t. ``qkv`` in the same interleaved layout."""
     if dqkv is None:
         dqkv = empty_padded(B * S, 3 * H * D, device=qkv.device)
     delta = torch.empty(B * H * S, dtype=torch.float32, device=qkv.device)
     dqacc = torch.empty(B * S, H * D, dtype=torch.float32, device=qkv.device)
-    rc = nat.lib().md_attn_bwd(qkv.data_ptr(), _ld(qkv), out.data_ptr(), _ld(out), dout.data_ptr(), _ld(dout),
-                               lse.data_ptr(), delta.data_ptr(), dqacc.data_ptr(), dqkv.data_ptr(), _ld(dqkv),
-                               B, H, S, D, 1.0 / math.sqrt(D), _s())
-    nat.check(rc, f"md_attn_bwd(D={D})")
+    impl = impl or _ATTN_BWD
+    if impl == "tc" and D == 64:
+        rc = nat.lib().md_attn_bwd_tc(qkv.data_ptr(), _ld(qkv), out.data_ptr(), _ld(out), dout.data_ptr(), _ld(dout),
+                                      lse.data_ptr(), delta.data_ptr(), dqacc.data_ptr(), dqkv.data_ptr(), _ld(dqkv),
+                                      B, H, S, D, 1.0 / math.sqrt(D), nat.status_ptr(qkv.device), _s())
+        nat.check(rc, f"md_attn_bwd_tc(D={D})")
+    else:
+        rc = nat.lib().md_attn_bwd(qkv.data_ptr(), _ld(qkv), out.data_ptr(), _ld(out), dout.data_ptr(), _ld(dout),
+                                   lse.data_ptr(), delta.data_ptr(), dqacc.data_ptr(), dqkv.data_ptr(), _ld(dqkv),
+                                   B, H, S, D, 1.0 / math.sqrt(D), _s())
+        nat.check(rc, f"md_attn_bwd(D={D})")
     return dqkv
 
 

@@ -75,8 +75,8 @@ def test_attention(B, S, H, D, impl):
     assert _rel(lse, torch.logsumexp(s, -1)) < 1e-3
     dy = torch.randn(B * S, H * D, device="cuda").bfloat16()
     ref.backward(dy.float())
-    dqkv = K.attention_bwd(qkv, y, dy, lse, B, S, H, D)
-    torch.cuda.synchronize()
+    dqkv = K.attention_bwd(qkv, y, dy, lse, B, S, H, D, impl=impl)
+    nat.check_status()
     assert _rel(dqkv, qf.grad) < 3e-2
 
 
@@ -93,6 +93,11 @@ def test_attention_fwd_tc_many_tiles():
     assert _rel(y, ref) < 2e-2
     assert _rel(y, y2) < 2e-2
     assert _rel(lse, lse2) < 1e-3
+    dy = torch.randn(B * S, H * D, device="cuda").bfloat16()
+    g1 = K.attention_bwd(qkv, y, dy, lse, B, S, H, D, impl="tc")
+    g2 = K.attention_bwd(qkv, y, dy, lse, B, S, H, D, impl="mma")
+    nat.check_status()
+    assert _rel(g1, g2) < 2e-2
 
 
 def test_embedding_and_colsum():
