@@ -8,15 +8,17 @@
 // the output is [B*S, ldo] with head h at columns h*D; lse [B, H, S] holds the
 // natural-log log-sum-exp of every query row for the backward pass.
 //
-// Persistent kernel, one CTA per SM, warp-specialised:
+// Persistent kernel (two CTAs per SM for head_dim 64, one for 128), warp-specialised:
 //   warp 0      TMA producer: Q tile (128 queries) and, per key block, K and V
 //               tiles (128 keys) through a 3-D tensor map [B, S, 3*H*D] whose
 //               sequence-end rows read as zero.
-//   warp 1      MMA issuer (one thread): S = Q K^T into one of two TMEM score
-//               buffers (128 x 128 fp32), then O += P V into a TMEM accumulator
-//               (128 x D fp32).  The score product of block g+1 is queued
-//               before the P V product of block g, so the tensor core computes
-//               scores while the softmax warps exponentiate.
+//   warp 1      MMA issuer (one thread): S = Q K^T into a TMEM score buffer
+//               (128 x 128 fp32; two buffers for head_dim 128), then O += P V
+//               into a TMEM accumulator (128 x D fp32).  The score product of
+//               block g+1 is queued before the P V product of block g (the
+//               softmax warps release the score buffer as soon as it is in
+//               registers), so the tensor core computes scores while the
+//               softmax warps exponentiate.
 //   warps 2..5  softmax: thread t owns query row t (TMEM lane t, 32x32b loads),
 //               so row max and row sum need no shuffles.  Scores come out of
 //               TMEM, exp2 on the MUFU pipe, P goes to shared memory as bf16 in
@@ -34,6 +36,7 @@
 // status, lets the other roles see the abort flag, drains its bulk copies and
 // MMAs, frees TMEM and exits.
 #include <cudaTypedefs.h>
+#include <stdlib.h>
 
 #include "md_sm100.cuh"
 
@@ -45,17 +48,25 @@ constexpr int kBN = 128;   // keys per block
 constexpr float kRescaleLog2 = 8.0f;
 constexpr int kThreads = 192;
 
+// head_dim 64 runs two CTAs per SM (112 KB shared memory, 256 TMEM columns
+// each) so two independent softmax pipelines share every SM sub-partition and
+// hide each other's latencies; head_dim 128 needs one SM per CTA.
 template <int D>
 struct FwdCfg {
   static constexpr int kChunks = D / 64;               // 64-column (128 B) swizzle atoms along head_dim
   static constexpr int kTileBytes = kBM * D * 2;       // one Q/K/V tile
-  static constexpr int kQBufs = D == 64 ? 2 : 1;
-  static constexpr int kKvStages = D == 64 ? 3 : 2;
+  static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
+  static constexpr int kQBufs = 1;
+  static constexpr int kKvStages = 2;
+  static constexpr int kSBufs = D == 64 ? 1 : 2;       // TMEM score buffers
   static constexpr int kPBytes = kBM * kBN * 2;        // P tile (bf16)
   static constexpr int kSmemData = (kQBufs + 2 * kKvStages) * kTileBytes + kPBytes;
-  static constexpr int kSmemBytes = kSmemData + 1024 /*barriers*/ + 1024 /*alignment slack*/;
-  static constexpr uint32_t kTmemCols = 512;           // S0 [0,128) S1 [128,256) O [256, 256+D)
-  static constexpr uint32_t kOCol = 256;
+  // Two CTAs per SM leave no room for alignment slack: the dynamic window is
+  // then required to start 1024-byte aligned (checked in the kernel).
+  static constexpr bool kAlignSlack = kCtasPerSm == 1;
+  static constexpr int kSmemBytes = kSmemData + 256 /*barriers*/ + (kAlignSlack ? 1024 : 0);
+  static constexpr uint32_t kTmemCols = D == 64 ? 256 : 512;  // S buffers, then O
+  static constexpr uint32_t kOCol = kSBufs * 128;
 };
 
 struct FwdParams {
@@ -96,13 +107,18 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
 
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
     fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ FwdParams p) {
   using C = FwdCfg<D>;
   constexpr int KST = C::kKvStages;
   constexpr int QB = C::kQBufs;
-  extern __shared__ uint8_t smem_raw[];
+  constexpr int SB = C::kSBufs;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if (!C::kAlignSlack && smem != smem_raw) {  // uniform across the CTA
+    if (threadIdx.x == 0) report(p.status, kBadArgument, 39, static_cast<uint32_t>(smem_u32(smem_raw)));
+    return;
+  }
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + QB * C::kTileBytes;
   uint8_t* sV = sK + KST * C::kTileBytes;
@@ -240,20 +256,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t qa = smem_u32(sQ + qb * C::kTileBytes);
       for (int j = 0; j <= qt; ++j, ++g) {
         const int st = g % KST;
+        const int sb = g % SB;
         if (!mbar_wait(&k_full[st], static_cast<uint32_t>(g / KST) & 1u, p.status, 51, abort_flag) ||
-            !mbar_wait(&s_free[g & 1], (static_cast<uint32_t>(g >> 1) & 1u) ^ 1u, p.status, 54, abort_flag)) {
+            !mbar_wait(&s_free[sb], (static_cast<uint32_t>(g / SB) & 1u) ^ 1u, p.status, 54, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t ka = smem_u32(sK + st * C::kTileBytes);
-        const uint32_t sd = tmem + static_cast<uint32_t>((g & 1) * kBN);
+        const uint32_t sd = tmem + static_cast<uint32_t>(sb * kBN);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
           umma_bf16_ss(sd, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[g & 1]);
+        umma_commit(&s_full[sb]);
         umma_commit(&k_empty[st]);
         if (j == qt) umma_commit(&q_empty[qb]);
         if (pend >= 0 && !issue_pv(pend, pend_first)) {
@@ -281,18 +298,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m = -INFINITY, l = 0.f;
       bool ok = true;
       for (int j = 0; j <= qt; ++j, ++g) {
-        if (!mbar_wait(&s_full[g & 1], static_cast<uint32_t>(g >> 1) & 1u, p.status, 60, abort_flag)) {
+        const int sb = g % SB;
+        if (!mbar_wait(&s_full[sb], static_cast<uint32_t>(g / SB) & 1u, p.status, 60, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         uint32_t r[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_base + static_cast<uint32_t>((g & 1) * kBN + c * 32), r[c]);
+        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_base + static_cast<uint32_t>(sb * kBN + c * 32), r[c]);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[g & 1]);
+        if (lane == 0) mbar_arrive(&s_free[sb]);
         if (j == qt) {  // diagonal block: key > query is masked
 #pragma unroll
           for (int c = 0; c < 4; ++c)
@@ -406,12 +424,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   dV  += P^T dO_i,   dK += dS^T Q_i      (TMEM accumulators for the whole item)
 //   dQ_i = dS K_j                            (TMEM, drained by the dQ warps into an
 //                                             fp32 accumulator with red.global.add)
-// Roles: warp 0 TMA, warp 1 MMA, warps 2..5 compute (thread = key row), warps
-// 6..9 dQ drain (thread = query row).  The score products of block i+1 are
-// issued before the dV/dK/dQ products of block i so the compute warps start on
-// i+1 while the tensor core finishes i.
+// Roles: warp 0 TMA, warp 1 MMA, warps 2..9 compute (thread = key row; warps
+// 2..5 take query columns 0..63, warps 6..9 columns 64..127, so two warps
+// share every SM sub-partition), warps 10..13 dQ drain (thread = query row).
+// P^T / dS^T are double-buffered in shared memory: the compute warps fill
+// buffer (i & 1) while the tensor core still reads the other one for the
+// dV/dK/dQ products of the previous block.
 // ===========================================================================
-constexpr int kBwdThreads = 320;
+constexpr int kBwdThreads = 448;
+constexpr int kBwdCompute = 8;  // compute warps
 
 template <int D>
 struct BwdCfg {
@@ -419,12 +440,15 @@ struct BwdCfg {
   static constexpr int kTileBytes = 128 * D * 2;
   static constexpr int kQStages = 2;
   static constexpr int kPBytes = 128 * 128 * 2;
-  // K, V | (Q, dO) x stages | P^T | dS^T | lse, delta x 2 parities
-  static constexpr int kSmemData = (2 + 2 * kQStages) * kTileBytes + 2 * kPBytes + 2 * 2 * 128 * 4;
-  static constexpr int kSmemBytes = kSmemData + 1024 + 1024;
+  // K, V | (Q, dO) x stages | (P^T, dS^T) x 2 | lse, delta x 2 parities
+  static constexpr int kSmemData = (2 + 2 * kQStages) * kTileBytes + 4 * kPBytes + 2 * 2 * 128 * 4;
+  // No alignment slack fits: the dynamic window must start 1024-byte aligned
+  // (checked in the kernel).
+  static constexpr int kSmemBytes = kSmemData + 256;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 256 + D, kColDQ = 256 + 2 * D;
   static_assert(256 + 3 * D <= 512, "TMEM budget");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 struct BwdParams {
@@ -438,6 +462,7 @@ struct BwdParams {
   int n_t;             // 128-row tiles per sequence
   int items;
   float scale, scale_log2;
+  int flags;           // bit 0: skip the dQ reductions (timing experiments only; dQ is then wrong)
   Status* status;
 };
 
@@ -452,16 +477,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                const __grid_constant__ BwdParams p) {
   using C = BwdCfg<D>;
   constexpr int QS = C::kQStages;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sK = smem;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if ((smem_u32(smem_raw) & 1023u) != 0u) {  // uniform across the CTA
+    if (threadIdx.x == 0) report(p.status, kBadArgument, 69, smem_u32(smem_raw));
+    return;
+  }
+  uint8_t* sK = smem_raw;
   uint8_t* sV = sK + C::kTileBytes;
   uint8_t* sQ = sV + C::kTileBytes;               // [QS]
   uint8_t* sdO = sQ + QS * C::kTileBytes;         // [QS]
-  uint8_t* sP = sdO + QS * C::kTileBytes;
-  uint8_t* sdS = sP + C::kPBytes;
-  float* sL = reinterpret_cast<float*>(sdS + C::kPBytes);  // [2][128] lse (log2 units)
-  float* sDel = sL + 2 * 128;                               // [2][128]
+  uint8_t* sPD = sdO + QS * C::kTileBytes;        // [2] x (P^T, dS^T)
+  float* sL = reinterpret_cast<float*>(sPD + 4 * C::kPBytes);  // [2][128] lse (log2 units)
+  float* sDel = sL + 2 * 128;                                   // [2][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 2 * 128);
   uint64_t* kv_full = bars + 0;
   uint64_t* kv_empty = bars + 1;
@@ -470,14 +497,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* sd_full = bars + 6;
   uint64_t* sd_free = bars + 7;
   uint64_t* pds_full = bars + 8;
-  uint64_t* mm_done = bars + 9;
-  uint64_t* dq_full = bars + 10;
-  uint64_t* dq_free = bars + 11;
-  uint64_t* dkv_free = bars + 12;
-  uint64_t* drain = bars + 13;
-  uint64_t* stage_bar = bars + 14;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
+  uint64_t* mm_done = bars + 9;    // [2] per P^T/dS^T buffer
+  uint64_t* dq_full = bars + 11;
+  uint64_t* dq_free = bars + 12;
+  uint64_t* dkv_free = bars + 13;
+  uint64_t* drain = bars + 14;
+  uint64_t* stage_bar = bars + 15;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -491,15 +518,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&qd_empty[i], 1);
     }
     mbar_init(sd_full, 1);
-    mbar_init(sd_free, 4);
-    mbar_init(pds_full, 4);
-    mbar_init(mm_done, 1);
+    mbar_init(sd_free, kBwdCompute);
+    mbar_init(pds_full, kBwdCompute);
+    mbar_init(&mm_done[0], 1);
+    mbar_init(&mm_done[1], 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 4);
-    mbar_init(dkv_free, 4);
+    mbar_init(dkv_free, kBwdCompute);
     mbar_init(drain, 1);
-    mbar_init(&stage_bar[0], 128);
-    mbar_init(&stage_bar[1], 128);
+    mbar_init(&stage_bar[0], 32 * kBwdCompute);
+    mbar_init(&stage_bar[1], 32 * kBwdCompute);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQKV);
@@ -540,7 +568,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&qd_full[st], 2 * C::kTileBytes);
-        q_armed[st] = static_cast<int>(ph);
+        if (st == 0) q_armed[0] = static_cast<int>(ph);
+        else q_armed[1] = static_cast<int>(ph);
 #pragma unroll
         for (int c = 0; c < C::kChunks; ++c) {
           tma_load_3d(&tmQKV, &qd_full[st], sQ + st * C::kTileBytes + c * 16384, col0 + c * 64, i * 128, b);
@@ -549,17 +578,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
     if (kv_armed >= 0) mbar_wait(kv_full, static_cast<uint32_t>(kv_armed), p.status, 72, nullptr);
-    for (int i = 0; i < QS; ++i)
-      if (q_armed[i] >= 0) mbar_wait(&qd_full[i], static_cast<uint32_t>(q_armed[i]), p.status, 73, nullptr);
+    if (q_armed[0] >= 0) mbar_wait(&qd_full[0], static_cast<uint32_t>(q_armed[0]), p.status, 73, nullptr);
+    if (q_armed[1] >= 0) mbar_wait(&qd_full[1], static_cast<uint32_t>(q_armed[1]), p.status, 73, nullptr);
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idS = idesc_bf16_f32(128, 128, false, false);   // S^T, dP^T
     constexpr uint32_t idKV = idesc_bf16_f32(128, D, false, true);     // dV, dK: B MN-major
     constexpr uint32_t idQ = idesc_bf16_f32(128, D, true, true);       // dQ: A (dS) and B (K) MN-major
-    const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP), adS = smem_u32(sdS);
+    const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
     int g = 0, t = 0;
     bool ok = true;
-    // Score products for block g (stage st).
+    // Score products for block gg.
     auto issue_scores = [&](int gg) -> bool {
       const int st = gg % QS;
       if (!mbar_wait(&qd_full[st], static_cast<uint32_t>(gg / QS) & 1u, p.status, 80, abort_flag) ||
@@ -578,29 +607,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       umma_commit(sd_full);
       return true;
     };
-    int next_scored = -1;  // last global block whose score products are issued
     for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
       const int kt = w / bhc;
       const int n = p.n_t - kt;
       if (!mbar_wait(kv_full, static_cast<uint32_t>(t) & 1u, p.status, 82, abort_flag)) break;
-      if (next_scored < g) {
-        if (!issue_scores(g)) break;
-        next_scored = g;
-      }
+      if (!issue_scores(g)) break;
       for (int u = 0; u < n; ++u, ++g) {
         const int st = g % QS;
+        const int pb = g & 1;
         if (!mbar_wait(pds_full, static_cast<uint32_t>(g) & 1u, p.status, 83, abort_flag)) {
           ok = false;
           break;
         }
         // Queue the next block's scores first (same item) so the compute warps
-        // can start on it while dV/dK/dQ of this block run.
-        if (u + 1 < n) {
-          if (!issue_scores(g + 1)) {
-            ok = false;
-            break;
-          }
-          next_scored = g + 1;
+        // start on it while dV/dK/dQ of this block run.
+        if (u + 1 < n && !issue_scores(g + 1)) {
+          ok = false;
+          break;
         }
         if (u == 0 && !mbar_wait(dkv_free, (static_cast<uint32_t>(t) & 1u) ^ 1u, p.status, 84, abort_flag)) {
           ok = false;
@@ -608,6 +631,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         tc_fence_after();
         const uint32_t aQ = smem_u32(sQ + st * C::kTileBytes), adO = smem_u32(sdO + st * C::kTileBytes);
+        const uint32_t aP = smem_u32(sPD + pb * 2 * C::kPBytes), adS = aP + C::kPBytes;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t offA = (kk >> 2) * 16384 + (kk & 3) * 32;
@@ -628,91 +652,88 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_bf16_ss(tmem + C::kColDQ, sdesc_sw128(adS + kk * 2048, 16384, 1024),
                        sdesc_sw128(aK + kk * 2048, 16384, 1024), idQ, kk > 0 ? 1u : 0u);
         umma_commit(dq_full);
-        umma_commit(mm_done);
+        umma_commit(&mm_done[pb]);
       }
       if (!ok) break;
       umma_commit(kv_empty);
     }
     umma_commit(drain);
     mbar_wait(drain, 0, p.status, 86, nullptr);
-  } else if (warp >= 2 && warp < 6) {
+  } else if (warp >= 2 && warp < 2 + kBwdCompute) {
     // ------------------------------------------------------------ compute (thread = key row)
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;  // query columns [64*half, 64*half + 64)
     const int krow = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const int ct = threadIdx.x - 64;  // 0..127
-    int g = 0, t = 0;
+    const int ct = threadIdx.x - 64;  // 0..255
+    int g = 0;
     bool ok = true;
-    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x) {
       const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
       const int n = p.n_t - kt;
       const long long lbase = static_cast<long long>(bh) * p.S;
       for (int u = 0; u < n; ++u, ++g) {
         const int i = kt + u;
-        // Stage lse (log2 units) and delta of this query block.
         {
-          // Every compute thread writes one entry, then all 128 meet on an
-          // mbarrier (bounded wait).  Buffer g&1 is rewritten at block g+2,
-          // after every thread has passed block g+1's meeting point.
-          const int q = i * 128 + ct;
-          float* L = sL + (g & 1) * 128;
-          float* Dl = sDel + (g & 1) * 128;
-          L[ct] = q < p.S ? p.lse[lbase + q] * 1.4426950408889634f : INFINITY;
-          Dl[ct] = q < p.S ? p.delta[lbase + q] : 0.f;
+          // Threads 0..127 stage lse (log2 units), 128..255 delta; all 256
+          // meet on an mbarrier (bounded wait).  Buffer g&1 is rewritten at
+          // block g+2, after every thread has passed block g+1's meeting point.
+          const int q = i * 128 + (ct & 127);
+          if (ct < 128) sL[(g & 1) * 128 + ct] = q < p.S ? p.lse[lbase + q] * 1.4426950408889634f : INFINITY;
+          else sDel[(g & 1) * 128 + ct - 128] = q < p.S ? p.delta[lbase + q] : 0.f;
           mbar_arrive(&stage_bar[g & 1]);
           if (!mbar_wait(&stage_bar[g & 1], static_cast<uint32_t>(g >> 1) & 1u, p.status, 89, abort_flag)) {
             ok = false;
             break;
           }
         }
-        const float* L = sL + (g & 1) * 128;
-        const float* Dl = sDel + (g & 1) * 128;
+        const float* L = sL + (g & 1) * 128 + half * 64;
+        const float* Dl = sDel + (g & 1) * 128 + half * 64;
         if (!mbar_wait(sd_full, static_cast<uint32_t>(g) & 1u, p.status, 90, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        uint8_t* sP = sPD + (g & 1) * 2 * C::kPBytes + half * 16384;
+        uint8_t* sdS = sP + C::kPBytes;
 #pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
-          uint32_t s0[32], s1[32], d0[32], d1[32];
-          tmem_ld_32x32b_x32(tmem + lane_base + C::kColS + half * 64, s0);
-          tmem_ld_32x32b_x32(tmem + lane_base + C::kColS + half * 64 + 32, s1);
-          tmem_ld_32x32b_x32(tmem + lane_base + C::kColDP + half * 64, d0);
-          tmem_ld_32x32b_x32(tmem + lane_base + C::kColDP + half * 64 + 32, d1);
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t col = static_cast<uint32_t>(half * 64 + c * 32);
+          uint32_t sv[32], dv[32];
+          tmem_ld_32x32b_x32(tmem + lane_base + C::kColS + col, sv);
+          tmem_ld_32x32b_x32(tmem + lane_base + C::kColDP + col, dv);
           tmem_ld_wait();
-          if (half == 1) {
+          if (c == 1) {
             // S^T and dP^T fully read: the next block's score products may overwrite them.
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(sd_free);
           }
-          uint32_t pp[32], dd[32];
+          uint32_t pp[16], dd[16];
 #pragma unroll
-          for (int e = 0; e < 64; e += 2) {
-            const int qc = half * 64 + e;
-            const uint32_t sa = e < 32 ? s0[e] : s1[e - 32], sb = e < 32 ? s0[e + 1] : s1[e - 31];
-            const uint32_t da = e < 32 ? d0[e] : d1[e - 32], db = e < 32 ? d0[e + 1] : d1[e - 31];
-            float p0 = ex2(fmaf(__uint_as_float(sa), p.scale_log2, -L[qc]));
-            float p1 = ex2(fmaf(__uint_as_float(sb), p.scale_log2, -L[qc + 1]));
+          for (int e = 0; e < 32; e += 2) {
+            const int qc = c * 32 + e;  // within this half
+            float p0 = ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -L[qc]));
+            float p1 = ex2(fmaf(__uint_as_float(sv[e + 1]), p.scale_log2, -L[qc + 1]));
             if (u == 0) {  // diagonal block: query < key is masked
-              if (qc < krow) p0 = 0.f;
-              if (qc + 1 < krow) p1 = 0.f;
+              if (half * 64 + qc < krow) p0 = 0.f;
+              if (half * 64 + qc + 1 < krow) p1 = 0.f;
             }
-            const float g0 = p0 * (__uint_as_float(da) - Dl[qc]);
-            const float g1 = p1 * (__uint_as_float(db) - Dl[qc + 1]);
+            const float g0 = p0 * (__uint_as_float(dv[e]) - Dl[qc]);
+            const float g1 = p1 * (__uint_as_float(dv[e + 1]) - Dl[qc + 1]);
             pp[e >> 1] = pack_bf16x2(p0, p1);
             dd[e >> 1] = pack_bf16x2(g0, g1);
           }
-          if (half == 0 && g > 0) {
-            // dV/dK/dQ of the previous block have finished reading P^T / dS^T.
-            if (!mbar_wait(mm_done, static_cast<uint32_t>(g - 1) & 1u, p.status, 91, abort_flag)) {
+          if (c == 0 && g >= 2) {
+            // dV/dK/dQ of block g-2 have finished reading this P^T / dS^T buffer.
+            if (!mbar_wait(&mm_done[g & 1], (static_cast<uint32_t>(g >> 1) & 1u) ^ 1u, p.status, 91, abort_flag)) {
               ok = false;
               break;
             }
           }
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t off = half * 16384 + sw128_off(krow, k);
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t off = sw128_off(krow, c * 4 + k);
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(sP + off)), "r"(pp[4 * k]),
                          "r"(pp[4 * k + 1]), "r"(pp[4 * k + 2]), "r"(pp[4 * k + 3])
                          : "memory");
@@ -728,31 +749,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (lane == 0) mbar_arrive(pds_full);
       }
       if (!ok) break;
-      // dK (scaled) and dV of this key tile.
-      if (!mbar_wait(mm_done, static_cast<uint32_t>(g - 1) & 1u, p.status, 92, abort_flag)) break;
+      // dK (scaled; warps of half 0) and dV (half 1) of this key tile.
+      if (!mbar_wait(&mm_done[(g - 1) & 1], static_cast<uint32_t>((g - 1) >> 1) & 1u, p.status, 92, abort_flag)) break;
       tc_fence_after();
       const int key = kt * 128 + krow;
+      const float sc = half == 0 ? p.scale : 1.f;
+      const uint32_t colx = half == 0 ? C::kColDK : C::kColDV;
       uint8_t* row = reinterpret_cast<uint8_t*>(p.dqkv) +
-                     ((static_cast<long long>(b) * p.S + key) * p.lddq + static_cast<long long>(h) * 3 * D) * 2;
+                     ((static_cast<long long>(b) * p.S + key) * p.lddq + static_cast<long long>(h) * 3 * D +
+                      (half + 1) * D) * 2;
 #pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        const float sc = which == 0 ? p.scale : 1.f;
-        const uint32_t col = which == 0 ? C::kColDK : C::kColDV;
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + colx + c * 32, o);
+        tmem_ld_wait();
+        if (key < p.S) {
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(tmem + lane_base + col + c * 32, o);
-          tmem_ld_wait();
-          if (key < p.S) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              uint4 v;
-              v.x = pack_bf16x2(__uint_as_float(o[8 * k + 0]) * sc, __uint_as_float(o[8 * k + 1]) * sc);
-              v.y = pack_bf16x2(__uint_as_float(o[8 * k + 2]) * sc, __uint_as_float(o[8 * k + 3]) * sc);
-              v.z = pack_bf16x2(__uint_as_float(o[8 * k + 4]) * sc, __uint_as_float(o[8 * k + 5]) * sc);
-              v.w = pack_bf16x2(__uint_as_float(o[8 * k + 6]) * sc, __uint_as_float(o[8 * k + 7]) * sc);
-              *reinterpret_cast<uint4*>(row + (which + 1) * D * 2 + c * 64 + k * 16) = v;
-            }
+          for (int k = 0; k < 4; ++k) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[8 * k + 0]) * sc, __uint_as_float(o[8 * k + 1]) * sc);
+            v.y = pack_bf16x2(__uint_as_float(o[8 * k + 2]) * sc, __uint_as_float(o[8 * k + 3]) * sc);
+            v.z = pack_bf16x2(__uint_as_float(o[8 * k + 4]) * sc, __uint_as_float(o[8 * k + 5]) * sc);
+            v.w = pack_bf16x2(__uint_as_float(o[8 * k + 6]) * sc, __uint_as_float(o[8 * k + 7]) * sc);
+            *reinterpret_cast<uint4*>(row + c * 64 + k * 16) = v;
           }
         }
       }
@@ -760,7 +779,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(dkv_free);
     }
-  } else if (warp >= 6) {
+  } else if (warp >= 2 + kBwdCompute) {
     // ------------------------------------------------------------ dQ drain (thread = query row)
     const int quarter = warp & 3;
     const int qrow = quarter * 32 + lane;
@@ -787,7 +806,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(dq_free);
           }
-          if (q < p.S) {
+          if (q < p.S && !(p.flags & 1)) {
 #pragma unroll
             for (int k = 0; k < 8; ++k)
               red_add_v4(dst + c * 32 + 4 * k, __uint_as_float(o[4 * k]), __uint_as_float(o[4 * k + 1]),
@@ -864,7 +883,8 @@ int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, floa
   auto k = md::attn_tc::fwd_kernel<D>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
-  const int grid = p.items < g_sms ? p.items : g_sms;
+  const int slots = g_sms * C::kCtasPerSm;
+  const int grid = p.items < slots ? p.items : slots;
   k<<<grid, md::attn_tc::kThreads, C::kSmemBytes, st>>>(tm, p);
   return static_cast<int>(cudaGetLastError());
 }
@@ -898,6 +918,11 @@ int bwd_tc_launch(const void* qkv, long long ldq, const void* dout, long long ld
   p.items = p.n_t * B * H;
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
+  static const int flags = [] {
+    const char* v = getenv("MINIDIST_ATTN_BWD_FLAGS");
+    return v ? atoi(v) : 0;
+  }();
+  p.flags = flags;
   p.status = reinterpret_cast<md::Status*>(status);
   auto k = md::attn_tc::bwd_kernel<D>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
