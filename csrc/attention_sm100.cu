@@ -222,11 +222,16 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
       if (k_armed[i] >= 0) mbar_wait(&k_full[i], static_cast<uint32_t>(k_armed[i]), p.status, 44, nullptr);
       if (v_armed[i] >= 0) mbar_wait(&v_full[i], static_cast<uint32_t>(v_armed[i]), p.status, 45, nullptr);
     }
-  } else if (warp == 1 && lane == 0) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (whole warp, elected lane issues)
     constexpr uint32_t idS = idesc_bf16_f32(kBM, kBN, false, false);
     constexpr uint32_t idO = idesc_bf16_f32(kBM, D, false, true);
-    const uint32_t sp = smem_u32(sP);
+    // Base descriptors; an operand at byte offset `off` is base + (off >> 4).
+    const uint64_t dP = sdesc_sw128(smem_u32(sP), 16, 1024);
+    const uint64_t dV = sdesc_sw128(smem_u32(sV), kBN * 128, 1024);
+    const uint64_t dQ = sdesc_sw128(smem_u32(sQ), 16, 1024);
+    const uint64_t dK = sdesc_sw128(smem_u32(sK), 16, 1024);
+    constexpr uint32_t kTile16 = C::kTileBytes >> 4;
     int pend = -1;
     bool pend_first = false;
     // O += P V for block gp (P from shared memory, V MN-major).
@@ -235,15 +240,13 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
       const int st = gp % KST;
       if (!mbar_wait(&v_full[st], static_cast<uint32_t>(gp / KST) & 1u, p.status, 53, abort_flag)) return false;
       tc_fence_after();
-      const uint32_t va = smem_u32(sV + st * C::kTileBytes);
+      const uint64_t v0 = dV + st * kTile16;
 #pragma unroll
-      for (int kk = 0; kk < kBN / 16; ++kk) {
-        const uint64_t ad = sdesc_sw128(sp + (kk >> 2) * (kBM * 128) + (kk & 3) * 32, 16, 1024);
-        const uint64_t bd = sdesc_sw128(va + kk * 2048, kBN * 128, 1024);
-        umma_bf16_ss(tmem + C::kOCol, ad, bd, idO, (first && kk == 0) ? 0u : 1u);
-      }
-      umma_commit(o_done);
-      umma_commit(&v_empty[st]);
+      for (int kk = 0; kk < kBN / 16; ++kk)
+        umma_bf16_ss_elect(tmem + C::kOCol, dP + (((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4), v0 + kk * 128,
+                           idO, (first && kk == 0) ? 0u : 1u);
+      umma_commit_elect(o_done);
+      umma_commit_elect(&v_empty[st]);
       return true;
     };
     int g = 0, t = 0;
@@ -253,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
       decode(p, w, qt, b, h);
       const int qb = t % QB;
       if (!mbar_wait(&q_full[qb], static_cast<uint32_t>(t / QB) & 1u, p.status, 50, abort_flag)) break;
-      const uint32_t qa = smem_u32(sQ + qb * C::kTileBytes);
+      const uint64_t q0 = dQ + qb * kTile16;
       for (int j = 0; j <= qt; ++j, ++g) {
         const int st = g % KST;
         const int sb = g % SB;
@@ -263,16 +266,16 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
           break;
         }
         tc_fence_after();
-        const uint32_t ka = smem_u32(sK + st * C::kTileBytes);
+        const uint64_t k0 = dK + st * kTile16;
         const uint32_t sd = tmem + static_cast<uint32_t>(sb * kBN);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
-          umma_bf16_ss(sd, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+          const uint32_t off = ((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4;
+          umma_bf16_ss_elect(sd, q0 + off, k0 + off, idS, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[sb]);
-        umma_commit(&k_empty[st]);
-        if (j == qt) umma_commit(&q_empty[qb]);
+        umma_commit_elect(&s_full[sb]);
+        umma_commit_elect(&k_empty[st]);
+        if (j == qt) umma_commit_elect(&q_empty[qb]);
         if (pend >= 0 && !issue_pv(pend, pend_first)) {
           ok = false;
           break;
@@ -282,8 +285,8 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
       }
     }
     if (ok && pend >= 0) issue_pv(pend, pend_first);
-    // Every MMA this thread issued completes before TMEM is released.
-    umma_commit(drain);
+    // Every MMA this warp issued completes before TMEM is released.
+    umma_commit_elect(drain);
     mbar_wait(drain, 0, p.status, 55, nullptr);
   } else if (warp >= 2) {
     // ------------------------------------------------------------ softmax + epilogue
@@ -423,13 +426,16 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
 //   P^T  = exp(S^T * scale - lse_i),  dS^T = P^T (dP^T - delta_i)   [compute warps, bf16 to smem]
 //   dV  += P^T dO_i,   dK += dS^T Q_i      (TMEM accumulators for the whole item)
 //   dQ_i = dS K_j                            (TMEM, drained by the dQ warps into an
-//                                             fp32 accumulator with red.global.add)
+//                                             fp32 accumulator with bulk reduce-adds)
 // Roles: warp 0 TMA, warp 1 MMA, warps 2..9 compute (thread = key row; warps
 // 2..5 take query columns 0..63, warps 6..9 columns 64..127, so two warps
-// share every SM sub-partition), warps 10..13 dQ drain (thread = query row).
-// P^T / dS^T are double-buffered in shared memory: the compute warps fill
-// buffer (i & 1) while the tensor core still reads the other one for the
-// dV/dK/dQ products of the previous block.
+// share every SM sub-partition), warps 10..13 dQ drain (thread = query row,
+// staged through shared memory into bulk reduce-adds).
+// The tensor core runs the next block's score products as soon as the compute
+// warps hold this block's scores in registers, then (once P^T/dS^T are in
+// shared memory) dK and dQ (which read dS^T; a single buffer, released as
+// soon as they are done), then dV (which reads P^T; double-buffered).  Q/dO tiles stream
+// through three stages so their loads start two blocks ahead.
 // ===========================================================================
 constexpr int kBwdThreads = 448;
 constexpr int kBwdCompute = 8;  // compute warps
@@ -438,10 +444,10 @@ template <int D>
 struct BwdCfg {
   static constexpr int kChunks = D / 64;
   static constexpr int kTileBytes = 128 * D * 2;
-  static constexpr int kQStages = 2;
+  static constexpr int kQStages = 3;
   static constexpr int kPBytes = 128 * 128 * 2;
-  // K, V | (Q, dO) x stages | (P^T, dS^T) x 2 | lse, delta x 2 parities
-  static constexpr int kSmemData = (2 + 2 * kQStages) * kTileBytes + 4 * kPBytes + 2 * 2 * 128 * 4;
+  // K, V | (Q, dO) x stages | P^T x 2 | dS^T | lse, delta x 2 blocks
+  static constexpr int kSmemData = (2 + 2 * kQStages) * kTileBytes + 3 * kPBytes + 2 * 2 * 128 * 4;
   // No alignment slack fits: the dynamic window must start 1024-byte aligned
   // (checked in the kernel).
   static constexpr int kSmemBytes = kSmemData + 256;
@@ -464,7 +470,14 @@ struct BwdParams {
   float scale, scale_log2;
   int flags;           // bit 0: skip the dQ reductions (timing experiments only; dQ is then wrong)
   Status* status;
+  long long* trace;    // optional: CTA 0 records clock64() at pipeline hand-offs, [64 blocks][32]
 };
+
+// Pipeline trace for performance analysis (CTA 0, first 64 blocks; no-op unless enabled).
+#define MD_TRACE(gg, slot)                                                                  \
+  do {                                                                                     \
+    if (p.trace != nullptr && blockIdx.x == 0 && (gg) < 64) p.trace[(gg) * 32 + (slot)] = clock64(); \
+  } while (0)
 
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
@@ -474,7 +487,7 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
 template <int D>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
-               const __grid_constant__ BwdParams p) {
+               const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ BwdParams p) {
   using C = BwdCfg<D>;
   constexpr int QS = C::kQStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -486,25 +499,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sV = sK + C::kTileBytes;
   uint8_t* sQ = sV + C::kTileBytes;               // [QS]
   uint8_t* sdO = sQ + QS * C::kTileBytes;         // [QS]
-  uint8_t* sPD = sdO + QS * C::kTileBytes;        // [2] x (P^T, dS^T)
-  float* sL = reinterpret_cast<float*>(sPD + 4 * C::kPBytes);  // [2][128] lse (log2 units)
+  uint8_t* sPt = sdO + QS * C::kTileBytes;        // [2] P^T
+  uint8_t* sdSt = sPt + 2 * C::kPBytes;           // dS^T
+  float* sL = reinterpret_cast<float*>(sdSt + C::kPBytes);  // [2][128] lse (log2 units)
   float* sDel = sL + 2 * 128;                                   // [2][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 2 * 128);
   uint64_t* kv_full = bars + 0;
   uint64_t* kv_empty = bars + 1;
-  uint64_t* qd_full = bars + 2;    // [2]
-  uint64_t* qd_empty = bars + 4;   // [2]
-  uint64_t* sd_full = bars + 6;
-  uint64_t* sd_free = bars + 7;
-  uint64_t* pds_full = bars + 8;
-  uint64_t* mm_done = bars + 9;    // [2] per P^T/dS^T buffer
-  uint64_t* dq_full = bars + 11;
-  uint64_t* dq_free = bars + 12;
-  uint64_t* dkv_free = bars + 13;
-  uint64_t* drain = bars + 14;
-  uint64_t* stage_bar = bars + 15;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18);
+  uint64_t* qd_full = bars + 2;    // [3]
+  uint64_t* qd_empty = bars + 5;   // [3]
+  uint64_t* sd_full = bars + 8;
+  uint64_t* sd_free = bars + 9;
+  uint64_t* pds_full = bars + 10;
+  uint64_t* p_free = bars + 11;    // [2] per P^T buffer
+  uint64_t* ds_free = bars + 13;
+  uint64_t* dq_full = bars + 14;
+  uint64_t* dq_free = bars + 15;
+  uint64_t* dkv_free = bars + 16;
+  uint64_t* drain = bars + 17;
+  uint64_t* stage_bar = bars + 18;  // [2] (slot 20 unused)
+  uint64_t* pst_free = bars + 21;   // [2] P^T buffer free again after the dQ staging
+  uint64_t* dq_staged = bars + 23;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -520,18 +537,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(sd_full, 1);
     mbar_init(sd_free, kBwdCompute);
     mbar_init(pds_full, kBwdCompute);
-    mbar_init(&mm_done[0], 1);
-    mbar_init(&mm_done[1], 1);
+    mbar_init(&p_free[0], 1);
+    mbar_init(&p_free[1], 1);
+    mbar_init(ds_free, 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 4);
     mbar_init(dkv_free, kBwdCompute);
     mbar_init(drain, 1);
-    mbar_init(&stage_bar[0], 32 * kBwdCompute);
-    mbar_init(&stage_bar[1], 32 * kBwdCompute);
+    for (int i = 0; i < 2; ++i) mbar_init(&stage_bar[i], kBwdCompute);
+    mbar_init(&pst_free[0], 1);
+    mbar_init(&pst_free[1], 1);
+    mbar_init(dq_staged, 4);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQKV);
     tma_prefetch_desc(&tmDO);
+    tma_prefetch_desc(&tmDQ);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -545,7 +566,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ TMA producer
     int kv_armed = -1;
-    int q_armed[2] = {-1, -1};
+    int q_armed[QS];
+    for (int i = 0; i < QS; ++i) q_armed[i] = -1;
     int g = 0, t = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
@@ -567,9 +589,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           ok = false;
           break;
         }
+        MD_TRACE(g, 11);
         mbar_arrive_expect_tx(&qd_full[st], 2 * C::kTileBytes);
-        if (st == 0) q_armed[0] = static_cast<int>(ph);
-        else q_armed[1] = static_cast<int>(ph);
+        q_armed[st] = static_cast<int>(ph);
 #pragma unroll
         for (int c = 0; c < C::kChunks; ++c) {
           tma_load_3d(&tmQKV, &qd_full[st], sQ + st * C::kTileBytes + c * 16384, col0 + c * 64, i * 128, b);
@@ -578,14 +600,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
     if (kv_armed >= 0) mbar_wait(kv_full, static_cast<uint32_t>(kv_armed), p.status, 72, nullptr);
-    if (q_armed[0] >= 0) mbar_wait(&qd_full[0], static_cast<uint32_t>(q_armed[0]), p.status, 73, nullptr);
-    if (q_armed[1] >= 0) mbar_wait(&qd_full[1], static_cast<uint32_t>(q_armed[1]), p.status, 73, nullptr);
-  } else if (warp == 1 && lane == 0) {
-    // ------------------------------------------------------------ MMA issuer
+    for (int i = 0; i < QS; ++i)
+      if (q_armed[i] >= 0) mbar_wait(&qd_full[i], static_cast<uint32_t>(q_armed[i]), p.status, 73, nullptr);
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (whole warp, elected lane issues)
     constexpr uint32_t idS = idesc_bf16_f32(128, 128, false, false);   // S^T, dP^T
     constexpr uint32_t idKV = idesc_bf16_f32(128, D, false, true);     // dV, dK: B MN-major
     constexpr uint32_t idQ = idesc_bf16_f32(128, D, true, true);       // dQ: A (dS) and B (K) MN-major
-    const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
+    // Base descriptors; an operand at byte offset `off` is base + (off >> 4).
+    const uint64_t dK_k = sdesc_sw128(smem_u32(sK), 16, 1024);
+    const uint64_t dK_mn = sdesc_sw128(smem_u32(sK), 16384, 1024);
+    const uint64_t dV_k = sdesc_sw128(smem_u32(sV), 16, 1024);
+    const uint64_t dQ_k = sdesc_sw128(smem_u32(sQ), 16, 1024);
+    const uint64_t dQ_mn = sdesc_sw128(smem_u32(sQ), 16384, 1024);
+    const uint64_t ddO_k = sdesc_sw128(smem_u32(sdO), 16, 1024);
+    const uint64_t ddO_mn = sdesc_sw128(smem_u32(sdO), 16384, 1024);
+    const uint64_t dP_k = sdesc_sw128(smem_u32(sPt), 16, 1024);
+    const uint64_t ddS_k = sdesc_sw128(smem_u32(sdSt), 16, 1024);
+    const uint64_t ddS_mn = sdesc_sw128(smem_u32(sdSt), 16384, 1024);
+    constexpr uint32_t kTile16 = C::kTileBytes >> 4;
+    constexpr uint32_t kP16 = C::kPBytes >> 4;
     int g = 0, t = 0;
     bool ok = true;
     // Score products for block gg.
@@ -594,17 +628,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (!mbar_wait(&qd_full[st], static_cast<uint32_t>(gg / QS) & 1u, p.status, 80, abort_flag) ||
           !mbar_wait(sd_free, (static_cast<uint32_t>(gg) & 1u) ^ 1u, p.status, 81, abort_flag))
         return false;
+      MD_TRACE(gg, 12);
       tc_fence_after();
-      const uint32_t aQ = smem_u32(sQ + st * C::kTileBytes), adO = smem_u32(sdO + st * C::kTileBytes);
+      const uint64_t q0 = dQ_k + st * kTile16, o0 = ddO_k + st * kTile16;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-        umma_bf16_ss(tmem + C::kColS, sdesc_sw128(aK + off, 16, 1024), sdesc_sw128(aQ + off, 16, 1024), idS,
-                     kk > 0 ? 1u : 0u);
-        umma_bf16_ss(tmem + C::kColDP, sdesc_sw128(aV + off, 16, 1024), sdesc_sw128(adO + off, 16, 1024), idS,
-                     kk > 0 ? 1u : 0u);
+        const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+        umma_bf16_ss_elect(tmem + C::kColS, dK_k + off, q0 + off, idS, kk > 0 ? 1u : 0u);
+        umma_bf16_ss_elect(tmem + C::kColDP, dV_k + off, o0 + off, idS, kk > 0 ? 1u : 0u);
       }
-      umma_commit(sd_full);
+      umma_commit_elect(sd_full);
       return true;
     };
     for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
@@ -615,49 +648,54 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int u = 0; u < n; ++u, ++g) {
         const int st = g % QS;
         const int pb = g & 1;
-        if (!mbar_wait(pds_full, static_cast<uint32_t>(g) & 1u, p.status, 83, abort_flag)) {
-          ok = false;
-          break;
-        }
-        // Queue the next block's scores first (same item) so the compute warps
-        // start on it while dV/dK/dQ of this block run.
+        // The next block's score products go first: they only need the
+        // compute warps to have read this block's scores into registers
+        // (mid-block), so they run while the compute warps finish this block.
         if (u + 1 < n && !issue_scores(g + 1)) {
           ok = false;
           break;
         }
+        MD_TRACE(g, 6);
+        if (!mbar_wait(pds_full, static_cast<uint32_t>(g) & 1u, p.status, 83, abort_flag)) {
+          ok = false;
+          break;
+        }
+        MD_TRACE(g, 5);
         if (u == 0 && !mbar_wait(dkv_free, (static_cast<uint32_t>(t) & 1u) ^ 1u, p.status, 84, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t aQ = smem_u32(sQ + st * C::kTileBytes), adO = smem_u32(sdO + st * C::kTileBytes);
-        const uint32_t aP = smem_u32(sPD + pb * 2 * C::kPBytes), adS = aP + C::kPBytes;
+        const uint64_t qmn = dQ_mn + st * kTile16, omn = ddO_mn + st * kTile16;
+        const uint64_t pk = dP_k + pb * kP16;
+        const uint32_t acc0 = u > 0 ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t offA = (kk >> 2) * 16384 + (kk & 3) * 32;
-          const uint32_t acc = (u > 0 || kk > 0) ? 1u : 0u;
-          umma_bf16_ss(tmem + C::kColDV, sdesc_sw128(aP + offA, 16, 1024), sdesc_sw128(adO + kk * 2048, 16384, 1024),
-                       idKV, acc);
-          umma_bf16_ss(tmem + C::kColDK, sdesc_sw128(adS + offA, 16, 1024), sdesc_sw128(aQ + kk * 2048, 16384, 1024),
-                       idKV, acc);
-        }
-        umma_commit(&qd_empty[st]);
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16_ss_elect(tmem + C::kColDK, ddS_k + (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4), qmn + kk * 128,
+                             idKV, (acc0 | kk) ? 1u : 0u);
         if (!mbar_wait(dq_free, (static_cast<uint32_t>(g) & 1u) ^ 1u, p.status, 85, abort_flag)) {
           ok = false;
           break;
         }
+        MD_TRACE(g, 7);
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_bf16_ss(tmem + C::kColDQ, sdesc_sw128(adS + kk * 2048, 16384, 1024),
-                       sdesc_sw128(aK + kk * 2048, 16384, 1024), idQ, kk > 0 ? 1u : 0u);
-        umma_commit(dq_full);
-        umma_commit(&mm_done[pb]);
+          umma_bf16_ss_elect(tmem + C::kColDQ, ddS_mn + kk * 128, dK_mn + kk * 128, idQ, kk > 0 ? 1u : 0u);
+        umma_commit_elect(ds_free);
+        umma_commit_elect(dq_full);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16_ss_elect(tmem + C::kColDV, pk + (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4), omn + kk * 128, idKV,
+                             (acc0 | kk) ? 1u : 0u);
+        umma_commit_elect(&qd_empty[st]);
+        umma_commit_elect(&p_free[pb]);
+        MD_TRACE(g, 8);
       }
       if (!ok) break;
-      umma_commit(kv_empty);
+      umma_commit_elect(kv_empty);
     }
-    umma_commit(drain);
+    umma_commit_elect(drain);
     mbar_wait(drain, 0, p.status, 86, nullptr);
   } else if (warp >= 2 && warp < 2 + kBwdCompute) {
     // ------------------------------------------------------------ compute (thread = key row)
@@ -666,43 +704,79 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int krow = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int ct = threadIdx.x - 64;  // 0..255
+    // Threads 0..127 stage lse (log2 units), 128..255 delta, one entry per
+    // block, one block ahead: block g+1's values go to buffer (g+1) & 1 in the
+    // middle of block g, right after the wait for dK/dQ of block g-1 (which
+    // implies every compute warp has finished block g-1 and its reads of that
+    // buffer); the 8 warps then meet on stage_bar[(g+1) & 1] (bounded wait at
+    // the start of block g+1, normally already complete).  The load for block
+    // g+2 uses a clamped index and is only scaled when stored, so no
+    // arithmetic waits on it meanwhile.
+    auto load_raw = [&](int w_, int i_) -> float {
+      const int q = min(i_ * 128 + (ct & 127), p.S - 1);
+      const long long idx = static_cast<long long>(w_ % bhc) * p.S + q;
+      return ct < 128 ? p.lse[idx] : p.delta[idx];
+    };
+    auto stage = [&](int gg, int i_, float raw) {
+      const int q = i_ * 128 + (ct & 127);
+      const float v = ct < 128 ? (q < p.S ? raw * 1.4426950408889634f : INFINITY) : (q < p.S ? raw : 0.f);
+      (ct < 128 ? sL : sDel)[(gg & 1) * 128 + (ct & 127)] = v;
+      __syncwarp();
+      if (lane == 0) {
+        MD_TRACE(gg, 24 + warp - 2);
+        mbar_arrive(&stage_bar[gg & 1]);
+      }
+    };
+    // The block after (w_, i_) in this CTA's work list: (item, query tile) or w = -1.
+    auto next_block = [&](int w_, int i_, int& wn, int& in) {
+      if (i_ + 1 < p.n_t) {
+        wn = w_;
+        in = i_ + 1;
+      } else if (w_ + static_cast<int>(gridDim.x) < p.items) {
+        wn = w_ + static_cast<int>(gridDim.x);
+        in = wn / bhc;
+      } else {
+        wn = -1;
+      }
+    };
+    float pre = 0.f;
+    int pre_w = -1, pre_i = 0;  // block whose raw value `pre` holds
+    if (static_cast<int>(blockIdx.x) < p.items) {
+      const int kt0 = blockIdx.x / bhc;
+      stage(0, kt0, load_raw(blockIdx.x, kt0));
+      next_block(blockIdx.x, kt0, pre_w, pre_i);
+      if (pre_w >= 0) pre = load_raw(pre_w, pre_i);
+    }
     int g = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x) {
       const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
       const int n = p.n_t - kt;
-      const long long lbase = static_cast<long long>(bh) * p.S;
       for (int u = 0; u < n; ++u, ++g) {
-        const int i = kt + u;
-        {
-          // Threads 0..127 stage lse (log2 units), 128..255 delta; all 256
-          // meet on an mbarrier (bounded wait).  Buffer g&1 is rewritten at
-          // block g+2, after every thread has passed block g+1's meeting point.
-          const int q = i * 128 + (ct & 127);
-          if (ct < 128) sL[(g & 1) * 128 + ct] = q < p.S ? p.lse[lbase + q] * 1.4426950408889634f : INFINITY;
-          else sDel[(g & 1) * 128 + ct - 128] = q < p.S ? p.delta[lbase + q] : 0.f;
-          mbar_arrive(&stage_bar[g & 1]);
-          if (!mbar_wait(&stage_bar[g & 1], static_cast<uint32_t>(g >> 1) & 1u, p.status, 89, abort_flag)) {
-            ok = false;
-            break;
-          }
+        if (!mbar_wait(&stage_bar[g & 1], static_cast<uint32_t>(g >> 1) & 1u, p.status, 89, abort_flag)) {
+          ok = false;
+          break;
         }
+        if (threadIdx.x == 64) MD_TRACE(g, 0);
         const float* L = sL + (g & 1) * 128 + half * 64;
         const float* Dl = sDel + (g & 1) * 128 + half * 64;
         if (!mbar_wait(sd_full, static_cast<uint32_t>(g) & 1u, p.status, 90, abort_flag)) {
           ok = false;
           break;
         }
+        if (threadIdx.x == 64) MD_TRACE(g, 1);
         tc_fence_after();
-        uint8_t* sP = sPD + (g & 1) * 2 * C::kPBytes + half * 16384;
-        uint8_t* sdS = sP + C::kPBytes;
+        uint8_t* sP = sPt + (g & 1) * C::kPBytes + half * 16384;
+        uint8_t* sdS = sdSt + half * 16384;
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
           const uint32_t col = static_cast<uint32_t>(half * 64 + c * 32);
           uint32_t sv[32], dv[32];
+          if (c == 1 && threadIdx.x == 64) MD_TRACE(g, 13);
           tmem_ld_32x32b_x32(tmem + lane_base + C::kColS + col, sv);
           tmem_ld_32x32b_x32(tmem + lane_base + C::kColDP + col, dv);
           tmem_ld_wait();
+          if (c == 1 && threadIdx.x == 64) MD_TRACE(g, 14);
           if (c == 1) {
             // S^T and dP^T fully read: the next block's score products may overwrite them.
             tc_fence_before();
@@ -724,11 +798,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             pp[e >> 1] = pack_bf16x2(p0, p1);
             dd[e >> 1] = pack_bf16x2(g0, g1);
           }
-          if (c == 0 && g >= 2) {
-            // dV/dK/dQ of block g-2 have finished reading this P^T / dS^T buffer.
-            if (!mbar_wait(&mm_done[g & 1], (static_cast<uint32_t>(g >> 1) & 1u) ^ 1u, p.status, 91, abort_flag)) {
+          if (c == 0) {
+            if (threadIdx.x == 64) MD_TRACE(g, 2);
+            // dV of block g-2 and the dQ staging after it are done with this
+            // P^T buffer; dK/dQ of block g-1 have finished reading dS^T.
+            if ((g >= 2 && !mbar_wait(&pst_free[g & 1], (static_cast<uint32_t>(g >> 1) & 1u) ^ 1u, p.status, 91,
+                                      abort_flag)) ||
+                (g >= 1 && !mbar_wait(ds_free, static_cast<uint32_t>(g - 1) & 1u, p.status, 93, abort_flag))) {
               ok = false;
               break;
+            }
+            if (threadIdx.x == 64) MD_TRACE(g, 3);
+            // Stage the next block's lse/delta (buffer (g+1) & 1 is free: see above).
+            if (pre_w >= 0) {
+              stage(g + 1, pre_i, pre);
+              int w2, i2;
+              next_block(pre_w, pre_i, w2, i2);
+              pre_w = w2;
+              pre_i = i2;
+              if (w2 >= 0) pre = load_raw(w2, i2);
             }
           }
 #pragma unroll
@@ -746,11 +834,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(pds_full);
+        if (lane == 0) {
+          MD_TRACE(g, 16 + warp - 2);
+          mbar_arrive(pds_full);
+        }
       }
       if (!ok) break;
       // dK (scaled; warps of half 0) and dV (half 1) of this key tile.
-      if (!mbar_wait(&mm_done[(g - 1) & 1], static_cast<uint32_t>((g - 1) >> 1) & 1u, p.status, 92, abort_flag)) break;
+      // dV (the last product of the last block) done: both accumulators final.
+      if (!mbar_wait(&p_free[(g - 1) & 1], static_cast<uint32_t>((g - 1) >> 1) & 1u, p.status, 92, abort_flag)) break;
       tc_fence_after();
       const int key = kt * 128 + krow;
       const float sc = half == 0 ? p.scale : 1.f;
@@ -781,9 +873,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else if (warp >= 2 + kBwdCompute) {
     // ------------------------------------------------------------ dQ drain (thread = query row)
+    // dQ_i leaves TMEM into the P^T buffer of its block once dV has consumed
+    // it (fp32, two 128 x 32 sub-tiles with the 128-byte swizzle), then one
+    // bulk tensor reduce-add per sub-tile adds it into the fp32 accumulator in
+    // global memory (the L2 reduces whole lines; rows past the sequence end
+    // are clipped by the tensor map).  The buffer is handed back to the compute
+    // warps once the bulk copies have read it.
     const int quarter = warp & 3;
     const int qrow = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const bool issuer = warp == 2 + kBwdCompute && lane == 0;
     int g = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x) {
@@ -793,28 +892,49 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           ok = false;
           break;
         }
+        if (threadIdx.x == 320) MD_TRACE(g, 9);
         tc_fence_after();
-        const int q = i * 128 + qrow;
-        float* dst = p.dqacc + (static_cast<long long>(b) * p.S + q) * p.ldacc + static_cast<long long>(h) * D;
+        uint32_t o[D / 32][32];
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(tmem + lane_base + C::kColDQ + c * 32, o);
-          tmem_ld_wait();
-          if (c == D / 32 - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(dq_free);
-          }
-          if (q < p.S && !(p.flags & 1)) {
+        for (int c = 0; c < D / 32; ++c) tmem_ld_32x32b_x32(tmem + lane_base + C::kColDQ + c * 32, o[c]);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_free);
+        // dV of this block has finished reading its P^T buffer.
+        if (!mbar_wait(&p_free[g & 1], static_cast<uint32_t>(g >> 1) & 1u, p.status, 96, abort_flag)) {
+          ok = false;
+          break;
+        }
+        uint8_t* stg = sPt + (g & 1) * C::kPBytes;
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              red_add_v4(dst + c * 32 + 4 * k, __uint_as_float(o[4 * k]), __uint_as_float(o[4 * k + 1]),
-                         __uint_as_float(o[4 * k + 2]), __uint_as_float(o[4 * k + 3]));
+        for (int c = 0; c < D / 32; ++c)
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(stg + c * 16384 +
+                                                                                   sw128_off(qrow, k))),
+                         "r"(o[c][4 * k]), "r"(o[c][4 * k + 1]), "r"(o[c][4 * k + 2]), "r"(o[c][4 * k + 3])
+                         : "memory");
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_staged);
+        if (issuer) {
+          if (!mbar_wait(dq_staged, static_cast<uint32_t>(g) & 1u, p.status, 97, abort_flag)) {
+            ok = false;
+          } else {
+            if (!(p.flags & 1)) {
+#pragma unroll
+              for (int c = 0; c < D / 32; ++c) tma_reduce_add_3d(&tmDQ, stg + c * 16384, h * D + c * 32, i * 128, b);
+              bulk_commit_group();
+              bulk_wait_read_all();
+            }
+            mbar_arrive(&pst_free[g & 1]);
           }
         }
+        ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
       }
     }
+    if (issuer) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -855,7 +975,19 @@ bool make_map_bsc(CUtensorMap* map, const void* ptr, int B, int S, long long col
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [B, S, cols] view of a [B*S, ld] fp32 matrix; box {32 cols, 128 rows, 1}, 128B swizzle.
+bool make_map_f32_bsc(CUtensorMap* map, const void* ptr, int B, int S, long long cols, long long ld) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(ld) * 4 * S};
+  cuuint32_t box[3] = {32, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode_attn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int g_sms = 0;
+long long* g_trace = nullptr;  // device buffer set by md_attn_trace_enable (analysis only)
 
 template <int D>
 int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, float* lse, int B, int H, int S,
@@ -896,8 +1028,9 @@ int bwd_tc_launch(const void* qkv, long long ldq, const void* dout, long long ld
                   float scale, void* status, cudaStream_t st) {
   using C = md::attn_tc::BwdCfg<D>;
   if (!get_encoder()) return -3;
-  CUtensorMap tq, tdo;
-  if (!make_map_bsc(&tq, qkv, B, S, 3LL * H * D, ldq) || !make_map_bsc(&tdo, dout, B, S, 1LL * H * D, lddo))
+  CUtensorMap tq, tdo, tdq;
+  if (!make_map_bsc(&tq, qkv, B, S, 3LL * H * D, ldq) || !make_map_bsc(&tdo, dout, B, S, 1LL * H * D, lddo) ||
+      !make_map_f32_bsc(&tdq, dqacc, B, S, 1LL * H * D, ldacc))
     return -4;
   if (g_sms == 0) {
     int dev = 0;
@@ -924,11 +1057,12 @@ int bwd_tc_launch(const void* qkv, long long ldq, const void* dout, long long ld
   }();
   p.flags = flags;
   p.status = reinterpret_cast<md::Status*>(status);
+  p.trace = g_trace;
   auto k = md::attn_tc::bwd_kernel<D>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
   const int grid = p.items < g_sms ? p.items : g_sms;
-  k<<<grid, md::attn_tc::kBwdThreads, C::kSmemBytes, st>>>(tq, tdo, p);
+  k<<<grid, md::attn_tc::kBwdThreads, C::kSmemBytes, st>>>(tq, tdo, tdq, p);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -945,6 +1079,25 @@ int md_attn_bwd_tc_main(const void* qkv, long long ldq, const void* dout, long l
                         int S, int D, float scale, void* status, cudaStream_t st) {
   if (D != 64) return -2;
   return bwd_tc_launch<64>(qkv, ldq, dout, lddo, lse, delta, dqacc, ldacc, dqkv, lddq, B, H, S, scale, status, st);
+}
+
+// Performance analysis: record clock64() hand-off timestamps of CTA 0 of the
+// backward kernel into a [64][32] device buffer (enable=1), read them back
+// into host memory (md_attn_trace_read), or switch recording off (enable=0).
+int md_attn_trace_enable(int enable) {
+  if (enable && g_trace == nullptr) {
+    if (cudaMalloc(&g_trace, 64 * 32 * sizeof(long long)) != cudaSuccess) return -1;
+    cudaMemset(g_trace, 0, 64 * 32 * sizeof(long long));
+  }
+  if (!enable && g_trace != nullptr) {
+    cudaFree(g_trace);
+    g_trace = nullptr;
+  }
+  return 0;
+}
+int md_attn_trace_read(long long* host) {
+  if (g_trace == nullptr) return -1;
+  return static_cast<int>(cudaMemcpy(host, g_trace, 64 * 32 * sizeof(long long), cudaMemcpyDeviceToHost));
 }
 
 // tcgen05 causal attention forward; same layouts as md_attn_fwd (attention.cu).
