@@ -99,11 +99,6 @@ __device__ __forceinline__ float lg2(float x) {
   return y;
 }
 
-// Byte offset of (row, 16-byte chunk) inside a 128-row, 128-byte-row tile with
-// the TMA 128B swizzle (chunk index XOR row % 8; 8-row groups 1024 B apart).
-__device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
-  return static_cast<uint32_t>((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
-}
 
 
 template <int D>

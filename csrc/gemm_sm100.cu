@@ -59,12 +59,18 @@ constexpr int kCeSlab = 128;  // CE statistics are kept per 128-column slab
 
 enum EpiMode : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiDGELU = 2, kEpiCE = 3 };
 
+// Epilogue staging: each epilogue warp owns slabs of 32 rows x 128 bytes
+// (128B-swizzled) that TMA stores / reduce-adds write out; two per warp with
+// four epilogue warps, one with eight (32 KB either way).
+constexpr int kSlabBytes = 32 * 128;
+constexpr int kEpiSmem = 8 * kSlabBytes;
+
 template <int CG>
 struct Cfg {
   static constexpr int kBBytes = (BN / CG) * BK * 2;  // B rows staged by this CTA
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = CG == 2 ? 6 : 4;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiSmem + 256;
 };
 
 }  // namespace gemm
@@ -184,6 +190,54 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
                : "memory");
 }
 
+// Warp-uniform issue: every lane of the MMA warp runs the loop, elect.sync
+// picks the issuing lane (the same lowest lane every time, so it also owns the
+// commits that track its MMAs), and descriptors stay in uniform registers.
+template <int CG>
+__device__ __forceinline__ void umma_elect(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  if constexpr (CG == 2) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    umma_bf16_ss_elect(tmem_d, adesc, bdesc, idesc, accumulate);
+  }
+}
+// Commit that arrives on `bar` in every CTA of the pair (CG = 2) or this CTA.
+template <int CG>
+__device__ __forceinline__ void commit_all_elect(uint64_t* bar) {
+  if constexpr (CG == 2) {
+    const uint16_t mask = 0x3;
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}\n" ::"r"(
+            smem_u32(bar)),
+        "h"(mask)
+        : "memory");
+  } else {
+    umma_commit_elect(bar);
+  }
+}
+// Commit that arrives on `bar` in this (leader) CTA only.
+template <int CG>
+__device__ __forceinline__ void commit_self_elect(uint64_t* bar) {
+  if constexpr (CG == 2) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(smem_u32(bar))
+        : "memory");
+  } else {
+    umma_commit_elect(bar);
+  }
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -191,28 +245,83 @@ __device__ __forceinline__ float ex2_approx(float x) {
 }
 
 // ---------------------------------------------------------------------------
-// Epilogue of one thread's row over the 32-column chunks [c_begin, c_end) of
-// the 256-column accumulator (TMEM address t_row: this warp's lane quarter,
-// accumulator base column).  Every thread of the warp calls this (tcgen05.ld
-// is warp-collective); rows past M only skip the stores.
+// Epilogue.  One thread owns one accumulator row (TMEM lane) and walks the
+// 32-column chunks [c_begin, c_end) of the 256-column tile; the warp stages
+// its 32 rows chunk by chunk in shared memory (128-byte rows, 128B swizzle,
+// conflict-free) and one lane writes each full slab with a TMA store (bf16:
+// 64 columns; fp32: 32 columns) or, when accumulating into D (beta, atomic
+// split-K), a TMA reduce-add.  Rows past M and columns past N are clipped by
+// the tensor map.  Every lane runs every step (tcgen05.ld, the staging and
+// the __syncwarp are warp-collective).
 // ---------------------------------------------------------------------------
+struct EpiStage {
+  uint8_t* base;  // this warp's slabs
+  int nbuf;       // 1 or 2
+  int ctr;        // slabs issued so far
+  int lane;
+};
+
+__device__ __forceinline__ uint8_t* slab_acquire(EpiStage& e) {
+  if (e.ctr >= e.nbuf) {
+    if (e.lane == 0) {
+      if (e.nbuf == 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+      else asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    }
+    __syncwarp();
+  }
+  return e.base + (e.ctr % e.nbuf) * kSlabBytes;
+}
+
+// mode 0: store, 1: reduce-add; dims 2 (x, y) or 3 (x, y, z).
+__device__ __forceinline__ void slab_issue(EpiStage& e, const CUtensorMap* map, const uint8_t* sb, int mode, int dims,
+                                           int x, int y, int z) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (e.lane == 0) {
+    const uint64_t m = reinterpret_cast<uint64_t>(map);
+    const uint32_t a = smem_u32(sb);
+    if (dims == 3) {
+      if (mode == 1)
+        asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];"
+                     ::"l"(m), "r"(a), "r"(x), "r"(y), "r"(z) : "memory");
+      else
+        asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+                     ::"l"(m), "r"(a), "r"(x), "r"(y), "r"(z) : "memory");
+    } else {
+      if (mode == 1)
+        asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];"
+                     ::"l"(m), "r"(a), "r"(x), "r"(y) : "memory");
+      else
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                     ::"l"(m), "r"(a), "r"(x), "r"(y) : "memory");
+    }
+    bulk_commit_group();
+  }
+  ++e.ctr;
+}
+
 template <int EPI>
-__device__ __forceinline__ void epilogue_row(const MdGemmParams& p, int row, int tn, int split, uint32_t t_row,
-                                             int c_begin, int c_end) {
+__device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtensorMap* tmD, EpiStage& es, int row,
+                                             int row0, int tn, int split, uint32_t t_row, int c_begin, int c_end) {
   const bool row_ok = row < p.M;
+  const int lane = es.lane;
   long long tgt = -1;
   if (EPI == kEpiCE && row_ok) tgt = p.ce_target[row] - p.ce_col_offset;
+  constexpr bool kF32 = EPI == kEpiF32;
+  const bool to_ws = kF32 && p.k_splits > 1 && p.workspace != nullptr;
+  const int f32_mode = (kF32 && !to_ws && (p.k_splits > 1 || p.beta)) ? 1 : 0;
+  uint8_t* sb = nullptr;
 #pragma unroll 1
   for (int slab = c_begin / 4; slab < c_end / 4; ++slab) {
     float ce_m = -INFINITY, ce_s = 0.f;
     bool ce_any = false;
 #pragma unroll 1
     for (int c = slab * 4; c < slab * 4 + 4; ++c) {
+      const int n0 = tn * BN + c * 32;
+      if (n0 >= p.N) break;  // warp-uniform: the rest of this tile lies past N
       uint32_t r[32];
       tmem_ld_32x32b_x32(t_row + c * 32, r);
       tmem_ld_wait();
-      const int n0 = tn * BN + c * 32;
-      if (!row_ok || n0 >= p.N) continue;
       const bool full = (n0 + 32 <= p.N);
       float v[32];
 #pragma unroll
@@ -224,29 +333,31 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, int row, int
           for (int j = 0; j < 32; ++j) v[j] += (n0 + j < p.N) ? p.bias[n0 + j] : 0.f;
         }
         if (p.gelu) {
-          __nv_bfloat16* aux = reinterpret_cast<__nv_bfloat16*>(p.aux) + row * p.ldaux + n0;
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
-          if (full) {
+          if (row_ok) {
+            __nv_bfloat16* aux = reinterpret_cast<__nv_bfloat16*>(p.aux) + row * p.ldaux + n0;
+            if (full) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 w;
-              w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-              w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-              w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-              w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-              reinterpret_cast<uint4*>(aux)[q] = w;
+              for (int q = 0; q < 4; ++q) {
+                uint4 w;
+                w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+                w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+                w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+                w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+                reinterpret_cast<uint4*>(aux)[q] = w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + j < p.N) aux[j] = __float2bfloat16_rn(v[j]);
             }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) aux[j] = __float2bfloat16_rn(v[j]);
           }
           // GELU of the bf16-rounded pre-activation: exactly what backward differentiates.
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
         }
-        if (p.resid != nullptr) {
+        if (p.resid != nullptr && row_ok) {
           const __nv_bfloat16* rs = reinterpret_cast<const __nv_bfloat16*>(p.resid) + row * p.ldres + n0;
           if (full) {
 #pragma unroll
@@ -264,112 +375,73 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, int row, int
           }
         }
       } else if (EPI == kEpiDGELU) {
-        const __nv_bfloat16* hx = reinterpret_cast<const __nv_bfloat16*>(p.aux) + row * p.ldaux + n0;
-        if (full) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 w = reinterpret_cast<const uint4*>(hx)[q];
-            float2 f0 = unpack_bf16x2(w.x), f1 = unpack_bf16x2(w.y), f2 = unpack_bf16x2(w.z),
-                   f3 = unpack_bf16x2(w.w);
-            v[q * 8 + 0] *= gelu_tanh_grad(f0.x); v[q * 8 + 1] *= gelu_tanh_grad(f0.y);
-            v[q * 8 + 2] *= gelu_tanh_grad(f1.x); v[q * 8 + 3] *= gelu_tanh_grad(f1.y);
-            v[q * 8 + 4] *= gelu_tanh_grad(f2.x); v[q * 8 + 5] *= gelu_tanh_grad(f2.y);
-            v[q * 8 + 6] *= gelu_tanh_grad(f3.x); v[q * 8 + 7] *= gelu_tanh_grad(f3.y);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + j < p.N) v[j] *= gelu_tanh_grad(__bfloat162float(hx[j]));
-        }
-      }
-
-      if (EPI == kEpiF32) {
-        float* dst;
-        bool add = false;
-        if (p.k_splits > 1 && p.workspace == nullptr) {
-          // Split-K by fp32 atomic accumulation straight into D (D was zeroed
-          // by the host unless accumulating).  Summation order varies run to
-          // run; the workspace path below is the deterministic alternative.
-          float* dd = reinterpret_cast<float*>(p.D) + row * p.ldd + n0;
+        if (row_ok) {
+          const __nv_bfloat16* hx = reinterpret_cast<const __nv_bfloat16*>(p.aux) + row * p.ldaux + n0;
           if (full) {
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dd + 4 * q), "f"(v[q * 4 + 0]),
-                           "f"(v[q * 4 + 1]), "f"(v[q * 4 + 2]), "f"(v[q * 4 + 3])
-                           : "memory");
+            for (int q = 0; q < 4; ++q) {
+              uint4 w = reinterpret_cast<const uint4*>(hx)[q];
+              float2 f0 = unpack_bf16x2(w.x), f1 = unpack_bf16x2(w.y), f2 = unpack_bf16x2(w.z),
+                     f3 = unpack_bf16x2(w.w);
+              v[q * 8 + 0] *= gelu_tanh_grad(f0.x); v[q * 8 + 1] *= gelu_tanh_grad(f0.y);
+              v[q * 8 + 2] *= gelu_tanh_grad(f1.x); v[q * 8 + 3] *= gelu_tanh_grad(f1.y);
+              v[q * 8 + 4] *= gelu_tanh_grad(f2.x); v[q * 8 + 5] *= gelu_tanh_grad(f2.y);
+              v[q * 8 + 6] *= gelu_tanh_grad(f3.x); v[q * 8 + 7] *= gelu_tanh_grad(f3.y);
+            }
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) atomicAdd(dd + j, v[j]);
+              if (n0 + j < p.N) v[j] *= gelu_tanh_grad(__bfloat162float(hx[j]));
           }
-          continue;
         }
-        if (p.k_splits > 1) {
-          dst = p.workspace + (static_cast<long long>(split) * p.M + row) * p.ldws + n0;
-        } else {
-          dst = reinterpret_cast<float*>(p.D) + row * p.ldd + n0;
-          add = p.beta != 0;
-        }
-        if (full) {
+      } else if (EPI == kEpiCE) {
+        // Statistics use the bf16-rounded logits the backward pass reads back.
+        constexpr float kLog2e = 1.4426950408889634f;
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            float4 w = make_float4(v[q * 4 + 0], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
-            if (add) {
-              float4 o = reinterpret_cast<const float4*>(dst)[q];
-              w.x += o.x; w.y += o.y; w.z += o.z; w.w += o.w;
-            }
-            reinterpret_cast<float4*>(dst)[q] = w;
-          }
-        } else {
+        for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
+        float cm = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (n0 + j < p.N) cm = fmaxf(cm, v[j]);
+        if (cm > ce_m) {
+          ce_s = ce_any ? ce_s * ex2_approx((ce_m - cm) * kLog2e) : 0.f;
+          ce_m = cm;
+        }
+        ce_any = true;
+        const float mb = ce_m * kLog2e;
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (n0 + j < p.N) s += ex2_approx(fmaf(v[j], kLog2e, -mb));
+        ce_s += s;
+        if (row_ok && tgt >= n0 && tgt < n0 + 32) {
+          float tv = 0.f;
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (n0 + j < p.N) dst[j] = add ? dst[j] + v[j] : v[j];
+            if (n0 + j == tgt) tv = v[j];
+          p.ce_tgt[row] = tv;
         }
+      }
+
+      // Stage and write out.
+      if (kF32) {
+        sb = slab_acquire(es);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(sb + sw128_off(lane, k))),
+                       "f"(v[4 * k]), "f"(v[4 * k + 1]), "f"(v[4 * k + 2]), "f"(v[4 * k + 3])
+                       : "memory");
+        slab_issue(es, tmD, sb, f32_mode, to_ws ? 3 : 2, n0, row0, split);
       } else {
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + n0;
-        if (EPI == kEpiCE) {
-          // Statistics use the bf16-rounded logits the backward pass reads back.
-          constexpr float kLog2e = 1.4426950408889634f;
+        if ((c & 1) == 0) sb = slab_acquire(es);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
-          float cm = -INFINITY;
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + j < p.N) cm = fmaxf(cm, v[j]);
-          if (cm > ce_m) {
-            ce_s = ce_any ? ce_s * ex2_approx((ce_m - cm) * kLog2e) : 0.f;
-            ce_m = cm;
-          }
-          ce_any = true;
-          const float mb = ce_m * kLog2e;
-          float s = 0.f;
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + j < p.N) s += ex2_approx(fmaf(v[j], kLog2e, -mb));
-          ce_s += s;
-          if (tgt >= n0 && tgt < n0 + 32) {
-            float tv = 0.f;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j == tgt) tv = v[j];
-            p.ce_tgt[row] = tv;
-          }
-        }
-        if (full) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 w;
-            w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-            w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-            w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-            w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-            reinterpret_cast<uint4*>(dst)[q] = w;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + j < p.N) dst[j] = __float2bfloat16_rn(v[j]);
-        }
+        for (int q = 0; q < 4; ++q)
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                           smem_u32(sb + sw128_off(lane, (c & 1) * 4 + q))),
+                       "r"(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1])), "r"(pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3])),
+                       "r"(pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5])), "r"(pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]))
+                       : "memory");
+        if ((c & 1) == 1 || n0 + 32 >= p.N) slab_issue(es, tmD, sb, 0, 2, n0 - (c & 1) * 32, row0, 0);
       }
     }
     if (EPI == kEpiCE && row_ok) {
@@ -388,14 +460,15 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, int row, int
 template <int CG, int EW, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(64 + 32 * EW, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ KParams kp) {
+                const __grid_constant__ CUtensorMap tmD, const __grid_constant__ KParams kp) {
   using C = Cfg<CG>;
   constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * C::kStageBytes);
+  uint8_t* sEpi = smem + kStages * C::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + kEpiSmem);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + kStages;
   uint64_t* tfull_bar = bars + 2 * kStages;
@@ -426,6 +499,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmD);
   }
   if (warp == 1) {
     if constexpr (CG == 2) {
@@ -505,10 +579,15 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     if (CG == 1 || leader)
       for (int s = 0; s < kStages; ++s)
         if (armed_phase[s] >= 0) mbar_wait(&full_bar[s], static_cast<uint32_t>(armed_phase[s]), p.status, 11, nullptr);
-  } else if (warp == 1 && lane == 0 && leader) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 && leader) {
+    // ------------------------------------------------------------ MMA issuer (whole warp, elected lane issues)
     constexpr uint32_t idesc = idesc_bf16_f32(CG * BM, BN, A_MN, B_MN);
     constexpr uint32_t kBChunkStride = 64 * BK * 2;
+    // Base descriptors of stage 0; stage s and k-step k are constant byte
+    // offsets, added as (offset >> 4).
+    const uint64_t a_base = A_MN ? sdesc_sw128(smem_u32(sA), kBChunkStride, 1024) : sdesc_sw128(smem_u32(sA), 16, 1024);
+    const uint64_t b_base =
+        B_MN ? sdesc_sw128(smem_u32(sB), kBChunkStride, 1024) : sdesc_sw128(smem_u32(sB), 16, 1024);
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
@@ -528,36 +607,30 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(sA + stage * kABytes);
-        const uint32_t b_addr = smem_u32(sB + stage * C::kBBytes);
+        const uint64_t a_st = a_base + static_cast<uint32_t>(stage * kABytes >> 4);
+        const uint64_t b_st = b_base + static_cast<uint32_t>(stage * C::kBBytes >> 4);
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k) {
-          const uint64_t adesc = A_MN ? sdesc_sw128(a_addr + k * 2048, kBChunkStride, 1024)
-                                      : sdesc_sw128(a_addr + k * 32, 16, 1024);
-          const uint64_t bdesc = B_MN ? sdesc_sw128(b_addr + k * 2048, kBChunkStride, 1024)
-                                      : sdesc_sw128(b_addr + k * 32, 16, 1024);
+          const uint32_t a_off = A_MN ? k * (2048 >> 4) : k * (32 >> 4);
+          const uint32_t b_off = B_MN ? k * (2048 >> 4) : k * (32 >> 4);
           const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
-          if constexpr (CG == 2) umma_bf16_ss_pair(d_tmem, adesc, bdesc, idesc, accum);
-          else umma_bf16_ss(d_tmem, adesc, bdesc, idesc, accum);
+          umma_elect<CG>(d_tmem, a_st + a_off, b_st + b_off, idesc, accum);
         }
-        if constexpr (CG == 2) umma_commit_pair_both(&empty_bar[stage]);
-        else umma_commit(&empty_bar[stage]);
+        commit_all_elect<CG>(&empty_bar[stage]);
         if (++stage == kStages) {
           stage = 0;
           phase ^= 1u;
         }
       }
       if (!ok) break;
-      if constexpr (CG == 2) umma_commit_pair_both(&tfull_bar[acc]);
-      else umma_commit(&tfull_bar[acc]);
+      commit_all_elect<CG>(&tfull_bar[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
-    // Drain: every MMA this thread issued completes before TMEM is released.
-    if constexpr (CG == 2) umma_commit_pair(drain_bar);
-    else umma_commit(drain_bar);
+    // Drain: every MMA this warp issued completes before TMEM is released.
+    commit_self_elect<CG>(drain_bar);
     mbar_wait(drain_bar, 0, p.status, 22, nullptr);
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
@@ -570,6 +643,11 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       tempty_addr[0] = map_to_cta(tempty_addr[0], 0);
       tempty_addr[1] = map_to_cta(tempty_addr[1], 0);
     }
+    EpiStage es;
+    es.nbuf = EW == 8 ? 1 : 2;
+    es.base = sEpi + ew * es.nbuf * kSlabBytes;
+    es.ctr = 0;
+    es.lane = lane;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int u = cluster_id; u < kp.units; u += nclusters) {
@@ -577,10 +655,10 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       decode_unit(kp, u, tm, tn, split);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, p.status, 30, abort_flag)) break;
       tc_fence_after();
-      const int row = tm * (CG * BM) + static_cast<int>(crank) * BM + quarter * 32 + lane;
+      const int row0 = tm * (CG * BM) + static_cast<int>(crank) * BM + quarter * 32;
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      epilogue_row<EPI>(p, row, tn, split, t_row, c_begin, c_end);
+      epilogue_row<EPI>(p, &tmD, es, row0 + lane, row0, tn, split, t_row, c_begin, c_end);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -592,6 +670,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
         acc_phase ^= 1u;
       }
     }
+    // Every bulk store / reduce-add of this warp has completed before exit.
+    if (lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -652,11 +732,27 @@ bool make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
   return r == CUDA_SUCCESS;
 }
 
+// Output map for the TMA-store epilogue: [depth, outer, inner] (depth 0 = 2-D)
+// with 128B swizzle and a box of 128 bytes x 32 rows (64 bf16 / 32 fp32).
+bool make_out_map(CUtensorMap* map, void* ptr, bool f32, uint64_t inner, uint64_t outer, uint64_t ld_elems,
+                  uint64_t depth) {
+  const uint64_t es = f32 ? 4 : 2;
+  cuuint64_t dims[3] = {inner, outer, depth};
+  cuuint64_t strides[2] = {ld_elems * es, ld_elems * es * outer};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / es), 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const cuuint32_t rank = depth > 0 ? 3 : 2;
+  CUresult r = g_encode(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, ptr, dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int g_num_sms = 0;
 
 template <int CG, int kEW, bool A_MN, bool B_MN, int EPI>
-cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const md::gemm::KParams& kp, int grid,
-                   cudaStream_t stream) {
+cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const md::gemm::KParams& kp,
+                   int grid, cudaStream_t stream) {
   auto kern = md::gemm::gemm_kernel<CG, kEW, A_MN, B_MN, EPI>;
   constexpr int smem = md::gemm::Cfg<CG>::kSmemBytes;
   static int attr_done[64] = {0};
@@ -686,28 +782,28 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const md::gemm:
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  return cudaLaunchKernelEx(&cfg, kern, ta, tb, kp);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, td, kp);
 }
 
 template <int CG, int EW>
-cudaError_t dispatch(bool amn, bool bmn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+cudaError_t dispatch(bool amn, bool bmn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
                      const md::gemm::KParams& kp, int grid, cudaStream_t s, bool* bad) {
   using namespace md::gemm;
   *bad = false;
   if (!amn && !bmn) {
-    if (epi == kEpiBF16) return launch<CG, EW, false, false, kEpiBF16>(ta, tb, kp, grid, s);
-    if (epi == kEpiF32) return launch<CG, EW, false, false, kEpiF32>(ta, tb, kp, grid, s);
-    if (epi == kEpiCE) return launch<CG, EW, false, false, kEpiCE>(ta, tb, kp, grid, s);
+    if (epi == kEpiBF16) return launch<CG, EW, false, false, kEpiBF16>(ta, tb, td, kp, grid, s);
+    if (epi == kEpiF32) return launch<CG, EW, false, false, kEpiF32>(ta, tb, td, kp, grid, s);
+    if (epi == kEpiCE) return launch<CG, EW, false, false, kEpiCE>(ta, tb, td, kp, grid, s);
   } else if (!amn && bmn) {
-    if (epi == kEpiBF16) return launch<CG, EW, false, true, kEpiBF16>(ta, tb, kp, grid, s);
-    if (epi == kEpiF32) return launch<CG, EW, false, true, kEpiF32>(ta, tb, kp, grid, s);
-    if (epi == kEpiDGELU) return launch<CG, EW, false, true, kEpiDGELU>(ta, tb, kp, grid, s);
+    if (epi == kEpiBF16) return launch<CG, EW, false, true, kEpiBF16>(ta, tb, td, kp, grid, s);
+    if (epi == kEpiF32) return launch<CG, EW, false, true, kEpiF32>(ta, tb, td, kp, grid, s);
+    if (epi == kEpiDGELU) return launch<CG, EW, false, true, kEpiDGELU>(ta, tb, td, kp, grid, s);
   } else if (amn && bmn) {
-    if (epi == kEpiF32) return launch<CG, EW, true, true, kEpiF32>(ta, tb, kp, grid, s);
-    if (epi == kEpiBF16) return launch<CG, EW, true, true, kEpiBF16>(ta, tb, kp, grid, s);
+    if (epi == kEpiF32) return launch<CG, EW, true, true, kEpiF32>(ta, tb, td, kp, grid, s);
+    if (epi == kEpiBF16) return launch<CG, EW, true, true, kEpiBF16>(ta, tb, td, kp, grid, s);
   } else {
-    if (epi == kEpiF32) return launch<CG, EW, true, false, kEpiF32>(ta, tb, kp, grid, s);
-    if (epi == kEpiBF16) return launch<CG, EW, true, false, kEpiBF16>(ta, tb, kp, grid, s);
+    if (epi == kEpiF32) return launch<CG, EW, true, false, kEpiF32>(ta, tb, td, kp, grid, s);
+    if (epi == kEpiBF16) return launch<CG, EW, true, false, kEpiBF16>(ta, tb, td, kp, grid, s);
   }
   *bad = true;
   return cudaSuccess;
@@ -774,6 +870,13 @@ extern "C" int md_gemm(const MdGemmParams* prm, cudaStream_t stream) {
   kp.p.k_splits = (kp.k_blocks + kp.kb_per_split - 1) / kp.kb_per_split;  // no empty split
   kp.units = kp.tiles_m * kp.tiles_n * kp.p.k_splits;
 
+  CUtensorMap td;
+  if (p.epi == kEpiF32 && kp.p.k_splits > 1 && p.workspace != nullptr)
+    ok = make_out_map(&td, p.workspace, true, p.N, p.M, p.ldws, kp.p.k_splits);
+  else
+    ok = make_out_map(&td, p.D, p.epi == kEpiF32, p.N, p.M, p.ldd, 0);
+  if (!ok) return -13;
+
   int cap = p.num_sms > 0 ? p.num_sms : g_num_sms;
   int grid;
   if (cg == 2) {
@@ -792,11 +895,11 @@ extern "C" int md_gemm(const MdGemmParams* prm, cudaStream_t stream) {
   const int ew = p.epi_warps == 4 ? 4 : 8;
   cudaError_t e;
   if (cg == 2) {
-    e = ew == 4 ? dispatch<2, 4>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, kp, grid, stream, &bad)
-                : dispatch<2, 8>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, kp, grid, stream, &bad);
+    e = ew == 4 ? dispatch<2, 4>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, td, kp, grid, stream, &bad)
+                : dispatch<2, 8>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, td, kp, grid, stream, &bad);
   } else {
-    e = ew == 4 ? dispatch<1, 4>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, kp, grid, stream, &bad)
-                : dispatch<1, 8>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, kp, grid, stream, &bad);
+    e = ew == 4 ? dispatch<1, 4>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, td, kp, grid, stream, &bad)
+                : dispatch<1, 8>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, td, kp, grid, stream, &bad);
   }
   if (bad) return -12;
   if (e != cudaSuccess) return static_cast<int>(e);
