@@ -108,6 +108,29 @@ struct MdGemmParams {
   int epi_warps;               // 0 = choose, 4 or 8
 };
 
+// Fused tensor-parallel all-reduce of the GEMM output (md_gemm_ar): the
+// epilogue writes this rank's partial tile (bf16) into its symmetric partial
+// buffer and publishes a per-chunk ready flag; comm warps reduce the chunks
+// this rank owns across all ranks (peer loads), add bias and residual once,
+// write the result to the local output and to this rank's symmetric final
+// buffer, publish a final flag, and copy every other chunk from its owner's
+// final buffer.  A chunk is 32 rows x one 256-column tile; owner = id % world.
+struct MdTpArParams {
+  void* partial[8];      // every rank's partial buffer (bf16, row stride ldp)
+  void* fin[8];          // every rank's final buffer (bf16, row stride ldp)
+  unsigned* flags[8];    // every rank's flag page: ready[max_chunks], final[max_chunks]
+  long long ldp;
+  void* out;             // this rank's output (bf16, row stride ldo)
+  long long ldo;
+  const float* bias;     // [N] or null, added after the reduction
+  const void* resid;     // bf16 [M, ldr] or null, added after the reduction
+  long long ldr;
+  int world, rank;
+  unsigned epoch;        // flags carry epochs; a call waits for >= epoch
+  int max_chunks;
+  unsigned long long timeout_ns;
+};
+
 namespace md {
 namespace gemm {
 
@@ -115,6 +138,7 @@ struct KParams {
   MdGemmParams p;
   int tiles_m;  // in units of CG*128 rows
   int tiles_n, units, k_blocks, kb_per_split;
+  MdTpArParams ar;
 };
 
 __device__ __forceinline__ void decode_unit(const KParams& kp, int u, int& tm, int& tn, int& split) {
@@ -455,10 +479,115 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
 }
 
 // ---------------------------------------------------------------------------
+// Peer flags for the fused all-reduce
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void flag_release_sys(unsigned* f, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned flag_acquire_sys(const unsigned* f) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+// Bounded wait until *f >= v (epochs only grow).  False on timeout / abort.
+__device__ __forceinline__ bool flag_wait_ge(const unsigned* f, unsigned v, const MdTpArParams& ar, Status* st,
+                                             uint32_t where, volatile int* abort_flag) {
+  if (flag_acquire_sys(f) >= v) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (flag_acquire_sys(f) >= v) return true;
+    if ((it & 15u) == 15u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > ar.timeout_ns) {
+        report(st, kTimeoutPeer, where, v);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// Comm warp, owned chunk: sum the 32 x 256 chunk over all ranks' partial
+// buffers (fixed rank order, so every rank's copy is bit-identical), add bias
+// and residual, write the local output and this rank's final buffer, publish.
+__device__ __forceinline__ bool ar_reduce_chunk(const MdGemmParams& p, const MdTpArParams& ar, int chunk, int row0,
+                                                int col0, int lane, volatile int* abort_flag) {
+  bool ok = true;
+  if (lane < ar.world) ok = flag_wait_ge(ar.flags[lane] + chunk, ar.epoch, ar, p.status, 60, abort_flag);
+  if (__any_sync(0xFFFFFFFFu, !ok)) return false;
+  const int col = col0 + lane * 8;
+  const bool col_ok = col < p.N;
+  float bias8[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) bias8[j] = (ar.bias != nullptr && col_ok) ? ar.bias[col + j] : 0.f;
+#pragma unroll 1
+  for (int i = 0; i < 32; ++i) {
+    const int row = row0 + i;
+    if (row >= p.M) break;
+    if (!col_ok) continue;
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = bias8[j];
+    for (int r = 0; r < ar.world; ++r) {
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ar.partial[r]) +
+                                                           row * ar.ldp + col));
+      const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), c = unpack_bf16x2(v.z), d = unpack_bf16x2(v.w);
+      acc[0] += a.x; acc[1] += a.y; acc[2] += b.x; acc[3] += b.y;
+      acc[4] += c.x; acc[5] += c.y; acc[6] += d.x; acc[7] += d.y;
+    }
+    if (ar.resid != nullptr) {
+      const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ar.resid) + row * ar.ldr + col);
+      const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), c = unpack_bf16x2(v.z), d = unpack_bf16x2(v.w);
+      acc[0] += a.x; acc[1] += a.y; acc[2] += b.x; acc[3] += b.y;
+      acc[4] += c.x; acc[5] += c.y; acc[6] += d.x; acc[7] += d.y;
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(ar.out) + row * ar.ldo + col) = o;
+    __stcg(reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(ar.fin[ar.rank]) + row * ar.ldp + col), o);
+  }
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence_system();
+    flag_release_sys(ar.flags[ar.rank] + ar.max_chunks + chunk, ar.epoch);
+  }
+  return true;
+}
+
+// Comm warp, chunk owned by `owner`: copy its final values into the output.
+// blocking = false returns false at once if the owner has not published yet.
+__device__ __forceinline__ int ar_pull_chunk(const MdGemmParams& p, const MdTpArParams& ar, int chunk, int owner,
+                                             int row0, int col0, int lane, bool blocking, volatile int* abort_flag) {
+  const unsigned* f = ar.flags[owner] + ar.max_chunks + chunk;
+  int ready = 0;
+  if (lane == 0) {
+    if (blocking) ready = flag_wait_ge(f, ar.epoch, ar, p.status, 61, abort_flag) ? 1 : -1;
+    else ready = flag_acquire_sys(f) >= ar.epoch ? 1 : 0;
+  }
+  ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
+  if (ready != 1) return ready;
+  const int col = col0 + lane * 8;
+  if (col < p.N) {
+    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(ar.fin[owner]);
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ar.out);
+#pragma unroll 4
+    for (int i = 0; i < 32; ++i) {
+      const int row = row0 + i;
+      if (row >= p.M) break;
+      *reinterpret_cast<uint4*>(dst + row * ar.ldo + col) = __ldcg(reinterpret_cast<const uint4*>(src + row * ar.ldp + col));
+    }
+  }
+  return 1;
+}
+
+// ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int CG, int EW, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(64 + 32 * EW, 1)
+template <int CG, int EW, bool A_MN, bool B_MN, int EPI, bool AR = false>
+__global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmD, const __grid_constant__ KParams kp) {
   using C = Cfg<CG>;
@@ -632,7 +761,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     // Drain: every MMA this warp issued completes before TMEM is released.
     commit_self_elect<CG>(drain_bar);
     mbar_wait(drain_bar, 0, p.status, 22, nullptr);
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && warp < 2 + EW) {
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 2;
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
@@ -659,6 +788,16 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       epilogue_row<EPI>(p, &tmD, es, row0 + lane, row0, tn, split, t_row, c_begin, c_end);
+      if constexpr (AR) {
+        // Publish this chunk of the partial product once its bulk stores have
+        // completed (bulk-async writes, then a proxy fence, then the release).
+        if (lane == 0 && row0 < p.M) {
+          bulk_wait_all();
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          __threadfence_system();
+          flag_release_sys(kp.ar.flags[kp.ar.rank] + (row0 >> 5) * kp.tiles_n + tn, kp.ar.epoch);
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -672,6 +811,44 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
     }
     // Every bulk store / reduce-add of this warp has completed before exit.
     if (lane == 0) bulk_wait_all();
+  } else if (AR && warp >= 2 + EW) {
+    // ------------------------------------------------------------ all-reduce (comm warps)
+    // Same tile walk as the epilogue; this warp covers the 32 rows of one
+    // lane quarter.  Owned chunks are reduced as soon as every rank has
+    // published its partial; the others are copied from their owners, first
+    // opportunistically in between, then (blocking) at the end.
+    const MdTpArParams& ar = kp.ar;
+    const int quarter = warp & 3;
+    int pull_u = cluster_id;  // next tile whose non-owned chunk still has to be copied
+    bool ok = true;
+    auto chunk_of = [&](int u, int& row0, int& col0, int& chunk) {
+      int tm, tn, split;
+      decode_unit(kp, u, tm, tn, split);
+      row0 = tm * (CG * BM) + static_cast<int>(crank) * BM + quarter * 32;
+      col0 = tn * BN;
+      chunk = (row0 >> 5) * kp.tiles_n + tn;
+    };
+    auto try_pulls = [&](int limit_u, bool blocking) {
+      while (ok && pull_u < limit_u) {
+        int row0, col0, chunk;
+        chunk_of(pull_u, row0, col0, chunk);
+        const int owner = chunk % ar.world;
+        if (row0 < p.M && owner != ar.rank) {
+          const int r = ar_pull_chunk(p, ar, chunk, owner, row0, col0, lane, blocking, abort_flag);
+          if (r < 0) ok = false;
+          if (r != 1) return;
+        }
+        pull_u += nclusters;
+      }
+    };
+    for (int u = cluster_id; u < kp.units && ok; u += nclusters) {
+      int row0, col0, chunk;
+      chunk_of(u, row0, col0, chunk);
+      if (row0 < p.M && chunk % ar.world == ar.rank)
+        ok = ar_reduce_chunk(p, ar, chunk, row0, col0, lane, abort_flag);
+      try_pulls(u + 1, false);
+    }
+    try_pulls(kp.units, true);
   }
 
   tc_fence_before();
@@ -750,10 +927,10 @@ bool make_out_map(CUtensorMap* map, void* ptr, bool f32, uint64_t inner, uint64_
 
 int g_num_sms = 0;
 
-template <int CG, int kEW, bool A_MN, bool B_MN, int EPI>
+template <int CG, int kEW, bool A_MN, bool B_MN, int EPI, bool AR = false>
 cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const md::gemm::KParams& kp,
                    int grid, cudaStream_t stream) {
-  auto kern = md::gemm::gemm_kernel<CG, kEW, A_MN, B_MN, EPI>;
+  auto kern = md::gemm::gemm_kernel<CG, kEW, A_MN, B_MN, EPI, AR>;
   constexpr int smem = md::gemm::Cfg<CG>::kSmemBytes;
   static int attr_done[64] = {0};
   int dev = 0;
@@ -769,7 +946,7 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(64 + 32 * kEW);
+  cfg.blockDim = dim3(64 + 32 * kEW + (AR ? 128 : 0));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -918,3 +1095,59 @@ extern "C" int md_gemm(const MdGemmParams* prm, cudaStream_t stream) {
 
 // Width of the column slabs the kEpiCE epilogue keeps statistics for.
 extern "C" int md_gemm_ce_slab() { return md::gemm::kCeSlab; }
+
+// GEMM + tensor-parallel all-reduce in one kernel (see MdTpArParams):
+// out = resid + bias + sum over ranks of (A_r B_r^T), bf16.  A and B K-major,
+// plain bf16 epilogue (alpha only) for the partials; prm->D is ignored (the
+// partial goes to ar->partial[ar->rank]).  Every rank of the group calls it
+// with the same shapes and epoch.
+extern "C" int md_gemm_ar(const MdGemmParams* prm, const MdTpArParams* arp, cudaStream_t stream) {
+  using namespace md::gemm;
+  if (prm == nullptr || arp == nullptr) return -1;
+  MdGemmParams p = *prm;
+  const MdTpArParams& ar = *arp;
+  if (p.M <= 0 || p.N <= 0 || p.K <= 0) return -2;
+  if (!get_encoder()) return -3;
+  if (!aligned16(p.A) || !aligned16(p.B) || (p.lda % 8) || (p.ldb % 8)) return -4;
+  if (p.a_mn_major || p.b_mn_major || p.epi != kEpiBF16 || p.gelu || p.bias || p.resid || p.k_splits > 1) return -5;
+  if (ar.world < 1 || ar.world > 8 || ar.rank < 0 || ar.rank >= ar.world || (ar.ldp % 8) || (ar.ldo % 8) ||
+      (p.N % 8) || !aligned16(ar.out) || (ar.resid != nullptr && (!aligned16(ar.resid) || (ar.ldr % 8))))
+    return -6;
+  p.D = ar.partial[ar.rank];
+  p.ldd = ar.ldp;
+  p.k_splits = 1;
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  int cg = p.cta_group;
+  if (cg != 1 && cg != 2) cg = p.M >= 512 ? 2 : 1;
+  CUtensorMap ta, tb, td;
+  if (!make_map(&ta, p.A, p.K, p.M, p.lda, BM)) return -10;
+  if (!make_map(&tb, p.B, p.K, p.N, p.ldb, BN / cg)) return -11;
+  if (!make_out_map(&td, p.D, false, p.N, p.M, p.ldd, 0)) return -13;
+  KParams kp;
+  kp.p = p;
+  kp.tiles_m = (p.M + cg * BM - 1) / (cg * BM);
+  kp.tiles_n = (p.N + BN - 1) / BN;
+  kp.k_blocks = (p.K + BK - 1) / BK;
+  kp.kb_per_split = kp.k_blocks;
+  kp.units = kp.tiles_m * kp.tiles_n;
+  kp.ar = ar;
+  if (((p.M + 31) / 32) * kp.tiles_n > ar.max_chunks) return -7;
+  if (kp.ar.timeout_ns == 0) kp.ar.timeout_ns = 10000000000ull;
+  // Every tile's CTA must be resident at once (comm warps wait on peers that
+  // wait on the same CTA index), so the grid never exceeds the SM count.
+  const int cap = p.num_sms > 0 ? p.num_sms : g_num_sms;
+  int grid;
+  if (cg == 2) {
+    const int clusters = kp.units < cap / 2 ? kp.units : cap / 2;
+    grid = 2 * (clusters > 0 ? clusters : 1);
+  } else {
+    grid = kp.units < cap ? kp.units : cap;
+  }
+  cudaError_t e = cg == 2 ? launch<2, 4, false, false, kEpiBF16, true>(ta, tb, td, kp, grid, stream)
+                          : launch<1, 4, false, false, kEpiBF16, true>(ta, tb, td, kp, grid, stream);
+  return static_cast<int>(e);
+}

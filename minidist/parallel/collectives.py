@@ -7,8 +7,9 @@
   all-gather over NVLink, csrc/symm.cu) on a side stream, ordered after the
   compute stream with CUDA events.  Launch order is bucket 0, 1, 2, ... on
   every rank, as with NCCL.
-* :func:`all_reduce_` / :func:`gemm_all_reduce` — tensor-parallel reductions;
-  NCCL for now.
+* :func:`gemm_all_reduce` — the row-parallel linear with its all-reduce fused
+  into the GEMM kernel (``md_gemm_ar``, peer memory); :func:`all_reduce_` —
+  NCCL all-reduce of a bf16 activation (gradient) for the other TP sites.
 
 Byte accounting goes to :data:`minidist.comm.comm_stats` with the same
 formulas as the NCCL path.
@@ -134,14 +135,96 @@ def all_reduce_(t: torch.Tensor, group) -> torch.Tensor:
     return t
 
 
+_TP_CHANNEL = 3
+
+
+class TpArParams(ctypes.Structure):
+    """Mirror of ``struct MdTpArParams`` (csrc/gemm_sm100.cu)."""
+
+    _fields_ = [
+        ("partial", ctypes.c_void_p * _MAXW),
+        ("fin", ctypes.c_void_p * _MAXW),
+        ("flags", ctypes.c_void_p * _MAXW),
+        ("ldp", ctypes.c_longlong),
+        ("out", ctypes.c_void_p),
+        ("ldo", ctypes.c_longlong),
+        ("bias", ctypes.c_void_p),
+        ("resid", ctypes.c_void_p),
+        ("ldr", ctypes.c_longlong),
+        ("world", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("epoch", ctypes.c_uint32),
+        ("max_chunks", ctypes.c_int),
+        ("timeout_ns", ctypes.c_ulonglong),
+    ]
+
+
+nat.declare("md_gemm_ar", "i:ppp")
+
+
+def _group_comm(group) -> symm.Communicator | None:
+    if not (torch.cuda.is_available() and comm.is_distributed()):
+        return None
+    ranks = list(range(comm.get_world_size())) if group is None else torch.distributed.get_process_group_ranks(group)
+    return symm.communicator(group, ranks)
+
+
+def _tp_fused_enabled() -> bool:
+    return os.environ.get("MINIDIST_TP_FUSED", "1") not in ("0", "false", "no")
+
+
 def gemm_all_reduce(x_local, w_local, bias, resid, group):
-    out = G.linear_fwd(x_local, w_local)
-    comm.all_reduce(out, group=group)
-    acc = out.float()
-    if bias is not None:
-        acc += bias
+    """``resid + bias + all_reduce(x_local @ w_local^T)`` (bf16) over the tensor-parallel group.
+
+    On the fused path this is one ``md_gemm_ar`` launch: the GEMM epilogue
+    publishes bf16 partial tiles into a symmetric buffer, and comm warps of the
+    same persistent kernel reduce the tiles this rank owns over NVLink (bias and
+    residual added once, as the reference adds the bias after the reduce,
+    tensor_parallel.py:354-368) and copy every other tile from its owner.
+    Otherwise: GEMM, NCCL all-reduce, then bias/residual.
+    """
+    M, K = x_local.shape
+    N = w_local.shape[0]
+    c = _group_comm(group) if _tp_fused_enabled() else None
+    if c is None or N % 8 or x_local.stride(1) != 1 or w_local.stride(1) != 1:
+        out = G.linear_fwd(x_local, w_local)
+        comm.all_reduce(out, group=group)
+        acc = out.float()
+        if bias is not None:
+            acc += bias
+        if resid is not None:
+            acc += resid.float()
+        res = G.empty_padded(out.shape[0], out.shape[1], device=out.device)
+        res.copy_(acc)
+        return res
+    ldp = N
+    chunks = (M + 31) // 32 * ((N + 255) // 256)
+    part = c.buffer("tp_partial", M * ldp * 2)
+    fin = c.buffer("tp_final", M * ldp * 2)
+    flags = c.zeroed_buffer("tp_flags", 2 * chunks * 4)
+    out = G.empty_padded(M, N, device=x_local.device)
+    ar = TpArParams()
+    for r in range(c.world):
+        ar.partial[r] = part.ptrs[r]
+        ar.fin[r] = fin.ptrs[r]
+        ar.flags[r] = flags.ptrs[r]
+    ar.ldp = ldp
+    ar.out, ar.ldo = out.data_ptr(), out.stride(0)
+    ar.bias = None if bias is None else bias.data_ptr()
     if resid is not None:
-        acc += resid.float()
-    res = G.empty_padded(out.shape[0], out.shape[1], device=out.device)
-    res.copy_(acc)
-    return res
+        ar.resid, ar.ldr = resid.data_ptr(), resid.stride(0)
+    ar.world, ar.rank = c.world, c.rank
+    ar.epoch = c.next_epoch(_TP_CHANNEL)
+    ar.max_chunks = flags.nbytes // 8
+    ar.timeout_ns = _timeout_ns()
+    p = nat.GemmParams()
+    p.A, p.B = x_local.data_ptr(), w_local.data_ptr()
+    p.lda, p.ldb = x_local.stride(0), w_local.stride(0)
+    p.M, p.N, p.K = M, N, K
+    p.epi = G.EPI_BF16
+    p.alpha = 1.0
+    p.status = nat.status_ptr(x_local.device)
+    rc = nat.lib().md_gemm_ar(ctypes.byref(p), ctypes.byref(ar), ctypes.c_void_p(nat.stream_ptr(None)))
+    nat.check(rc, f"md_gemm_ar(M={M},N={N},K={K})")
+    comm.comm_stats.add("all_reduce", M * N * 2, int(2 * (c.world - 1) / c.world * M * N * 2))
+    return out

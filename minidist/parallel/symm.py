@@ -129,6 +129,18 @@ class Communicator:
         self.epochs[channel] += 1
         return self.epochs[channel]
 
+    def zeroed_buffer(self, name: str, nbytes: int) -> SymmBuffer:
+        """Like :meth:`buffer`, but a new allocation is zero-filled on every rank before any
+        rank can use it (flag pages whose epochs must start below 1)."""
+        b = self.scratch.get(name)
+        if b is not None and b.nbytes >= nbytes:
+            return b
+        b = self.buffer(name, nbytes)
+        b.view(torch.uint8, 0, b.nbytes).zero_()
+        torch.cuda.synchronize(b.device)
+        dist.barrier(group=self.group)
+        return b
+
     def buffer(self, name: str, nbytes: int) -> SymmBuffer:
         """A named symmetric buffer of at least ``nbytes`` (collective on first use / growth)."""
         b = self.scratch.get(name)

@@ -1,4 +1,5 @@
-"""Multi-GPU tier: peer-memory collectives and DDP on 2+ GPUs (skipped with fewer GPUs).
+"""Multi-GPU tier: peer-memory collectives, the fused GEMM + all-reduce, DDP and tensor-parallel
+GPT on 2+ GPUs (skipped with fewer GPUs).
 
 Each test launches ``torchrun`` with one process per GPU (NCCL, 127.0.0.1) on a
 worker script in this directory and checks its exit code; the workers assert
@@ -24,7 +25,7 @@ def _ngpus() -> int:
 
 
 def _torchrun(script: str, n: int, *args: str, timeout: int = 300) -> None:
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=os.path.dirname(HERE))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MINIDIST_PEER_TIMEOUT_S="20", PYTHONPATH=os.path.dirname(HERE))
     cmd = ["timeout", "-k", "30", str(timeout), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={n}", "--master-addr=127.0.0.1", "--master-port=29533",
            os.path.join(HERE, script), *args]
