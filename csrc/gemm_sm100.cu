@@ -129,6 +129,7 @@ struct MdTpArParams {
   unsigned epoch;        // flags carry epochs; a call waits for >= epoch
   int max_chunks;
   unsigned long long timeout_ns;
+  unsigned long long* trace;  // optional analysis trace ([64][8] %globaltimer stamps of CTA 0), or null
 };
 
 namespace md {
@@ -478,24 +479,45 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
   }
 }
 
+// Analysis trace of the fused all-reduce: CTA 0 stamps %globaltimer at its
+// hand-offs (no-op unless a trace buffer is passed).
+#define MD_AR_TRACE(ar, idx, slot)                                                          \
+  do {                                                                                      \
+    if ((ar).trace != nullptr && blockIdx.x == 0 && (idx) < 64) (ar).trace[(idx) * 8 + (slot)] = globaltimer_ns(); \
+  } while (0)
+
 // ---------------------------------------------------------------------------
 // Peer flags for the fused all-reduce
 // ---------------------------------------------------------------------------
+// Publishing protocol.  Everything a flag publishes (the partial tile, the
+// final chunk) and the flag itself live in the publishing GPU's own memory, and
+// peers read both over NVLink through that GPU's L2.  The writer therefore
+// releases at GPU scope (a system-scope release costs ~10 us here while the
+// SM has NVLink traffic in flight); the reader polls the peer flag with
+// relaxed system-scope loads and, once it has seen the epoch, orders its
+// subsequent loads after that observation with an acquire fence.
 __device__ __forceinline__ void flag_release_sys(unsigned* f, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
 }
 __device__ __forceinline__ unsigned flag_acquire_sys(const unsigned* f) {
   unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
   return v;
 }
+__device__ __forceinline__ void acquire_fence() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 // Bounded wait until *f >= v (epochs only grow).  False on timeout / abort.
 __device__ __forceinline__ bool flag_wait_ge(const unsigned* f, unsigned v, const MdTpArParams& ar, Status* st,
                                              uint32_t where, volatile int* abort_flag) {
-  if (flag_acquire_sys(f) >= v) return true;
+  if (flag_acquire_sys(f) >= v) {
+    acquire_fence();
+    return true;
+  }
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 0;; ++it) {
-    if (flag_acquire_sys(f) >= v) return true;
+    if (flag_acquire_sys(f) >= v) {
+      acquire_fence();
+      return true;
+    }
     if ((it & 15u) == 15u) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > ar.timeout_ns) {
@@ -510,50 +532,85 @@ __device__ __forceinline__ bool flag_wait_ge(const unsigned* f, unsigned v, cons
 // Comm warp, owned chunk: sum the 32 x 256 chunk over all ranks' partial
 // buffers (fixed rank order, so every rank's copy is bit-identical), add bias
 // and residual, write the local output and this rank's final buffer, publish.
+// Lane l covers columns [8l, 8l+8) of the tile; each step issues the peer
+// loads of 16 / W rows for all W ranks at once (16 loads in flight per lane).
+template <int W>
+__device__ __forceinline__ void ar_reduce_rows(const MdGemmParams& p, const MdTpArParams& ar, int row0, int col,
+                                               const float (&bias8)[8]) {
+  constexpr int R = 16 / W;  // rows per step
+#pragma unroll 1
+  for (int i0 = 0; i0 < 32; i0 += R) {
+    bool rv[R];
+#pragma unroll
+    for (int k = 0; k < R; ++k) rv[k] = row0 + i0 + k < p.M;
+    uint4 v[R][W];
+#pragma unroll
+    for (int k = 0; k < R; ++k)
+#pragma unroll
+      for (int r = 0; r < W; ++r)
+        v[k][r] = rv[k] ? __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ar.partial[r]) +
+                                                               (row0 + i0 + k) * ar.ldp + col))
+                        : make_uint4(0, 0, 0, 0);
+    uint4 rs[R];
+#pragma unroll
+    for (int k = 0; k < R; ++k)
+      rs[k] = (ar.resid != nullptr && rv[k])
+                  ? *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ar.resid) +
+                                                    (row0 + i0 + k) * ar.ldr + col)
+                  : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      if (!rv[k]) continue;
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = bias8[j];
+#pragma unroll
+      for (int r = 0; r < W; ++r) {
+        const float2 a = unpack_bf16x2(v[k][r].x), b = unpack_bf16x2(v[k][r].y), c = unpack_bf16x2(v[k][r].z),
+                     d = unpack_bf16x2(v[k][r].w);
+        acc[0] += a.x; acc[1] += a.y; acc[2] += b.x; acc[3] += b.y;
+        acc[4] += c.x; acc[5] += c.y; acc[6] += d.x; acc[7] += d.y;
+      }
+      {
+        const float2 a = unpack_bf16x2(rs[k].x), b = unpack_bf16x2(rs[k].y), c = unpack_bf16x2(rs[k].z),
+                     d = unpack_bf16x2(rs[k].w);
+        acc[0] += a.x; acc[1] += a.y; acc[2] += b.x; acc[3] += b.y;
+        acc[4] += c.x; acc[5] += c.y; acc[6] += d.x; acc[7] += d.y;
+      }
+      const long long row = row0 + i0 + k;
+      uint4 o;
+      o.x = pack_bf16x2(acc[0], acc[1]);
+      o.y = pack_bf16x2(acc[2], acc[3]);
+      o.z = pack_bf16x2(acc[4], acc[5]);
+      o.w = pack_bf16x2(acc[6], acc[7]);
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(ar.out) + row * ar.ldo + col) = o;
+      __stcg(reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(ar.fin[ar.rank]) + row * ar.ldp + col), o);
+    }
+  }
+}
+
 __device__ __forceinline__ bool ar_reduce_chunk(const MdGemmParams& p, const MdTpArParams& ar, int chunk, int row0,
                                                 int col0, int lane, volatile int* abort_flag) {
   bool ok = true;
   if (lane < ar.world) ok = flag_wait_ge(ar.flags[lane] + chunk, ar.epoch, ar, p.status, 60, abort_flag);
   if (__any_sync(0xFFFFFFFFu, !ok)) return false;
+  acquire_fence();  // every lane's loads below follow the lanes' observations (ordered by the vote)
   const int col = col0 + lane * 8;
-  const bool col_ok = col < p.N;
-  float bias8[8];
+  if (col < p.N) {
+    float bias8[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) bias8[j] = (ar.bias != nullptr && col_ok) ? ar.bias[col + j] : 0.f;
-#pragma unroll 1
-  for (int i = 0; i < 32; ++i) {
-    const int row = row0 + i;
-    if (row >= p.M) break;
-    if (!col_ok) continue;
-    float acc[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = bias8[j];
-    for (int r = 0; r < ar.world; ++r) {
-      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ar.partial[r]) +
-                                                           row * ar.ldp + col));
-      const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), c = unpack_bf16x2(v.z), d = unpack_bf16x2(v.w);
-      acc[0] += a.x; acc[1] += a.y; acc[2] += b.x; acc[3] += b.y;
-      acc[4] += c.x; acc[5] += c.y; acc[6] += d.x; acc[7] += d.y;
+    for (int j = 0; j < 8; ++j) bias8[j] = ar.bias != nullptr ? ar.bias[col + j] : 0.f;
+    switch (ar.world) {
+      case 1: ar_reduce_rows<1>(p, ar, row0, col, bias8); break;
+      case 2: ar_reduce_rows<2>(p, ar, row0, col, bias8); break;
+      case 4: ar_reduce_rows<4>(p, ar, row0, col, bias8); break;
+      default: ar_reduce_rows<8>(p, ar, row0, col, bias8); break;  // md_gemm_ar admits 1, 2, 4, 8 only
     }
-    if (ar.resid != nullptr) {
-      const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ar.resid) + row * ar.ldr + col);
-      const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), c = unpack_bf16x2(v.z), d = unpack_bf16x2(v.w);
-      acc[0] += a.x; acc[1] += a.y; acc[2] += b.x; acc[3] += b.y;
-      acc[4] += c.x; acc[5] += c.y; acc[6] += d.x; acc[7] += d.y;
-    }
-    uint4 o;
-    o.x = pack_bf16x2(acc[0], acc[1]);
-    o.y = pack_bf16x2(acc[2], acc[3]);
-    o.z = pack_bf16x2(acc[4], acc[5]);
-    o.w = pack_bf16x2(acc[6], acc[7]);
-    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(ar.out) + row * ar.ldo + col) = o;
-    __stcg(reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(ar.fin[ar.rank]) + row * ar.ldp + col), o);
   }
+  // __syncwarp orders every lane's stores before lane 0's release (which is
+  // cumulative), so one release store publishes the whole chunk.
   __syncwarp();
-  if (lane == 0) {
-    __threadfence_system();
-    flag_release_sys(ar.flags[ar.rank] + ar.max_chunks + chunk, ar.epoch);
-  }
+  if (lane == 0) flag_release_sys(ar.flags[ar.rank] + ar.max_chunks + chunk, ar.epoch);
   return true;
 }
 
@@ -568,16 +625,26 @@ __device__ __forceinline__ int ar_pull_chunk(const MdGemmParams& p, const MdTpAr
     else ready = flag_acquire_sys(f) >= ar.epoch ? 1 : 0;
   }
   ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
+  if (ready == 1) acquire_fence();  // every lane's loads below follow the observation
   if (ready != 1) return ready;
   const int col = col0 + lane * 8;
   if (col < p.N) {
     const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(ar.fin[owner]);
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ar.out);
-#pragma unroll 4
-    for (int i = 0; i < 32; ++i) {
-      const int row = row0 + i;
-      if (row >= p.M) break;
-      *reinterpret_cast<uint4*>(dst + row * ar.ldo + col) = __ldcg(reinterpret_cast<const uint4*>(src + row * ar.ldp + col));
+    // Sixteen rows of peer loads in flight per step.
+#pragma unroll 1
+    for (int i0 = 0; i0 < 32; i0 += 16) {
+      uint4 v[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const long long row = row0 + i0 + k;
+        v[k] = row < p.M ? __ldcg(reinterpret_cast<const uint4*>(src + row * ar.ldp + col)) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const long long row = row0 + i0 + k;
+        if (row < p.M) *reinterpret_cast<uint4*>(dst + row * ar.ldo + col) = v[k];
+      }
     }
   }
   return 1;
@@ -792,10 +859,16 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
         // Publish this chunk of the partial product once its bulk stores have
         // completed (bulk-async writes, then a proxy fence, then the release).
         if (lane == 0 && row0 < p.M) {
+          const int ti = (u - cluster_id) / nclusters;
+          if (quarter == 0) MD_AR_TRACE(kp.ar, ti, 0);
           bulk_wait_all();
+          if (quarter == 0) MD_AR_TRACE(kp.ar, ti, 7);
+          // The completed bulk writes are ordered before the release by the
+          // proxy fence; the release store itself publishes them system-wide.
           asm volatile("fence.proxy.async.global;" ::: "memory");
-          __threadfence_system();
+          if (quarter == 0) MD_AR_TRACE(kp.ar, ti, 6);
           flag_release_sys(kp.ar.flags[kp.ar.rank] + (row0 >> 5) * kp.tiles_n + tn, kp.ar.epoch);
+          if (quarter == 0) MD_AR_TRACE(kp.ar, ti, 1);
         }
       }
       tc_fence_before();
@@ -844,11 +917,18 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
     for (int u = cluster_id; u < kp.units && ok; u += nclusters) {
       int row0, col0, chunk;
       chunk_of(u, row0, col0, chunk);
-      if (row0 < p.M && chunk % ar.world == ar.rank)
+      const int ti = (u - cluster_id) / nclusters;
+      if (quarter == 0 && lane == 0) MD_AR_TRACE(ar, ti, 2);
+      if (row0 < p.M && chunk % ar.world == ar.rank) {
         ok = ar_reduce_chunk(p, ar, chunk, row0, col0, lane, abort_flag);
+        if (quarter == 0 && lane == 0) MD_AR_TRACE(ar, ti, 3);
+      }
       try_pulls(u + 1, false);
+      if (quarter == 0 && lane == 0) MD_AR_TRACE(ar, ti, 4);
     }
+    if (quarter == 0 && lane == 0) MD_AR_TRACE(ar, 63, 5);
     try_pulls(kp.units, true);
+    if (quarter == 0 && lane == 0) MD_AR_TRACE(ar, 63, 6);
   }
 
   tc_fence_before();
@@ -1101,6 +1181,8 @@ extern "C" int md_gemm_ce_slab() { return md::gemm::kCeSlab; }
 // plain bf16 epilogue (alpha only) for the partials; prm->D is ignored (the
 // partial goes to ar->partial[ar->rank]).  Every rank of the group calls it
 // with the same shapes and epoch.
+static unsigned long long* g_ar_trace = nullptr;  // analysis trace buffer (md_gemm_ar_trace_enable)
+
 extern "C" int md_gemm_ar(const MdGemmParams* prm, const MdTpArParams* arp, cudaStream_t stream) {
   using namespace md::gemm;
   if (prm == nullptr || arp == nullptr) return -1;
@@ -1110,7 +1192,8 @@ extern "C" int md_gemm_ar(const MdGemmParams* prm, const MdTpArParams* arp, cuda
   if (!get_encoder()) return -3;
   if (!aligned16(p.A) || !aligned16(p.B) || (p.lda % 8) || (p.ldb % 8)) return -4;
   if (p.a_mn_major || p.b_mn_major || p.epi != kEpiBF16 || p.gelu || p.bias || p.resid || p.k_splits > 1) return -5;
-  if (ar.world < 1 || ar.world > 8 || ar.rank < 0 || ar.rank >= ar.world || (ar.ldp % 8) || (ar.ldo % 8) ||
+  if ((ar.world != 1 && ar.world != 2 && ar.world != 4 && ar.world != 8) || ar.rank < 0 || ar.rank >= ar.world ||
+      (ar.ldp % 8) || (ar.ldo % 8) ||
       (p.N % 8) || !aligned16(ar.out) || (ar.resid != nullptr && (!aligned16(ar.resid) || (ar.ldr % 8))))
     return -6;
   p.D = ar.partial[ar.rank];
@@ -1135,6 +1218,7 @@ extern "C" int md_gemm_ar(const MdGemmParams* prm, const MdTpArParams* arp, cuda
   kp.kb_per_split = kp.k_blocks;
   kp.units = kp.tiles_m * kp.tiles_n;
   kp.ar = ar;
+  kp.ar.trace = g_ar_trace;
   if (((p.M + 31) / 32) * kp.tiles_n > ar.max_chunks) return -7;
   if (kp.ar.timeout_ns == 0) kp.ar.timeout_ns = 10000000000ull;
   // Every tile's CTA must be resident at once (comm warps wait on peers that
@@ -1150,4 +1234,21 @@ extern "C" int md_gemm_ar(const MdGemmParams* prm, const MdTpArParams* arp, cuda
   cudaError_t e = cg == 2 ? launch<2, 4, false, false, kEpiBF16, true>(ta, tb, td, kp, grid, stream)
                           : launch<1, 4, false, false, kEpiBF16, true>(ta, tb, td, kp, grid, stream);
   return static_cast<int>(e);
+}
+
+// Analysis: allocate (enable=1) / free (enable=0) the md_gemm_ar trace buffer;
+// md_gemm_ar_trace_read copies its [64][8] stamps to host memory.
+extern "C" int md_gemm_ar_trace_enable(int enable) {
+  if (enable && g_ar_trace == nullptr) {
+    if (cudaMalloc(&g_ar_trace, 64 * 8 * 8) != cudaSuccess) return -1;
+    cudaMemset(g_ar_trace, 0, 64 * 8 * 8);
+  } else if (!enable && g_ar_trace != nullptr) {
+    cudaFree(g_ar_trace);
+    g_ar_trace = nullptr;
+  }
+  return 0;
+}
+extern "C" int md_gemm_ar_trace_read(unsigned long long* host) {
+  if (g_ar_trace == nullptr) return -1;
+  return static_cast<int>(cudaMemcpy(host, g_ar_trace, 64 * 8 * 8, cudaMemcpyDeviceToHost));
 }

@@ -156,10 +156,25 @@ class TpArParams(ctypes.Structure):
         ("epoch", ctypes.c_uint32),
         ("max_chunks", ctypes.c_int),
         ("timeout_ns", ctypes.c_ulonglong),
+        ("trace", ctypes.c_void_p),
     ]
 
 
 nat.declare("md_gemm_ar", "i:ppp")
+_AR_CACHE: dict[int, tuple] = {}
+
+
+class _LazyFn:
+    def __init__(self, name):
+        self.name, self.fn = name, None
+
+    def __call__(self, *a):
+        if self.fn is None:
+            self.fn = getattr(nat.lib(), self.name)
+        return self.fn(*a)
+
+
+_LIB_GEMM_AR = _LazyFn("md_gemm_ar")
 
 
 def _group_comm(group) -> symm.Communicator | None:
@@ -186,7 +201,7 @@ def gemm_all_reduce(x_local, w_local, bias, resid, group):
     M, K = x_local.shape
     N = w_local.shape[0]
     c = _group_comm(group) if _tp_fused_enabled() else None
-    if c is None or N % 8 or x_local.stride(1) != 1 or w_local.stride(1) != 1:
+    if c is None or c.world not in (2, 4, 8) or N % 8 or x_local.stride(1) != 1 or w_local.stride(1) != 1:
         out = G.linear_fwd(x_local, w_local)
         comm.all_reduce(out, group=group)
         acc = out.float()
@@ -203,28 +218,38 @@ def gemm_all_reduce(x_local, w_local, bias, resid, group):
     fin = c.buffer("tp_final", M * ldp * 2)
     flags = c.zeroed_buffer("tp_flags", 2 * chunks * 4)
     out = G.empty_padded(M, N, device=x_local.device)
-    ar = TpArParams()
-    for r in range(c.world):
-        ar.partial[r] = part.ptrs[r]
-        ar.fin[r] = fin.ptrs[r]
-        ar.flags[r] = flags.ptrs[r]
-    ar.ldp = ldp
+    # The parameter structs are built once per (buffers, shape) and patched per call.
+    key = (id(part), id(fin), id(flags), M, N, K)
+    st = _AR_CACHE.get(id(c))
+    if st is None or st[0] != key:
+        ar = TpArParams()
+        for r in range(c.world):
+            ar.partial[r] = part.ptrs[r]
+            ar.fin[r] = fin.ptrs[r]
+            ar.flags[r] = flags.ptrs[r]
+        ar.ldp = ldp
+        ar.world, ar.rank = c.world, c.rank
+        ar.max_chunks = flags.nbytes // 8
+        ar.timeout_ns = _timeout_ns()
+        gp = nat.GemmParams()
+        gp.M, gp.N, gp.K = M, N, K
+        gp.epi = G.EPI_BF16
+        gp.alpha = 1.0
+        gp.status = nat.status_ptr(x_local.device)
+        st = (key, ar, gp, ctypes.byref(gp), ctypes.byref(ar))
+        _AR_CACHE[id(c)] = st
+    _, ar, gp, gp_ref, ar_ref = st
     ar.out, ar.ldo = out.data_ptr(), out.stride(0)
     ar.bias = None if bias is None else bias.data_ptr()
     if resid is not None:
         ar.resid, ar.ldr = resid.data_ptr(), resid.stride(0)
-    ar.world, ar.rank = c.world, c.rank
+    else:
+        ar.resid = None
     ar.epoch = c.next_epoch(_TP_CHANNEL)
-    ar.max_chunks = flags.nbytes // 8
-    ar.timeout_ns = _timeout_ns()
-    p = nat.GemmParams()
-    p.A, p.B = x_local.data_ptr(), w_local.data_ptr()
-    p.lda, p.ldb = x_local.stride(0), w_local.stride(0)
-    p.M, p.N, p.K = M, N, K
-    p.epi = G.EPI_BF16
-    p.alpha = 1.0
-    p.status = nat.status_ptr(x_local.device)
-    rc = nat.lib().md_gemm_ar(ctypes.byref(p), ctypes.byref(ar), ctypes.c_void_p(nat.stream_ptr(None)))
-    nat.check(rc, f"md_gemm_ar(M={M},N={N},K={K})")
+    gp.A, gp.B = x_local.data_ptr(), w_local.data_ptr()
+    gp.lda, gp.ldb = x_local.stride(0), w_local.stride(0)
+    rc = _LIB_GEMM_AR(gp_ref, ar_ref, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    if rc != 0:
+        nat.check(rc, f"md_gemm_ar(M={M},N={N},K={K})")
     comm.comm_stats.add("all_reduce", M * N * 2, int(2 * (c.world - 1) / c.world * M * N * 2))
     return out
