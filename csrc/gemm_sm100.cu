@@ -1177,8 +1177,9 @@ extern "C" int md_gemm(const MdGemmParams* prm, cudaStream_t stream) {
 extern "C" int md_gemm_ce_slab() { return md::gemm::kCeSlab; }
 
 // GEMM + tensor-parallel all-reduce in one kernel (see MdTpArParams):
-// out = resid + bias + sum over ranks of (A_r B_r^T), bf16.  A and B K-major,
-// plain bf16 epilogue (alpha only) for the partials; prm->D is ignored (the
+// out = resid + bias + sum over ranks of (A_r B_r^T), bf16.  A K-major, B
+// K-major (forward) or MN-major (data gradient, dx = dy W); plain bf16
+// epilogue (alpha only) for the partials; prm->D is ignored (the
 // partial goes to ar->partial[ar->rank]).  Every rank of the group calls it
 // with the same shapes and epoch.
 static unsigned long long* g_ar_trace = nullptr;  // analysis trace buffer (md_gemm_ar_trace_enable)
@@ -1191,7 +1192,7 @@ extern "C" int md_gemm_ar(const MdGemmParams* prm, const MdTpArParams* arp, cuda
   if (p.M <= 0 || p.N <= 0 || p.K <= 0) return -2;
   if (!get_encoder()) return -3;
   if (!aligned16(p.A) || !aligned16(p.B) || (p.lda % 8) || (p.ldb % 8)) return -4;
-  if (p.a_mn_major || p.b_mn_major || p.epi != kEpiBF16 || p.gelu || p.bias || p.resid || p.k_splits > 1) return -5;
+  if (p.a_mn_major || p.epi != kEpiBF16 || p.gelu || p.bias || p.resid || p.k_splits > 1) return -5;
   if ((ar.world != 1 && ar.world != 2 && ar.world != 4 && ar.world != 8) || ar.rank < 0 || ar.rank >= ar.world ||
       (ar.ldp % 8) || (ar.ldo % 8) ||
       (p.N % 8) || !aligned16(ar.out) || (ar.resid != nullptr && (!aligned16(ar.resid) || (ar.ldr % 8))))
@@ -1208,7 +1209,11 @@ extern "C" int md_gemm_ar(const MdGemmParams* prm, const MdTpArParams* arp, cuda
   if (cg != 1 && cg != 2) cg = p.M >= 512 ? 2 : 1;
   CUtensorMap ta, tb, td;
   if (!make_map(&ta, p.A, p.K, p.M, p.lda, BM)) return -10;
-  if (!make_map(&tb, p.B, p.K, p.N, p.ldb, BN / cg)) return -11;
+  if (!p.b_mn_major) {
+    if (!make_map(&tb, p.B, p.K, p.N, p.ldb, BN / cg)) return -11;
+  } else if (!make_map(&tb, p.B, p.N, p.K, p.ldb, 64)) {
+    return -11;
+  }
   if (!make_out_map(&td, p.D, false, p.N, p.M, p.ldd, 0)) return -13;
   KParams kp;
   kp.p = p;
@@ -1231,8 +1236,13 @@ extern "C" int md_gemm_ar(const MdGemmParams* prm, const MdTpArParams* arp, cuda
   } else {
     grid = kp.units < cap ? kp.units : cap;
   }
-  cudaError_t e = cg == 2 ? launch<2, 4, false, false, kEpiBF16, true>(ta, tb, td, kp, grid, stream)
-                          : launch<1, 4, false, false, kEpiBF16, true>(ta, tb, td, kp, grid, stream);
+  cudaError_t e;
+  if (p.b_mn_major)  // data-gradient products: dx = dy W
+    e = cg == 2 ? launch<2, 4, false, true, kEpiBF16, true>(ta, tb, td, kp, grid, stream)
+                : launch<1, 4, false, true, kEpiBF16, true>(ta, tb, td, kp, grid, stream);
+  else
+    e = cg == 2 ? launch<2, 4, false, false, kEpiBF16, true>(ta, tb, td, kp, grid, stream)
+                : launch<1, 4, false, false, kEpiBF16, true>(ta, tb, td, kp, grid, stream);
   return static_cast<int>(e);
 }
 

@@ -124,6 +124,15 @@ def _tp_world(group) -> int:
     return comm.get_world_size(group)
 
 
+def _dgrad_all_reduce(dy: torch.Tensor, w: torch.Tensor, group) -> torch.Tensor:
+    """``dy @ w`` summed over the tensor-parallel group (one fused kernel when tp > 1)."""
+    if _tp_world(group) == 1:
+        return G.linear_dgrad(dy, w)
+    from ..parallel import collectives
+
+    return collectives.dgrad_all_reduce(dy, w, group)
+
+
 def _all_reduce_(t: torch.Tensor, group) -> torch.Tensor:
     """Sum ``t`` over the TP group in place (fused NVLink kernel when available, else NCCL)."""
     if _tp_world(group) > 1:
@@ -263,8 +272,7 @@ class _BlockFn(torch.autograd.Function):
         if t_fb is not None:
             K.colsum(dh, t_fb.dst, accumulate=t_fb.accumulate)
             t_fb.commit()
-        dh2 = G.linear_dgrad(dh, w_fc)
-        _all_reduce_(dh2, group)  # f: gradient of the replicated LN2 output
+        dh2 = _dgrad_all_reduce(dh, w_fc, group)  # f: gradient of the replicated LN2 output
         # LN2 backward + residual, with both row-parallel bias gradients fused.
         t_l2g, t_l2b, t_mb, t_pb = _targets(blk.ln2.weight, blk.ln2.bias, mlp.proj.bias, attn.proj.bias)
         dx1 = K.layernorm_bwd(
@@ -291,8 +299,7 @@ class _BlockFn(torch.autograd.Function):
         if t_qb is not None:
             K.colsum(dqkv, t_qb.dst, accumulate=t_qb.accumulate)
             t_qb.commit()
-        dh1 = G.linear_dgrad(dqkv, w_qkv)
-        _all_reduce_(dh1, group)
+        dh1 = _dgrad_all_reduce(dqkv, w_qkv, group)
         t_l1g, t_l1b = _targets(blk.ln1.weight, blk.ln1.bias)
         dx = K.layernorm_bwd(
             dh1, xin, mu1, r1, ln1g, resid_grad=dx1,

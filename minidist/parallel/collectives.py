@@ -188,7 +188,13 @@ def _tp_fused_enabled() -> bool:
     return os.environ.get("MINIDIST_TP_FUSED", "1") not in ("0", "false", "no")
 
 
-def gemm_all_reduce(x_local, w_local, bias, resid, group):
+def dgrad_all_reduce(dy_local: torch.Tensor, w_local: torch.Tensor, group) -> torch.Tensor:
+    """``all_reduce(dy_local @ w_local)`` (bf16): the tensor-parallel ``f`` backward of a
+    column-parallel layer (tensor_parallel.py:148-152) fused with its data-gradient GEMM."""
+    return gemm_all_reduce(dy_local, w_local, None, None, group, b_mn=True)
+
+
+def gemm_all_reduce(x_local, w_local, bias, resid, group, b_mn: bool = False):
     """``resid + bias + all_reduce(x_local @ w_local^T)`` (bf16) over the tensor-parallel group.
 
     On the fused path this is one ``md_gemm_ar`` launch: the GEMM epilogue
@@ -199,10 +205,10 @@ def gemm_all_reduce(x_local, w_local, bias, resid, group):
     Otherwise: GEMM, NCCL all-reduce, then bias/residual.
     """
     M, K = x_local.shape
-    N = w_local.shape[0]
+    N = w_local.shape[1] if b_mn else w_local.shape[0]
     c = _group_comm(group) if _tp_fused_enabled() else None
     if c is None or c.world not in (2, 4, 8) or N % 8 or x_local.stride(1) != 1 or w_local.stride(1) != 1:
-        out = G.linear_fwd(x_local, w_local)
+        out = G.linear_dgrad(x_local, w_local) if b_mn else G.linear_fwd(x_local, w_local)
         comm.all_reduce(out, group=group)
         acc = out.float()
         if bias is not None:
@@ -219,7 +225,7 @@ def gemm_all_reduce(x_local, w_local, bias, resid, group):
     flags = c.zeroed_buffer("tp_flags", 2 * chunks * 4)
     out = G.empty_padded(M, N, device=x_local.device)
     # The parameter structs are built once per (buffers, shape) and patched per call.
-    key = (id(part), id(fin), id(flags), M, N, K)
+    key = (id(part), id(fin), id(flags), M, N, K, b_mn)
     st = _AR_CACHE.get(id(c))
     if st is None or st[0] != key:
         ar = TpArParams()
@@ -235,6 +241,7 @@ def gemm_all_reduce(x_local, w_local, bias, resid, group):
         gp.M, gp.N, gp.K = M, N, K
         gp.epi = G.EPI_BF16
         gp.alpha = 1.0
+        gp.b_mn_major = int(b_mn)
         gp.status = nat.status_ptr(x_local.device)
         st = (key, ar, gp, ctypes.byref(gp), ctypes.byref(ar))
         _AR_CACHE[id(c)] = st

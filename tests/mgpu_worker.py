@@ -122,6 +122,10 @@ def check_tp_gpt(rank, world):
     want = gfull[:, rank * cols:(rank + 1) * cols]
     err = ((gpart - want).abs().max() / want.abs().max()).item()
     assert err < 5e-2, f"rank {rank}: mlp.proj grad err {err}"
+    # position-embedding gradient: downstream of every fused data-gradient all-reduce
+    gw, gr = model.embedding.wpe.grad, ref.embedding.wpe.grad
+    err = ((gw - gr).abs().max() / gr.abs().max()).item()
+    assert err < 5e-2, f"rank {rank}: wpe grad err {err}"
     nat.check_status()
 
 
