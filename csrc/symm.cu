@@ -50,6 +50,32 @@ struct MdArParams {
   md::Status* status;
 };
 
+// Reduce-scatter of FSDP gradients (md_rs_shard): every rank holds the
+// unit's full fp32 gradient at `offset` of its symmetric buffer; rank r sums
+// elements [offset + r*shard, +shard) over all ranks (fixed rank order),
+// scales by `scale`, and either writes / accumulates the result into its
+// shard gradient `grad_out`, or (p != null) applies AdamW to its shard in
+// place -- the reduce-scatter, 1/W scale, cast and optimizer update of the
+// reference's fsdp.py:215-241 + optimizer.step() in one pass.
+struct MdRsParams {
+  float* bufs[md::symm::kMaxWorld];
+  uint32_t* flags[md::symm::kMaxWorld];
+  long long offset;      // element offset of the unit in every buffer
+  long long shard;       // elements per rank (multiple of 4)
+  int world, rank;
+  float scale;
+  uint32_t epoch;
+  int channel;
+  unsigned long long timeout_ns;
+  md::Status* status;
+  float* grad_out;       // shard gradient, or null when p != null
+  int accumulate;        // grad_out += result
+  float* p;              // fused AdamW: fp32 shard, first moment, second moment
+  float* m;
+  float* v;
+  float lr, b1, b2, eps, wd, bc1, bc2_sqrt;
+};
+
 namespace md {
 namespace symm {
 
@@ -69,7 +95,8 @@ __device__ __forceinline__ size_t flag_idx(int channel, int cta, int src) {
 
 // Per-CTA all-to-all barrier with the same-index CTA of every rank.
 // Returns false on timeout (status recorded).
-__device__ bool cta_barrier(const MdArParams& p, uint32_t value, uint32_t where) {
+template <typename P>
+__device__ bool cta_barrier(const P& p, uint32_t value, uint32_t where) {
   __shared__ int ok_sh;
   if (threadIdx.x == 0) ok_sh = 1;
   __syncthreads();
@@ -131,10 +158,81 @@ __global__ void __launch_bounds__(512) md_ar_bucket_kernel(const __grid_constant
   cta_barrier(p, depart, 101);
 }
 
+__global__ void __launch_bounds__(512) md_rs_shard_kernel(const __grid_constant__ MdRsParams p) {
+  const uint32_t arrive = 2u * p.epoch + 1u, depart = 2u * p.epoch + 2u;
+  if (!cta_barrier(p, arrive, 110)) return;
+  const long long n4 = p.shard / 4;
+  const long long base = (p.offset + static_cast<long long>(p.rank) * p.shard) / 4;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const float4* srcs[kMaxWorld];
+#pragma unroll
+  for (int r = 0; r < kMaxWorld; ++r) srcs[r] = r < p.world ? reinterpret_cast<const float4*>(p.bufs[r]) + base : nullptr;
+  const float step = p.lr / p.bc1, decay = 1.f - p.lr * p.wd;
+  for (long long u = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; u < n4; u += stride) {
+    float4 v[kMaxWorld];
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r)
+      if (r < p.world) v[r] = __ldcg(srcs[r] + u);
+    float4 s = v[0];
+#pragma unroll
+    for (int r = 1; r < kMaxWorld; ++r)
+      if (r < p.world) {
+        s.x += v[r].x;
+        s.y += v[r].y;
+        s.z += v[r].z;
+        s.w += v[r].w;
+      }
+    s.x *= p.scale;
+    s.y *= p.scale;
+    s.z *= p.scale;
+    s.w *= p.scale;
+    if (p.p != nullptr) {
+      float4 pp = reinterpret_cast<float4*>(p.p)[u], mm = reinterpret_cast<float4*>(p.m)[u],
+             vv = reinterpret_cast<float4*>(p.v)[u];
+      float* P = &pp.x;
+      float* M = &mm.x;
+      float* V = &vv.x;
+      const float* G = &s.x;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        M[q] = p.b1 * M[q] + (1.f - p.b1) * G[q];
+        V[q] = p.b2 * V[q] + (1.f - p.b2) * G[q] * G[q];
+        P[q] = P[q] * decay - step * M[q] / (sqrtf(V[q]) / p.bc2_sqrt + p.eps);
+      }
+      reinterpret_cast<float4*>(p.p)[u] = pp;
+      reinterpret_cast<float4*>(p.m)[u] = mm;
+      reinterpret_cast<float4*>(p.v)[u] = vv;
+    } else {
+      float4* g = reinterpret_cast<float4*>(p.grad_out) + u;
+      if (p.accumulate) {
+        const float4 o = *g;
+        s.x += o.x;
+        s.y += o.y;
+        s.z += o.z;
+        s.w += o.w;
+      }
+      *g = s;
+    }
+  }
+  // No rank rewrites its gradient buffer before every peer has read it.
+  cta_barrier(p, depart, 111);
+}
+
 }  // namespace symm
 }  // namespace md
 
 extern "C" {
+
+// Launch md_rs_shard_kernel with `ctas` CTAs (<= 64).
+int md_rs_shard(const MdRsParams* prm, int ctas, cudaStream_t s) {
+  if (prm == nullptr || prm->world < 1 || prm->world > md::symm::kMaxWorld || (prm->shard % 4) || (prm->offset % 4))
+    return -1;
+  if (ctas < 1 || ctas > md::symm::kMaxCtas || prm->channel < 0 || prm->channel >= md::symm::kChannels) return -2;
+  if (prm->p == nullptr && prm->grad_out == nullptr) return -3;
+  md::symm::md_rs_shard_kernel<<<ctas, 512, 0, s>>>(*prm);
+  return static_cast<int>(cudaGetLastError());
+}
+
 
 int md_symm_max_world() { return md::symm::kMaxWorld; }
 long long md_symm_flag_bytes() {

@@ -22,8 +22,11 @@ leftovers).  Each unit:
 B200 design.  On CUDA the gather for the *next* unit is issued on a side
 stream while the current unit computes (the reference gathers synchronously,
 fsdp.py:172-182), so NVLink traffic overlaps compute; the gather and the
-reduce-scatter use the peer-memory kernels of :mod:`minidist.parallel.collectives`
-when every rank of the group is on this node, NCCL otherwise.
+reduce-scatter of gradients is one peer-memory kernel (md_rs_shard in
+csrc/symm.cu: sum of this rank's shard over every rank's fp32 full gradient,
+1/W scale, accumulate into the shard gradient -- or, with ``fused_adamw``, the
+AdamW update of the shard) when every rank of the group is on this node; NCCL
+otherwise.  The gather is NCCL's all-gather on the prefetch stream.
 """
 
 from __future__ import annotations
@@ -57,7 +60,7 @@ class MixedPrecisionPolicy:
 
 class _FSDPUnit:
     def __init__(self, module: nn.Module, params: list[nn.Parameter], group, policy: MixedPrecisionPolicy,
-                 reshard_after_forward: bool, device: torch.device, name: str):
+                 reshard_after_forward: bool, device: torch.device, name: str, align: int = 1):
         self.module, self.params, self.group, self.policy = module, params, group, policy
         self.reshard_after_forward = reshard_after_forward
         self.name = name
@@ -67,6 +70,7 @@ class _FSDPUnit:
         self.numels = [p.numel() for p in params]
         self.total_numel = sum(self.numels)
         self.shard_numel = -(-self.total_numel // self.world)
+        self.shard_numel = -(-self.shard_numel // align) * align
         self.padded_numel = self.shard_numel * self.world
 
         src_dtype = params[0].dtype
@@ -89,6 +93,9 @@ class _FSDPUnit:
         self._pending = 0
         self._grad_acc: torch.Tensor | None = None  # fp32 full grads written by fused kernels
         self._hook_handles: list = []
+        # Peer-memory reduce-scatter: (communicator, symmetric buffer, element offset) or None.
+        self._peer: tuple | None = None
+        self._adam: dict | None = None  # fused AdamW: hyper-parameters, m, v, step
 
     # -- gather / free -------------------------------------------------------------
 
@@ -158,17 +165,62 @@ class _FSDPUnit:
         self.reshard()
 
     def _full_grad_buffer(self) -> torch.Tensor:
-        """fp32 buffer for the fused kernels' full gradients (laid out like ``_full``)."""
+        """fp32 buffer for the fused kernels' full gradients (laid out like ``_full``); with the
+        peer-memory reduce-scatter it is this unit's slice of the symmetric gradient buffer."""
         if self._grad_acc is None:
-            self._grad_acc = torch.zeros(self.padded_numel, dtype=self.policy.reduce_dtype,
-                                         device=self.flat_shard.device)
+            if self._peer is not None:
+                _, buf, off = self._peer
+                self._grad_acc = buf.view(torch.float32, off * 4, self.padded_numel)
+            else:
+                self._grad_acc = torch.zeros(self.padded_numel, dtype=self.policy.reduce_dtype,
+                                             device=self.flat_shard.device)
             off = 0
             for p, n, shape in zip(self.params, self.numels, self.shapes, strict=True):
                 gradsink.set_main_grad(p, self._grad_acc[off : off + n].view(shape))
                 off += n
         return self._grad_acc
 
+    def _reduce_scatter_peer(self) -> None:
+        """Reduce-scatter through peer memory: the full fp32 gradients sit in this rank's slice of
+        the symmetric buffer; one kernel sums this rank's shard over every rank, scales by 1/W and
+        accumulates into ``flat_shard.grad`` -- or applies AdamW to the shard in place."""
+        from .parallel import collectives
+
+        comm_, buf, off = self._peer
+        full = self._full_grad_buffer()
+        o = 0
+        with torch.no_grad():
+            for p, n in zip(self.params, self.numels, strict=True):
+                slot = full[o : o + n]
+                g = p.grad
+                if g is not None and g.data_ptr() == slot.data_ptr():
+                    pass  # written in place (fused kernels' main gradient, or autograd accumulating into it)
+                elif g is not None:
+                    slot.copy_(g.detach().reshape(-1))
+                else:
+                    slot.zero_()  # no gradient this step
+                o += n
+        shard = self.flat_shard
+        if self._adam is not None:
+            a = self._adam
+            a["step"] += 1
+            b1, b2 = a["betas"]
+            collectives.reduce_scatter_shard(buf, comm_, off, self.shard_numel, None, False, 1.0 / self.world,
+                                             adam=(shard.data, a["m"], a["v"], a["lr"], b1, b2, a["eps"],
+                                                   a["weight_decay"], a["step"]))
+        else:
+            acc = shard.grad is not None
+            if not acc:
+                shard.grad = torch.empty(self.shard_numel, dtype=torch.float32, device=shard.device)
+            collectives.reduce_scatter_shard(buf, comm_, off, self.shard_numel, shard.grad, acc, 1.0 / self.world)
+        for p in self.params:
+            p.grad = None
+            p._md_grad_written = False
+
     def reduce_scatter_grads(self) -> None:
+        if self._peer is not None:
+            self._reduce_scatter_peer()
+            return
         rdt = self.policy.reduce_dtype
         dev = self.flat_shard.device
         buf = torch.zeros(self.padded_numel, dtype=rdt, device=dev)
@@ -213,7 +265,11 @@ class FullyShardedDataParallel(nn.Module):
         broadcast_parameters: bool = True,
         device: torch.device | None = None,
         prefetch: bool = True,
+        fused_adamw: dict | None = None,
     ):
+        """``fused_adamw`` (dict with ``lr``, ``betas``, ``eps``, ``weight_decay``) applies AdamW to
+        each shard inside the gradient reduce-scatter kernel, right when the unit's gradients are
+        complete (peer-memory path only; no separate optimizer for these parameters)."""
         super().__init__()
         self.module = module
         self.process_group = process_group
@@ -228,8 +284,32 @@ class FullyShardedDataParallel(nn.Module):
                     comm.broadcast(p.data, src=gsrc, group=process_group)
                 for b in module.buffers():
                     comm.broadcast(b.data, src=gsrc, group=process_group)
+        self._peer_comm = None
+        if device.type == "cuda" and self.world_size > 1 and self.policy.reduce_dtype == torch.float32:
+            from .parallel import collectives
+
+            self._peer_comm = collectives.fsdp_communicator(process_group)
+        self._align = 4 if self._peer_comm is not None else 1
         self._units = self._build_units(module, tuple(unit_types), reshard_after_forward,
                                         reshard_root_after_forward, device)
+        if self._peer_comm is not None:
+            total = sum(u.padded_numel for u in self._units)
+            self._grad_buf = self._peer_comm.buffer(f"fsdp_grads_{id(self)}", total * 4)
+            off = 0
+            for u in self._units:
+                u._peer = (self._peer_comm, self._grad_buf, off)
+                u._full_grad_buffer()  # fused kernels write gradients straight into the symmetric buffer
+                off += u.padded_numel
+        if fused_adamw is not None:
+            if self._peer_comm is None or any(u.flat_shard.dtype != torch.float32 for u in self._units):
+                raise ValueError("fused_adamw needs the peer-memory reduce-scatter and fp32 shards")
+            for u in self._units:
+                u._adam = {"lr": float(fused_adamw.get("lr", 1e-3)),
+                           "betas": tuple(fused_adamw.get("betas", (0.9, 0.999))),
+                           "eps": float(fused_adamw.get("eps", 1e-8)),
+                           "weight_decay": float(fused_adamw.get("weight_decay", 0.01)),
+                           "m": torch.zeros_like(u.flat_shard.data), "v": torch.zeros_like(u.flat_shard.data),
+                           "step": 0}
         self._shards = nn.ParameterList([u.flat_shard for u in self._units])
         self._prefetch_stream = None
         if prefetch and device.type == "cuda" and self.world_size > 1:
@@ -247,12 +327,13 @@ class FullyShardedDataParallel(nn.Module):
                 continue
             claimed.update(id(p) for p in params)
             units.append(_FSDPUnit(m, params, self.process_group, self.policy, reshard_after_forward,
-                                   device, name or "root"))
+                                   device, name or "root", align=self._align))
         rest = [p for p in root.parameters() if id(p) not in claimed]
         if rest:
             # The root unit (embeddings, final norm, head) is needed at both ends
             # of backward, so by default it stays gathered after forward.
-            units.append(_FSDPUnit(root, rest, self.process_group, self.policy, reshard_root, device, "<root>"))
+            units.append(_FSDPUnit(root, rest, self.process_group, self.policy, reshard_root, device, "<root>",
+                                   align=self._align))
         if not units:
             raise ValueError("FSDP wrapped a module with no parameters")
         return units

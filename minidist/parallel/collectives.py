@@ -260,3 +260,81 @@ def gemm_all_reduce(x_local, w_local, bias, resid, group, b_mn: bool = False):
         nat.check(rc, f"md_gemm_ar(M={M},N={N},K={K})")
     comm.comm_stats.add("all_reduce", M * N * 2, int(2 * (c.world - 1) / c.world * M * N * 2))
     return out
+
+
+# ---------------------------------------------------------------------------
+# FSDP: reduce-scatter (+ AdamW) over peer memory
+# ---------------------------------------------------------------------------
+_FSDP_CHANNEL = 4
+
+
+class RsParams(ctypes.Structure):
+    """Mirror of ``struct MdRsParams`` (csrc/symm.cu)."""
+
+    _fields_ = [
+        ("bufs", ctypes.c_void_p * _MAXW),
+        ("flags", ctypes.c_void_p * _MAXW),
+        ("offset", ctypes.c_longlong),
+        ("shard", ctypes.c_longlong),
+        ("world", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("scale", ctypes.c_float),
+        ("epoch", ctypes.c_uint32),
+        ("channel", ctypes.c_int),
+        ("timeout_ns", ctypes.c_ulonglong),
+        ("status", ctypes.c_void_p),
+        ("grad_out", ctypes.c_void_p),
+        ("accumulate", ctypes.c_int),
+        ("p", ctypes.c_void_p),
+        ("m", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("lr", ctypes.c_float),
+        ("b1", ctypes.c_float),
+        ("b2", ctypes.c_float),
+        ("eps", ctypes.c_float),
+        ("wd", ctypes.c_float),
+        ("bc1", ctypes.c_float),
+        ("bc2_sqrt", ctypes.c_float),
+    ]
+
+
+nat.declare("md_rs_shard", "i:pip")
+
+
+def fsdp_communicator(group) -> symm.Communicator | None:
+    """Peer-memory communicator for FSDP's gradient reduce-scatter (``None`` -> NCCL)."""
+    if os.environ.get("MINIDIST_FSDP_FUSED", "1") in ("0", "false", "no"):
+        return None
+    return _group_comm(group)
+
+
+def reduce_scatter_shard(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offset: int, shard: int,
+                         grad_out: torch.Tensor | None, accumulate: bool, scale: float,
+                         adam: tuple | None = None) -> None:
+    """Rank r's slice ``[elem_offset + r*shard, +shard)`` of ``buf`` summed over ranks, times ``scale``,
+    into ``grad_out`` (or, with ``adam = (p, m, v, lr, b1, b2, eps, wd, step)``, an AdamW update of ``p``)."""
+    prm = RsParams()
+    for r in range(comm_.world):
+        prm.bufs[r] = buf.ptrs[r]
+        prm.flags[r] = buf.flag_ptrs[r]
+    prm.offset, prm.shard = elem_offset, shard
+    prm.world, prm.rank = comm_.world, comm_.rank
+    prm.scale = scale
+    prm.epoch = comm_.next_epoch(_FSDP_CHANNEL)
+    prm.channel = _FSDP_CHANNEL
+    prm.timeout_ns = _timeout_ns()
+    prm.status = nat.status_ptr(buf.device)
+    if adam is not None:
+        p, m, v, lr, b1, b2, eps, wd, step = adam
+        prm.p, prm.m, prm.v = p.data_ptr(), m.data_ptr(), v.data_ptr()
+        prm.lr, prm.b1, prm.b2, prm.eps, prm.wd = lr, b1, b2, eps, wd
+        prm.bc1 = 1.0 - b1 ** step
+        prm.bc2_sqrt = (1.0 - b2 ** step) ** 0.5
+    else:
+        prm.grad_out = grad_out.data_ptr()
+        prm.accumulate = int(accumulate)
+    ctas = min(64, max(1, shard // (4 * 512 * 4)))
+    rc = nat.lib().md_rs_shard(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr(None)))
+    nat.check(rc, "md_rs_shard")
+    n = shard * comm_.world * 4
+    comm.comm_stats.add("reduce_scatter", n, int((comm_.world - 1) / comm_.world * n))

@@ -73,6 +73,61 @@ def check_ddp(rank, world):
     nat.check_status()
 
 
+def check_fsdp(rank, world):
+    """FSDP with the peer-memory reduce-scatter: shard gradients equal the full-batch reference's
+    shard; the in-kernel AdamW (fused_adamw) matches FSDP + FusedAdamW step for step."""
+    import minidist as md
+    from minidist.models import GPT, Block, GPTConfig
+    from minidist.optim import FusedAdamW
+
+    cfg = GPTConfig(vocab_size=1000, block_size=128, n_layer=2, n_head=4, n_embd=256)
+    mesh = md.ParallelMesh(tp_size=1)
+    ref = GPT(cfg, tp_group=mesh.tp_group, device="cuda")
+    model = md.FullyShardedDataParallel(GPT(cfg, tp_group=mesh.tp_group, device="cuda"), unit_types=(Block,),
+                                        process_group=mesh.dp_group)
+    assert all(u._peer is not None for u in model._units), "peer-memory reduce-scatter not in use"
+    g = torch.Generator().manual_seed(11)
+    ids = torch.randint(0, cfg.vocab_size, (2 * world, 128), generator=g).cuda()
+    tgt = torch.randint(0, cfg.vocab_size, (2 * world, 128), generator=g).cuda()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        ref(ids, tgt)[1].backward()
+        model(ids.chunk(world)[rank], tgt.chunk(world)[rank])[1].backward()
+    model.finish_gradient_sync()
+    torch.cuda.synchronize()
+    refp = dict(ref.named_parameters())
+    names = {id(p): n for n, p in model.module.named_parameters()}
+    for u in model._units:
+        full = torch.cat([refp[names[id(p)]].grad.reshape(-1).float() for p in u.params])
+        full = torch.cat([full, full.new_zeros(u.padded_numel - u.total_numel)])
+        want = full[rank * u.shard_numel:(rank + 1) * u.shard_numel]
+        err = ((u.flat_shard.grad - want).abs().max() / want.abs().max().clamp(min=1e-8)).item()
+        assert err < 5e-2, f"rank {rank} unit {u.name}: shard grad err {err}"
+    # in-kernel AdamW vs FusedAdamW on the same FSDP shards
+    hp = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    fa = md.FullyShardedDataParallel(GPT(cfg, tp_group=mesh.tp_group, device="cuda"), unit_types=(Block,),
+                                     process_group=mesh.dp_group, fused_adamw=hp)
+    fb = md.FullyShardedDataParallel(GPT(cfg, tp_group=mesh.tp_group, device="cuda"), unit_types=(Block,),
+                                     process_group=mesh.dp_group)
+    opt = FusedAdamW(fb.parameters(), **hp)
+    for it in range(3):
+        x = ids.roll(it, 1).chunk(world)[rank]
+        y = tgt.roll(it, 1).chunk(world)[rank]
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            fa(x, y)[1].backward()
+        fa.finish_gradient_sync()
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            fb(x, y)[1].backward()
+        fb.finish_gradient_sync()
+        opt.step()
+    torch.cuda.synchronize()
+    for ua, ub in zip(fa._units, fb._units):
+        assert ua.flat_shard.grad is None, "fused AdamW left a shard gradient behind"
+        d = (ua.flat_shard.data - ub.flat_shard.data).abs().max().item()
+        assert d < 1e-4, f"rank {rank} unit {ua.name}: fused AdamW differs by {d}"
+    nat.check_status()
+
+
 def check_gemm_ar(rank, world):
     """Fused GEMM + all-reduce (md_gemm_ar) against fp32 torch on the gathered partials."""
     for it, (M, K, N, with_resid) in enumerate([(1000, 192, 768, True), (4096, 384, 768, False),
@@ -137,6 +192,7 @@ def main():
         check_allreduce(rank, world)
         check_gemm_ar(rank, world)
         check_ddp(rank, world)
+        check_fsdp(rank, world)
         check_tp_gpt(rank, world)
     finally:
         symm.release_all()
