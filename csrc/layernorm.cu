@@ -256,6 +256,198 @@ __global__ void __launch_bounds__(kThreads) ln_bwd_kernel(
   }
 }
 
+// Backward for rows of up to 1024 columns (one warp per row, lane l owns the
+// 16-byte vectors j = l + 32 i).  Same math and outputs as ln_bwd_kernel, but
+// every lane streams its own vectors of dy, x and resid_grad through a
+// kStages-deep cp.async ring in shared memory, so each warp has the next
+// kStages-1 rows in flight while it computes the current one (the register
+// version held one row per warp in flight: ~30 % of DRAM bandwidth).  A lane
+// reads back only what it copied itself, so no cross-lane synchronisation is
+// needed until the final fixed-order reduction, which reuses the ring.
+constexpr int kPipeStages = 4;
+
+__device__ __forceinline__ void cp_async16_ln(uint32_t smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_ln() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_ln() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int V, int NACC>
+__global__ void __launch_bounds__(kThreads, 1) ln_bwd_pipe_kernel(
+    const __nv_bfloat16* __restrict__ dy, long long lddy, const __nv_bfloat16* __restrict__ x, long long ldx,
+    const float* __restrict__ mean_in, const float* __restrict__ rstd_in, const float* __restrict__ gamma,
+    const __nv_bfloat16* __restrict__ resid_grad, long long ldr, __nv_bfloat16* __restrict__ dx, long long lddx,
+    float* __restrict__ partials, int M, int C) {
+  extern __shared__ __align__(16) uint8_t smem_u8[];
+  constexpr int kWarps = kThreads / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nvec = C / 8;
+  const float inv_c = 1.0f / static_cast<float>(C);
+  const bool has_r = resid_grad != nullptr;
+  // Ring: [warp][stage][tensor (dy, x, r)][V][32 lanes] x 16 bytes, then
+  // [warp][stage] x (mean, rstd) copied by lane 0.
+  uint8_t* ring = smem_u8 + static_cast<size_t>(warp) * kPipeStages * 3 * V * 32 * 16;
+  float* stats = reinterpret_cast<float*>(smem_u8 + static_cast<size_t>(kWarps) * kPipeStages * 3 * V * 32 * 16) +
+                 warp * kPipeStages * 2;
+  auto slot = [&](int st, int tsr, int i) -> uint32_t {
+    return smem_u32(ring + (((st * 3 + tsr) * V + i) * 32 + lane) * 16);
+  };
+  const int rows_per_pass = gridDim.x * kWarps;
+  const int first = blockIdx.x * kWarps + warp;
+  const int passes = first < M ? (M - 1 - first) / rows_per_pass + 1 : 0;
+  auto issue = [&](int pass) {
+    if (pass < passes) {
+      const long long r = first + static_cast<long long>(pass) * rows_per_pass;
+      const int st = pass % kPipeStages;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const int j = lane + 32 * i;
+        if (j < nvec) {
+          cp_async16_ln(slot(st, 0, i), reinterpret_cast<const uint4*>(dy + r * lddy) + j);
+          cp_async16_ln(slot(st, 1, i), reinterpret_cast<const uint4*>(x + r * ldx) + j);
+          if (has_r) cp_async16_ln(slot(st, 2, i), reinterpret_cast<const uint4*>(resid_grad + r * ldr) + j);
+        }
+      }
+      if (lane == 0) {
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(stats + 2 * st)), "l"(mean_in + r)
+                     : "memory");
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(stats + 2 * st + 1)), "l"(rstd_in + r)
+                     : "memory");
+      }
+    }
+    cp_async_commit_ln();  // empty groups keep the count uniform
+  };
+
+  float acc[NACC][V][8];
+#pragma unroll
+  for (int a = 0; a < NACC; ++a)
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[a][i][e] = 0.f;
+  float gam[V][8];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int j = lane + 32 * i;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) gam[i][e] = j < nvec ? gamma[8 * j + e] : 0.f;
+  }
+
+#pragma unroll
+  for (int k = 0; k < kPipeStages - 1; ++k) issue(k);
+  for (int pass = 0; pass < passes; ++pass) {
+    __syncwarp();  // every lane has read the previous row's statistics before lane 0 refills that slot
+    issue(pass + kPipeStages - 1);
+    cp_async_wait_ln<kPipeStages - 1>();
+    __syncwarp();  // lane 0's statistics copy is visible to the warp
+    const long long row = first + static_cast<long long>(pass) * rows_per_pass;
+    const int st = pass % kPipeStages;
+    const float mean = stats[2 * st], rstd = stats[2 * st + 1];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int j = lane + 32 * i;
+      if (j < nvec) {
+        uint4 wd, wx;
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(wd.x), "=r"(wd.y), "=r"(wd.z), "=r"(wd.w)
+                     : "r"(slot(st, 0, i)));
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(wx.x), "=r"(wx.y), "=r"(wx.z), "=r"(wx.w)
+                     : "r"(slot(st, 1, i)));
+        const uint32_t ds[4] = {wd.x, wd.y, wd.z, wd.w}, xs[4] = {wx.x, wx.y, wx.z, wx.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 dv = unpack_bf16x2(ds[q]), xv = unpack_bf16x2(xs[q]);
+          const float h0 = (xv.x - mean) * rstd, h1 = (xv.y - mean) * rstd;
+          acc[0][i][2 * q] += dv.x * h0;
+          acc[0][i][2 * q + 1] += dv.y * h1;
+          acc[1][i][2 * q] += dv.x;
+          acc[1][i][2 * q + 1] += dv.y;
+          const float g0 = dv.x * gam[i][2 * q], g1 = dv.y * gam[i][2 * q + 1];
+          s1 += g0 + g1;
+          s2 += g0 * h0 + g1 * h1;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    const float a1 = s1 * inv_c, a2 = s2 * inv_c;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int j = lane + 32 * i;
+      if (j < nvec) {
+        uint4 wd, wx;
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(wd.x), "=r"(wd.y), "=r"(wd.z), "=r"(wd.w)
+                     : "r"(slot(st, 0, i)));
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(wx.x), "=r"(wx.y), "=r"(wx.z), "=r"(wx.w)
+                     : "r"(slot(st, 1, i)));
+        const uint32_t ds[4] = {wd.x, wd.y, wd.z, wd.w}, xs[4] = {wx.x, wx.y, wx.z, wx.w};
+        float o[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 dv = unpack_bf16x2(ds[q]), xv = unpack_bf16x2(xs[q]);
+          o[2 * q] = rstd * (dv.x * gam[i][2 * q] - a1 - (xv.x - mean) * rstd * a2);
+          o[2 * q + 1] = rstd * (dv.y * gam[i][2 * q + 1] - a1 - (xv.y - mean) * rstd * a2);
+        }
+        if (has_r) {
+          uint4 wr;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(wr.x), "=r"(wr.y), "=r"(wr.z), "=r"(wr.w)
+                       : "r"(slot(st, 2, i)));
+          const uint32_t rs[4] = {wr.x, wr.y, wr.z, wr.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 rv = unpack_bf16x2(rs[q]);
+            o[2 * q] += rv.x;
+            o[2 * q + 1] += rv.y;
+            if constexpr (NACC == 4) {
+              acc[2][i][2 * q] += rv.x;
+              acc[2][i][2 * q + 1] += rv.y;
+            }
+          }
+        }
+        uint4 w;
+        w.x = pack_bf16x2(o[0], o[1]);
+        w.y = pack_bf16x2(o[2], o[3]);
+        w.z = pack_bf16x2(o[4], o[5]);
+        w.w = pack_bf16x2(o[6], o[7]);
+        reinterpret_cast<uint4*>(dx + row * lddx)[j] = w;
+        if constexpr (NACC == 4) {
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 ov = unpack_bf16x2(ws[q]);
+            acc[3][i][2 * q] += ov.x;
+            acc[3][i][2 * q + 1] += ov.y;
+          }
+        }
+      }
+    }
+  }
+  cp_async_wait_ln<0>();
+  __syncthreads();  // every warp is done with its ring: reuse it for the reduction
+  float* red = reinterpret_cast<float*>(smem_u8);  // [warp][NACC][C]
+#pragma unroll
+  for (int a = 0; a < NACC; ++a)
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int j = lane + 32 * i;
+      if (j < nvec)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) red[(warp * NACC + a) * C + j * 8 + e] = acc[a][i][e];
+    }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < NACC * C; idx += kThreads) {
+    float s = 0.f;
+    for (int w = 0; w < kWarps; ++w) s += red[w * NACC * C + idx];
+    partials[static_cast<long long>(blockIdx.x) * NACC * C + idx] = s;
+  }
+}
+
 // out_a[c] (+)= sum_b partials[b][a][c] for each accumulator a with a non-null destination.
 // Block = 32 columns x 8 row groups; each group sums a contiguous range of
 // partial rows, then the 8 group sums are added in a fixed order.
@@ -327,6 +519,23 @@ cudaError_t ln_bwd_launch(const void* dy, long long lddy, const void* x, long lo
   return cudaGetLastError();
 }
 
+template <int V, int NACC>
+cudaError_t ln_bwd_pipe_launch(const void* dy, long long lddy, const void* x, long long ldx, const float* mean,
+                               const float* rstd, const float* g, const void* rg, long long ldr, void* dx,
+                               long long lddx, float* partials, int grid, int M, int C, cudaStream_t s) {
+  constexpr int kWarps = md::ln::kThreads / 32;
+  const size_t ring = static_cast<size_t>(kWarps) * md::ln::kPipeStages * (3 * V * 32 * 16 + 2 * sizeof(float));
+  const size_t red = static_cast<size_t>(kWarps) * NACC * C * sizeof(float);
+  const size_t smem = ring > red ? ring : red;
+  auto kern = md::ln::ln_bwd_pipe_kernel<V, NACC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  kern<<<grid, md::ln::kThreads, smem, s>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dy), lddy, reinterpret_cast<const __nv_bfloat16*>(x), ldx, mean, rstd, g,
+      reinterpret_cast<const __nv_bfloat16*>(rg), ldr, reinterpret_cast<__nv_bfloat16*>(dx), lddx, partials, M, C);
+  return cudaGetLastError();
+}
+
 bool ok16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 }  // namespace
 
@@ -334,8 +543,9 @@ extern "C" {
 
 // Number of CTAs (= partial rows) md_ln_bwd uses for M rows of width C.
 int md_ln_bwd_grid(int M, int C) {
-  (void)C;
-  int g = sms() * 2;
+  // The pipelined kernel (C <= 1024) holds one CTA per SM (its prefetch ring
+  // takes most of shared memory); the register kernel runs two.
+  int g = C <= 1024 ? sms() : sms() * 2;
   return g < M ? g : (M > 0 ? M : 1);
 }
 
@@ -388,13 +598,25 @@ int md_ln_bwd(const void* dy, long long lddy, const void* x, long long ldx, cons
     else if (v == 3) e = MD_LN_BWD_TV(TT, 3);   \
     else e = MD_LN_BWD_TV(TT, 4);               \
   }
-  if (C <= 1024)      MD_LN_BWD_T(32)
+#define MD_LN_BWD_PIPE(VV)                                                                                          \
+  (nacc == 2 ? ln_bwd_pipe_launch<VV, 2>(dy, lddy, x, ldx, mean, rstd, gamma, resid_grad, ldr, dx, lddx, partials,   \
+                                         grid, M, C, s)                                                              \
+             : ln_bwd_pipe_launch<VV, 4>(dy, lddy, x, ldx, mean, rstd, gamma, resid_grad, ldr, dx, lddx, partials,   \
+                                         grid, M, C, s))
+  if (C <= 1024) {
+    const int v = (nvec + 31) / 32;
+    if (v <= 1) e = MD_LN_BWD_PIPE(1);
+    else if (v == 2) e = MD_LN_BWD_PIPE(2);
+    else if (v == 3) e = MD_LN_BWD_PIPE(3);
+    else e = MD_LN_BWD_PIPE(4);
+  }
   else if (C <= 2048) MD_LN_BWD_T(64)
   else if (C <= 4096) MD_LN_BWD_T(128)
   else if (C <= 8192) MD_LN_BWD_T(256)
   else return -2;
 #undef MD_LN_BWD_T
 #undef MD_LN_BWD_TV
+#undef MD_LN_BWD_PIPE
   return static_cast<int>(e);
 }
 
