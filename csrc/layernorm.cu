@@ -275,6 +275,116 @@ __device__ __forceinline__ void cp_async_wait_ln() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Forward for rows of up to 1024 columns with the same per-lane cp.async ring
+// (kPipeStages - 1 rows in flight per warp): mean and variance in two passes
+// over registers, gamma and beta held in registers for the whole kernel.
+template <int V>
+__global__ void __launch_bounds__(kThreads, 2) ln_fwd_pipe_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                              const float* __restrict__ gamma,
+                                                              const float* __restrict__ beta,
+                                                              __nv_bfloat16* __restrict__ y, long long ldy,
+                                                              float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                                                              int M, int C, float eps) {
+  extern __shared__ __align__(16) uint8_t smem_u8[];
+  constexpr int kWarps = kThreads / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nvec = C / 8;
+  const float inv_c = 1.0f / static_cast<float>(C);
+  uint8_t* ring = smem_u8 + static_cast<size_t>(warp) * kPipeStages * V * 32 * 16;
+  auto slot = [&](int st, int i) -> uint32_t { return smem_u32(ring + ((st * V + i) * 32 + lane) * 16); };
+  const int rows_per_pass = gridDim.x * kWarps;
+  const int first = blockIdx.x * kWarps + warp;
+  const int passes = first < M ? (M - 1 - first) / rows_per_pass + 1 : 0;
+  auto issue = [&](int pass) {
+    if (pass < passes) {
+      const long long r = first + static_cast<long long>(pass) * rows_per_pass;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const int j = lane + 32 * i;
+        if (j < nvec) cp_async16_ln(slot(pass % kPipeStages, i), reinterpret_cast<const uint4*>(x + r * ldx) + j);
+      }
+    }
+    cp_async_commit_ln();
+  };
+  float gam[V][8], bet[V][8];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int j = lane + 32 * i;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      gam[i][e] = j < nvec ? gamma[8 * j + e] : 0.f;
+      bet[i][e] = j < nvec ? beta[8 * j + e] : 0.f;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kPipeStages - 1; ++k) issue(k);
+  for (int pass = 0; pass < passes; ++pass) {
+    issue(pass + kPipeStages - 1);
+    cp_async_wait_ln<kPipeStages - 1>();
+    const long long row = first + static_cast<long long>(pass) * rows_per_pass;
+    const int st = pass % kPipeStages;
+    float v[V][8];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int j = lane + 32 * i;
+      if (j < nvec) {
+        uint4 w;
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+                     : "r"(slot(st, i)));
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(ws[q]);
+          v[i][2 * q] = f.x;
+          v[i][2 * q + 1] = f.y;
+          s += f.x + f.y;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s * inv_c;
+    float q2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int j = lane + 32 * i;
+      if (j < nvec)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = v[i][e] - mean;
+          q2 += d * d;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q2 += __shfl_xor_sync(0xffffffffu, q2, o);
+    const float rstd = rsqrtf(q2 * inv_c + eps);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int j = lane + 32 * i;
+      if (j < nvec) {
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = (v[i][e] - mean) * rstd * gam[i][e] + bet[i][e];
+        uint4 w;
+        w.x = pack_bf16x2(o[0], o[1]);
+        w.y = pack_bf16x2(o[2], o[3]);
+        w.z = pack_bf16x2(o[4], o[5]);
+        w.w = pack_bf16x2(o[6], o[7]);
+        reinterpret_cast<uint4*>(y + row * ldy)[j] = w;
+      }
+    }
+    if (lane == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+  }
+  cp_async_wait_ln<0>();
+}
+
 template <int V, int NACC>
 __global__ void __launch_bounds__(kThreads, 1) ln_bwd_pipe_kernel(
     const __nv_bfloat16* __restrict__ dy, long long lddy, const __nv_bfloat16* __restrict__ x, long long ldx,
@@ -519,6 +629,22 @@ cudaError_t ln_bwd_launch(const void* dy, long long lddy, const void* x, long lo
   return cudaGetLastError();
 }
 
+template <int V>
+cudaError_t ln_fwd_pipe_launch(const void* x, long long ldx, const float* g, const float* b, void* y, long long ldy,
+                               float* mean, float* rstd, int M, int C, float eps, cudaStream_t s) {
+  constexpr int kWarps = md::ln::kThreads / 32;
+  const size_t smem = static_cast<size_t>(kWarps) * md::ln::kPipeStages * V * 32 * 16;
+  auto kern = md::ln::ln_fwd_pipe_kernel<V>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int grid = (M + kWarps - 1) / kWarps;
+  const int cap = sms() * 2;  // 2 CTAs (16 warps) per SM: 48 rows in flight per SM
+  if (grid > cap) grid = cap;
+  kern<<<grid, md::ln::kThreads, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, g, b,
+                                            reinterpret_cast<__nv_bfloat16*>(y), ldy, mean, rstd, M, C, eps);
+  return cudaGetLastError();
+}
+
 template <int V, int NACC>
 cudaError_t ln_bwd_pipe_launch(const void* dy, long long lddy, const void* x, long long ldx, const float* mean,
                                const float* rstd, const float* g, const void* rg, long long ldr, void* dx,
@@ -563,7 +689,13 @@ int md_ln_fwd(const void* x, long long ldx, const float* gamma, const float* bet
     else if (v == 3) e = ln_fwd_launch<TT, 3>(x, ldx, gamma, beta, y, ldy, mean, rstd, M, C, eps, s); \
     else e = ln_fwd_launch<TT, 4>(x, ldx, gamma, beta, y, ldy, mean, rstd, M, C, eps, s); \
   }
-  if (C <= 1024)      MD_LN_FWD_T(32)
+  if (C <= 1024) {
+    const int v = (nvec + 31) / 32;
+    if (v <= 1) e = ln_fwd_pipe_launch<1>(x, ldx, gamma, beta, y, ldy, mean, rstd, M, C, eps, s);
+    else if (v == 2) e = ln_fwd_pipe_launch<2>(x, ldx, gamma, beta, y, ldy, mean, rstd, M, C, eps, s);
+    else if (v == 3) e = ln_fwd_pipe_launch<3>(x, ldx, gamma, beta, y, ldy, mean, rstd, M, C, eps, s);
+    else e = ln_fwd_pipe_launch<4>(x, ldx, gamma, beta, y, ldy, mean, rstd, M, C, eps, s);
+  }
   else if (C <= 2048) MD_LN_FWD_T(64)
   else if (C <= 4096) MD_LN_FWD_T(128)
   else if (C <= 8192) MD_LN_FWD_T(256)

@@ -19,7 +19,8 @@ def _rel(a, b):
     return ((a - b).abs().max() / b.abs().max().clamp(min=1e-6)).item()
 
 
-@pytest.mark.parametrize("M,C", [(1000, 768), (257, 1600), (64, 2560), (33, 4096)])
+@pytest.mark.parametrize("M,C", [(1000, 768), (100, 256), (300, 1024), (2049, 512), (257, 1600), (64, 2560),
+                                 (33, 4096)])
 def test_layernorm(M, C):
     torch.manual_seed(0)
     x = (torch.randn(M, C, device="cuda") * 2 + 0.5).bfloat16()
