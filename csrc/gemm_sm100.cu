@@ -59,18 +59,21 @@ constexpr int kCeSlab = 128;  // CE statistics are kept per 128-column slab
 
 enum EpiMode : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiDGELU = 2, kEpiCE = 3 };
 
-// Epilogue staging: each epilogue warp owns slabs of 32 rows x 128 bytes
-// (128B-swizzled) that TMA stores / reduce-adds write out; two per warp with
-// four epilogue warps, one with eight (32 KB either way).
+// Epilogue staging: each epilogue warp owns two slabs of 32 rows x 128 bytes
+// (128B-swizzled) that TMA stores / reduce-adds write out (double-buffered
+// output, or output + GELU pre-activation).  Eight epilogue warps (the
+// heavy GELU / dGELU / cross-entropy epilogues) take 64 KB of staging, paid
+// for with one mainloop stage less.
 constexpr int kSlabBytes = 32 * 128;
-constexpr int kEpiSmem = 8 * kSlabBytes;
 
-template <int CG>
+template <int CG, int EW>
 struct Cfg {
   static constexpr int kBBytes = (BN / CG) * BK * 2;  // B rows staged by this CTA
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = CG == 2 ? 6 : 4;
+  static constexpr int kStages = EW == 8 ? (CG == 2 ? 5 : 3) : (CG == 2 ? 6 : 4);
+  static constexpr int kEpiSmem = EW * 2 * kSlabBytes;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiSmem + 256;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 }  // namespace gemm
@@ -326,8 +329,9 @@ __device__ __forceinline__ void slab_issue(EpiStage& e, const CUtensorMap* map, 
 }
 
 template <int EPI>
-__device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtensorMap* tmD, EpiStage& es, int row,
-                                             int row0, int tn, int split, uint32_t t_row, int c_begin, int c_end) {
+__device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtensorMap* tmD, const CUtensorMap* tmX,
+                                             EpiStage& es, int row, int row0, int tn, int split, uint32_t t_row,
+                                             int c_begin, int c_end) {
   const bool row_ok = row < p.M;
   const int lane = es.lane;
   long long tgt = -1;
@@ -336,6 +340,28 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
   const bool to_ws = kF32 && p.k_splits > 1 && p.workspace != nullptr;
   const int f32_mode = (kF32 && !to_ws && (p.k_splits > 1 || p.beta)) ? 1 : 0;
   uint8_t* sb = nullptr;
+  // Second input of the epilogue (the residual for kEpiBF16, the
+  // pre-activation for kEpiDGELU), read one chunk ahead so its load latency
+  // overlaps the current chunk instead of stalling every chunk.
+  const __nv_bfloat16* in_base = nullptr;
+  long long in_ld = 0;
+  if (EPI == kEpiBF16 && p.resid != nullptr) {
+    in_base = reinterpret_cast<const __nv_bfloat16*>(p.resid);
+    in_ld = p.ldres;
+  } else if (EPI == kEpiDGELU) {
+    in_base = reinterpret_cast<const __nv_bfloat16*>(p.aux);
+    in_ld = p.ldaux;
+  }
+  uint4 nxt[4];
+  auto load_in = [&](int c) {
+    const int n0 = tn * BN + c * 32;
+    if (in_base != nullptr && row_ok && c < c_end && n0 + 32 <= p.N) {
+      const uint4* src = reinterpret_cast<const uint4*>(in_base + row * in_ld + n0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) nxt[q] = src[q];
+    }
+  };
+  load_in(c_begin);
 #pragma unroll 1
   for (int slab = c_begin / 4; slab < c_end / 4; ++slab) {
     float ce_m = -INFINITY, ce_s = 0.f;
@@ -344,6 +370,10 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
     for (int c = slab * 4; c < slab * 4 + 4; ++c) {
       const int n0 = tn * BN + c * 32;
       if (n0 >= p.N) break;  // warp-uniform: the rest of this tile lies past N
+      uint4 cur[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) cur[q] = nxt[q];
+      load_in(c + 1);
       uint32_t r[32];
       tmem_ld_32x32b_x32(t_row + c * 32, r);
       tmem_ld_wait();
@@ -360,24 +390,22 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
         if (p.gelu) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
-          if (row_ok) {
-            __nv_bfloat16* aux = reinterpret_cast<__nv_bfloat16*>(p.aux) + row * p.ldaux + n0;
-            if (full) {
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                uint4 w;
-                w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-                w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-                w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-                w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-                reinterpret_cast<uint4*>(aux)[q] = w;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n0 + j < p.N) aux[j] = __float2bfloat16_rn(v[j]);
+          // The pre-activation goes out through the second slab of this warp
+          // (TMA store on tmX at the end of the slab); see the staging below.
+          if ((c & 1) == 0) {
+            if (es.ctr > 0) {
+              if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+              __syncwarp();
             }
+            sb = es.base;
           }
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                             smem_u32(es.base + kSlabBytes + sw128_off(lane, (c & 1) * 4 + q))),
+                         "r"(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1])), "r"(pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3])),
+                         "r"(pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5])), "r"(pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]))
+                         : "memory");
           // GELU of the bf16-rounded pre-activation: exactly what backward differentiates.
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
@@ -387,7 +415,7 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
           if (full) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              uint4 w = reinterpret_cast<const uint4*>(rs)[q];
+              const uint4 w = cur[q];
               float2 f0 = unpack_bf16x2(w.x), f1 = unpack_bf16x2(w.y), f2 = unpack_bf16x2(w.z),
                      f3 = unpack_bf16x2(w.w);
               v[q * 8 + 0] += f0.x; v[q * 8 + 1] += f0.y; v[q * 8 + 2] += f1.x; v[q * 8 + 3] += f1.y;
@@ -405,7 +433,7 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
           if (full) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              uint4 w = reinterpret_cast<const uint4*>(hx)[q];
+              const uint4 w = cur[q];
               float2 f0 = unpack_bf16x2(w.x), f1 = unpack_bf16x2(w.y), f2 = unpack_bf16x2(w.z),
                      f3 = unpack_bf16x2(w.w);
               v[q * 8 + 0] *= gelu_tanh_grad(f0.x); v[q * 8 + 1] *= gelu_tanh_grad(f0.y);
@@ -458,7 +486,8 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
                        : "memory");
         slab_issue(es, tmD, sb, f32_mode, to_ws ? 3 : 2, n0, row0, split);
       } else {
-        if ((c & 1) == 0) sb = slab_acquire(es);
+        const bool two = EPI == kEpiBF16 && p.gelu;  // output + pre-activation slabs (four epilogue warps)
+        if ((c & 1) == 0 && !two) sb = slab_acquire(es);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
@@ -466,7 +495,10 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
                        "r"(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1])), "r"(pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3])),
                        "r"(pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5])), "r"(pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]))
                        : "memory");
-        if ((c & 1) == 1 || n0 + 32 >= p.N) slab_issue(es, tmD, sb, 0, 2, n0 - (c & 1) * 32, row0, 0);
+        if ((c & 1) == 1 || n0 + 32 >= p.N) {
+          slab_issue(es, tmD, sb, 0, 2, n0 - (c & 1) * 32, row0, 0);
+          if (two) slab_issue(es, tmX, es.base + kSlabBytes, 0, 2, n0 - (c & 1) * 32, row0, 0);
+        }
       }
     }
     if (EPI == kEpiCE && row_ok) {
@@ -656,15 +688,16 @@ __device__ __forceinline__ int ar_pull_chunk(const MdGemmParams& p, const MdTpAr
 template <int CG, int EW, bool A_MN, bool B_MN, int EPI, bool AR = false>
 __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmD, const __grid_constant__ KParams kp) {
-  using C = Cfg<CG>;
+                const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmX,
+                const __grid_constant__ KParams kp) {
+  using C = Cfg<CG, EW>;
   constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * kABytes;
   uint8_t* sEpi = smem + kStages * C::kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + kEpiSmem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + C::kEpiSmem);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + kStages;
   uint64_t* tfull_bar = bars + 2 * kStages;
@@ -840,8 +873,8 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
       tempty_addr[1] = map_to_cta(tempty_addr[1], 0);
     }
     EpiStage es;
-    es.nbuf = EW == 8 ? 1 : 2;
-    es.base = sEpi + ew * es.nbuf * kSlabBytes;
+    es.nbuf = 2;
+    es.base = sEpi + ew * 2 * kSlabBytes;
     es.ctr = 0;
     es.lane = lane;
     int acc = 0;
@@ -854,7 +887,7 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
       const int row0 = tm * (CG * BM) + static_cast<int>(crank) * BM + quarter * 32;
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      epilogue_row<EPI>(p, &tmD, es, row0 + lane, row0, tn, split, t_row, c_begin, c_end);
+      epilogue_row<EPI>(p, &tmD, &tmX, es, row0 + lane, row0, tn, split, t_row, c_begin, c_end);
       if constexpr (AR) {
         // Publish this chunk of the partial product once its bulk stores have
         // completed (bulk-async writes, then a proxy fence, then the release).
@@ -1008,10 +1041,10 @@ bool make_out_map(CUtensorMap* map, void* ptr, bool f32, uint64_t inner, uint64_
 int g_num_sms = 0;
 
 template <int CG, int kEW, bool A_MN, bool B_MN, int EPI, bool AR = false>
-cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const md::gemm::KParams& kp,
-                   int grid, cudaStream_t stream) {
+cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& tx,
+                   const md::gemm::KParams& kp, int grid, cudaStream_t stream) {
   auto kern = md::gemm::gemm_kernel<CG, kEW, A_MN, B_MN, EPI, AR>;
-  constexpr int smem = md::gemm::Cfg<CG>::kSmemBytes;
+  constexpr int smem = md::gemm::Cfg<CG, kEW>::kSmemBytes;
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1039,28 +1072,28 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  return cudaLaunchKernelEx(&cfg, kern, ta, tb, td, kp);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, td, tx, kp);
 }
 
 template <int CG, int EW>
 cudaError_t dispatch(bool amn, bool bmn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
-                     const md::gemm::KParams& kp, int grid, cudaStream_t s, bool* bad) {
+                     const CUtensorMap& tx, const md::gemm::KParams& kp, int grid, cudaStream_t s, bool* bad) {
   using namespace md::gemm;
   *bad = false;
   if (!amn && !bmn) {
-    if (epi == kEpiBF16) return launch<CG, EW, false, false, kEpiBF16>(ta, tb, td, kp, grid, s);
-    if (epi == kEpiF32) return launch<CG, EW, false, false, kEpiF32>(ta, tb, td, kp, grid, s);
-    if (epi == kEpiCE) return launch<CG, EW, false, false, kEpiCE>(ta, tb, td, kp, grid, s);
+    if (epi == kEpiBF16) return launch<CG, EW, false, false, kEpiBF16>(ta, tb, td, tx, kp, grid, s);
+    if (epi == kEpiF32) return launch<CG, EW, false, false, kEpiF32>(ta, tb, td, tx, kp, grid, s);
+    if (epi == kEpiCE) return launch<CG, EW, false, false, kEpiCE>(ta, tb, td, tx, kp, grid, s);
   } else if (!amn && bmn) {
-    if (epi == kEpiBF16) return launch<CG, EW, false, true, kEpiBF16>(ta, tb, td, kp, grid, s);
-    if (epi == kEpiF32) return launch<CG, EW, false, true, kEpiF32>(ta, tb, td, kp, grid, s);
-    if (epi == kEpiDGELU) return launch<CG, EW, false, true, kEpiDGELU>(ta, tb, td, kp, grid, s);
+    if (epi == kEpiBF16) return launch<CG, EW, false, true, kEpiBF16>(ta, tb, td, tx, kp, grid, s);
+    if (epi == kEpiF32) return launch<CG, EW, false, true, kEpiF32>(ta, tb, td, tx, kp, grid, s);
+    if (epi == kEpiDGELU) return launch<CG, EW, false, true, kEpiDGELU>(ta, tb, td, tx, kp, grid, s);
   } else if (amn && bmn) {
-    if (epi == kEpiF32) return launch<CG, EW, true, true, kEpiF32>(ta, tb, td, kp, grid, s);
-    if (epi == kEpiBF16) return launch<CG, EW, true, true, kEpiBF16>(ta, tb, td, kp, grid, s);
+    if (epi == kEpiF32) return launch<CG, EW, true, true, kEpiF32>(ta, tb, td, tx, kp, grid, s);
+    if (epi == kEpiBF16) return launch<CG, EW, true, true, kEpiBF16>(ta, tb, td, tx, kp, grid, s);
   } else {
-    if (epi == kEpiF32) return launch<CG, EW, true, false, kEpiF32>(ta, tb, td, kp, grid, s);
-    if (epi == kEpiBF16) return launch<CG, EW, true, false, kEpiBF16>(ta, tb, td, kp, grid, s);
+    if (epi == kEpiF32) return launch<CG, EW, true, false, kEpiF32>(ta, tb, td, tx, kp, grid, s);
+    if (epi == kEpiBF16) return launch<CG, EW, true, false, kEpiBF16>(ta, tb, td, tx, kp, grid, s);
   }
   *bad = true;
   return cudaSuccess;
@@ -1105,8 +1138,14 @@ extern "C" int md_gemm(const MdGemmParams* prm, cudaStream_t stream) {
   if (cg != 1 && cg != 2) cg = p.a_mn_major ? (p.M >= 2304 ? 2 : 1) : (p.M >= 512 ? 2 : 1);
   // Four epilogue warps measured best across the GPT shapes (eight only
   // matched it for the GELU / cross-entropy epilogues).
+  // Eight epilogue warps where the epilogue does real work per element and the
+  // mainloop is too short to hide it (GELU, dGELU, cross-entropy statistics,
+  // residual add with K <= 1024); four (and one more mainloop stage)
+  // otherwise.  Measured in the GPT-2 step: fc+GELU 118 -> 97 us, proj+residual
+  // (K = 768) 41 -> 34 us; mlp.proj+residual (K = 3072) prefers four.
   if (p.epi_warps != 4 && p.epi_warps != 8)
-    p.epi_warps = (p.epi == kEpiCE || p.epi == kEpiDGELU || (p.epi == kEpiBF16 && p.gelu)) ? 8 : 4;
+    p.epi_warps = (p.epi == kEpiCE || p.epi == kEpiDGELU ||
+                   (p.epi == kEpiBF16 && (p.gelu || (p.resid && p.K <= 1024)))) ? 8 : 4;
 
   CUtensorMap ta, tb;
   bool ok;
@@ -1133,6 +1172,8 @@ extern "C" int md_gemm(const MdGemmParams* prm, cudaStream_t stream) {
   else
     ok = make_out_map(&td, p.D, p.epi == kEpiF32, p.N, p.M, p.ldd, 0);
   if (!ok) return -13;
+  CUtensorMap tx = td;  // second epilogue output: the GELU pre-activation
+  if (p.epi == kEpiBF16 && p.gelu && !make_out_map(&tx, p.aux, false, p.N, p.M, p.ldaux, 0)) return -14;
 
   int cap = p.num_sms > 0 ? p.num_sms : g_num_sms;
   int grid;
@@ -1152,11 +1193,11 @@ extern "C" int md_gemm(const MdGemmParams* prm, cudaStream_t stream) {
   const int ew = p.epi_warps == 4 ? 4 : 8;
   cudaError_t e;
   if (cg == 2) {
-    e = ew == 4 ? dispatch<2, 4>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, td, kp, grid, stream, &bad)
-                : dispatch<2, 8>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, td, kp, grid, stream, &bad);
+    e = ew == 4 ? dispatch<2, 4>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, td, tx, kp, grid, stream, &bad)
+                : dispatch<2, 8>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, td, tx, kp, grid, stream, &bad);
   } else {
-    e = ew == 4 ? dispatch<1, 4>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, td, kp, grid, stream, &bad)
-                : dispatch<1, 8>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, td, kp, grid, stream, &bad);
+    e = ew == 4 ? dispatch<1, 4>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, td, tx, kp, grid, stream, &bad)
+                : dispatch<1, 8>(p.a_mn_major, p.b_mn_major, p.epi, ta, tb, td, tx, kp, grid, stream, &bad);
   }
   if (bad) return -12;
   if (e != cudaSuccess) return static_cast<int>(e);
@@ -1238,11 +1279,11 @@ extern "C" int md_gemm_ar(const MdGemmParams* prm, const MdTpArParams* arp, cuda
   }
   cudaError_t e;
   if (p.b_mn_major)  // data-gradient products: dx = dy W
-    e = cg == 2 ? launch<2, 4, false, true, kEpiBF16, true>(ta, tb, td, kp, grid, stream)
-                : launch<1, 4, false, true, kEpiBF16, true>(ta, tb, td, kp, grid, stream);
+    e = cg == 2 ? launch<2, 4, false, true, kEpiBF16, true>(ta, tb, td, td, kp, grid, stream)
+                : launch<1, 4, false, true, kEpiBF16, true>(ta, tb, td, td, kp, grid, stream);
   else
-    e = cg == 2 ? launch<2, 4, false, false, kEpiBF16, true>(ta, tb, td, kp, grid, stream)
-                : launch<1, 4, false, false, kEpiBF16, true>(ta, tb, td, kp, grid, stream);
+    e = cg == 2 ? launch<2, 4, false, false, kEpiBF16, true>(ta, tb, td, td, kp, grid, stream)
+                : launch<1, 4, false, false, kEpiBF16, true>(ta, tb, td, td, kp, grid, stream);
   return static_cast<int>(e);
 }
 
