@@ -60,9 +60,16 @@ _REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_pow
 
 
 class ClockSampler:
-    def __init__(self, gpu_id: str):
-        self.gpu_id = gpu_id
-        self.rows: list[list[str]] = []
+    """One ``nvidia-smi -lms 200`` process per node, over every GPU of the run.
+
+    Started before the warm-up steps (its NVML start-up takes host CPU and must
+    not overlap the timed window); each sample is stamped on arrival and
+    :meth:`stop` keeps the samples inside ``[t0, t1]``, the timed window.
+    """
+
+    def __init__(self, gpu_ids: list[str]):
+        self.gpu_ids = gpu_ids
+        self.rows: list[tuple[float, list[str]]] = []
         self.proc = None
         self.thread = None
 
@@ -72,7 +79,8 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200", "-i", self.gpu_id],
+                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", ",".join(self.gpu_ids)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -84,9 +92,9 @@ class ClockSampler:
         for line in self.proc.stdout:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) == 8:
-                self.rows.append(parts)
+                self.rows.append((time.time(), parts))
 
-    def stop(self) -> dict:
+    def stop(self, t0: float, t1: float) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         self.proc.terminate()
@@ -96,21 +104,29 @@ class ClockSampler:
             self.proc.kill()
         if self.thread is not None:
             self.thread.join(timeout=5)
+
         def num(s):
             try:
                 return float(s)
             except ValueError:
                 return None
-        loaded = [r for r in self.rows if (num(r[3]) or 0) >= 50] or self.rows
+
+        # Samples inside the timed window (a sample arrives up to one period after it was taken).
+        window = [r for t, r in self.rows if t0 <= t <= t1 + 0.25]
+        if not window:  # window shorter than the sampling period: take the samples closest to it
+            near = sorted(self.rows, key=lambda tr: abs(tr[0] - (t0 + t1) / 2))
+            window = [r for _, r in near[: len(self.gpu_ids)]]
+        loaded = [r for r in window if (num(r[3]) or 0) >= 50] or window
         sm = [num(r[0]) for r in loaded if num(r[0]) is not None]
-        mx = [num(r[1]) for r in self.rows if num(r[1]) is not None]
+        mx = [num(r[1]) for _, r in self.rows if num(r[1]) is not None]
         reasons = sorted({name for r in loaded for name, v in zip(_REASONS, r[4:8]) if v.lower() == "active"})
         return {
             "sm_mhz": statistics.median(sm) if sm else None,
             "sm_max_mhz": max(mx) if mx else None,
             "reasons": reasons,
-            "samples": len(self.rows),
-            "power_w_max": max((num(r[2]) or 0) for r in self.rows) if self.rows else None,
+            "samples": len(window),
+            "gpus": len(self.gpu_ids),
+            "power_w_max": max((num(r[2]) or 0) for r in window) if window else None,
         }
 
 
@@ -190,7 +206,10 @@ def build(impl: str, world: int, seed: int):
     mesh = md.ParallelMesh(tp_size=1, pp_size=1)
     model = GPT(cfg, tp_group=mesh.tp_group, device=torch.device("cuda"))
     if world > 1:
-        model = md.DistributedDataParallel(model, process_group=mesh.dp_group, bucket_cap_mb=25.0)
+        # The last bucket (the token-embedding gradient, produced last in backward)
+        # finishes its all-reduce while FusedAdamW updates every other parameter.
+        model = md.DistributedDataParallel(model, process_group=mesh.dp_group, bucket_cap_mb=25.0,
+                                           defer_last_buckets=2)
     opt = make_opt(model.parameters())
 
     def step(ids, tgt):
@@ -243,26 +262,43 @@ def main() -> int:
     K, W = args.steps, args.warmup
     dev_batches = make_batches(K + W, rank, args.seed, cfg.vocab_size, pinned=False)
 
+    # Clock sampling: one nvidia-smi per node (local rank 0) over every GPU of
+    # this node's ranks, started before the warm-up so its start-up is over
+    # when the timed window opens.
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    uuids = [uuid]
+    if world > 1:
+        import torch.distributed as dist
+
+        allu = [None] * world
+        dist.all_gather_object(allu, (os.uname().nodename, uuid))
+        uuids = [u for n, u in allu if n == os.uname().nodename]
+    sampler = ClockSampler(uuids) if local == 0 else None
+    if sampler is not None:
+        sampler.start()
+
     for i in range(W):
         step(*dev_batches[i])
     torch.cuda.synchronize()
     barrier(world)
-
-    uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
-    sampler = ClockSampler(uuid)
-    sampler.start()
-    time.sleep(0.3)
-    barrier(world)
     torch.cuda.synchronize()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    host_t0 = time.time()
     t_start.record()
     loss = None
     for i in range(K):
         loss = step(*dev_batches[W + i])
     t_end.record()
     torch.cuda.synchronize()
+    host_t1 = time.time()
     barrier(world)
-    clocks = sampler.stop()
+    clocks = sampler.stop(host_t0, host_t1) if sampler is not None else None
+    if world > 1:
+        import torch.distributed as dist
+
+        got = [None] * world
+        dist.all_gather_object(got, clocks)
+        clocks = got[0]
     ms = max_over_ranks(t_start.elapsed_time(t_end) / K, world)
     final_loss = float(loss.detach().float().item())
 

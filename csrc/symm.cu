@@ -102,7 +102,8 @@ __device__ bool cta_barrier(const P& p, uint32_t value, uint32_t where) {
   __syncthreads();
   const int peer = threadIdx.x;
   if (peer < p.world) {
-    __threadfence_system();
+    // The release store orders this CTA's earlier writes (ordered before it by
+    // the __syncthreads above) at system scope; no separate fence needed.
     st_release_sys(p.flags[peer] + flag_idx(p.channel, blockIdx.x, p.rank), value);
     const uint32_t* mine = p.flags[p.rank] + flag_idx(p.channel, blockIdx.x, peer);
     const uint64_t t0 = globaltimer_ns();
@@ -133,12 +134,19 @@ __global__ void __launch_bounds__(512) md_ar_bucket_kernel(const __grid_constant
   for (int r = 0; r < kMaxWorld; ++r)
     bases[r] = r < p.world ? reinterpret_cast<float4*>(p.bufs[r] + p.offset) : nullptr;
 
-  for (long long u = lo + static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; u < hi; u += stride) {
-    float4 v[kMaxWorld];
+  // Two vectors per thread per step, every rank's loads of both issued before
+  // any sum: twice the bytes in flight per thread (NVLink latency is ~us).
+  for (long long u = lo + static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; u < hi; u += 2 * stride) {
+    const long long u2 = u + stride;
+    const bool two = u2 < hi;
+    float4 v[kMaxWorld], w[kMaxWorld];
 #pragma unroll
     for (int r = 0; r < kMaxWorld; ++r)
-      if (r < p.world) v[r] = __ldcg(bases[r] + u);
-    float4 s = v[0];
+      if (r < p.world) {
+        v[r] = __ldcg(bases[r] + u);
+        if (two) w[r] = __ldcg(bases[r] + u2);
+      }
+    float4 s = v[0], t = w[0];
 #pragma unroll
     for (int r = 1; r < kMaxWorld; ++r)
       if (r < p.world) {
@@ -146,14 +154,25 @@ __global__ void __launch_bounds__(512) md_ar_bucket_kernel(const __grid_constant
         s.y += v[r].y;
         s.z += v[r].z;
         s.w += v[r].w;
+        t.x += w[r].x;
+        t.y += w[r].y;
+        t.z += w[r].z;
+        t.w += w[r].w;
       }
     s.x *= p.scale;
     s.y *= p.scale;
     s.z *= p.scale;
     s.w *= p.scale;
+    t.x *= p.scale;
+    t.y *= p.scale;
+    t.z *= p.scale;
+    t.w *= p.scale;
 #pragma unroll
     for (int r = 0; r < kMaxWorld; ++r)
-      if (r < p.world) __stcg(bases[r] + u, s);
+      if (r < p.world) {
+        __stcg(bases[r] + u, s);
+        if (two) __stcg(bases[r] + u2, t);
+      }
   }
   cta_barrier(p, depart, 101);
 }
@@ -268,7 +287,7 @@ int md_allreduce_ctas(long long n, int world) {
   const long long per4 = (n / 4 + world - 1) / world;
   long long g = (per4 + 512 * 4 - 1) / (512 * 4);
   if (g < 1) g = 1;
-  if (g > 32) g = 32;
+  if (g > md::symm::kMaxCtas) g = md::symm::kMaxCtas;
   return static_cast<int>(g);
 }
 

@@ -85,8 +85,18 @@ class DistributedDataParallel(nn.Module):
         broadcast_parameters: bool = True,
         overlap_with_backward: bool = True,
         src: int = 0,
+        defer_last_buckets: int = 0,
     ):
+        """``defer_last_buckets = k``: backward returns without waiting for the all-reduce
+        of the last ``k`` buckets (on the fused peer-memory reducer, whose work is a CUDA
+        event).  Their parameters carry the event as ``_md_grad_event``;
+        :class:`minidist.optim.FusedAdamW` updates every other parameter first and waits on
+        the events only for those, so the all-reduce of the gradients produced last in
+        backward (the token embedding) overlaps the optimizer.  Other consumers of the
+        gradients call :meth:`wait_gradients` first."""
         super().__init__()
+        self.defer_last_buckets = int(defer_last_buckets)
+        self._deferred: list = []
         self.module = module
         self.process_group = process_group
         self.world_size = comm.get_world_size(process_group)
@@ -214,14 +224,31 @@ class DistributedDataParallel(nn.Module):
         while self._next_to_launch < len(self._buckets):
             self._launch(self._buckets[self._next_to_launch])
             self._next_to_launch += 1
+        tail = {id(b) for b in self._buckets[len(self._buckets) - self.defer_last_buckets:]} \
+            if self.defer_last_buckets > 0 else set()
+        self._deferred = []
         for b in self._buckets:
             if b.launched:
-                self._reducer.wait(b)
+                if id(b) in tail and isinstance(b.work, torch.cuda.Event):
+                    for p in b.params:
+                        p._md_grad_event = b.work
+                    self._deferred.extend(b.params)
+                else:
+                    self._reducer.wait(b)
             b.reset()
         self._next_to_launch = 0
         self._ready.clear()
 
     # -- public API --------------------------------------------------------------
+
+    def wait_gradients(self) -> None:
+        """Make the current stream wait for the deferred buckets (see ``defer_last_buckets``)."""
+        for p in self._deferred:
+            ev = getattr(p, "_md_grad_event", None)
+            if ev is not None:
+                torch.cuda.current_stream().wait_event(ev)
+                p._md_grad_event = None
+        self._deferred = []
 
     @contextmanager
     def no_sync(self) -> Iterator[None]:

@@ -51,8 +51,9 @@ class FusedAdamW(torch.optim.Optimizer):
             if not params:
                 continue
             states = [self._state(p) for p in params]
-            for st in states:
-                st["step"] += 1
+            # One multi-tensor op for every parameter's step count (a per-tensor
+            # loop of CPU adds cost ~0.6 ms of host time per step at GPT-2 size).
+            torch._foreach_add_([st["step"] for st in states], 1.0)
             t = float(states[0]["step"])
             b1, b2 = group["betas"]
             lr, eps, wd = group["lr"], group["eps"], group["weight_decay"]
@@ -62,7 +63,20 @@ class FusedAdamW(torch.optim.Optimizer):
             fused = [p for p, c in zip(params, cuda) if c]
             rest = [p for p, c in zip(params, cuda) if not c]
             if fused:
-                self._fused_update(gi, fused, lr, b1, b2, eps, wd, bc1, bc2_sqrt)
+                # Parameters whose gradient all-reduce is still in flight (DDP with
+                # defer_last_buckets) are updated last, after waiting on its event.
+                late = [p for p in fused if getattr(p, "_md_grad_event", None) is not None]
+                if late:
+                    early = [p for p in fused if getattr(p, "_md_grad_event", None) is None]
+                    if early:
+                        self._fused_update((gi, 0), early, lr, b1, b2, eps, wd, bc1, bc2_sqrt)
+                    for ev in {id(p._md_grad_event): p._md_grad_event for p in late}.values():
+                        torch.cuda.current_stream().wait_event(ev)
+                    for p in late:
+                        p._md_grad_event = None
+                    self._fused_update((gi, 1), late, lr, b1, b2, eps, wd, bc1, bc2_sqrt)
+                else:
+                    self._fused_update(gi, fused, lr, b1, b2, eps, wd, bc1, bc2_sqrt)
                 self._ensure_grad_buffers()
             for p in rest:
                 st = self.state[p]

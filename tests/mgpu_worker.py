@@ -47,7 +47,7 @@ def check_ddp(rank, world):
     mesh = md.ParallelMesh(tp_size=1)  # data parallel: each rank holds the whole model
     ref = GPT(cfg, tp_group=mesh.tp_group, device="cuda")
     model = md.DistributedDataParallel(GPT(cfg, tp_group=mesh.tp_group, device="cuda"),
-                                       process_group=mesh.dp_group, bucket_cap_mb=1.0)
+                                       process_group=mesh.dp_group, bucket_cap_mb=1.0, defer_last_buckets=2)
     assert model.reducer_name == "fused-nvlink", model.reducer_name
     g = torch.Generator().manual_seed(7)
     ids = torch.randint(0, cfg.vocab_size, (2 * world, 128), generator=g).cuda()
@@ -55,6 +55,7 @@ def check_ddp(rank, world):
     with torch.autocast("cuda", dtype=torch.bfloat16):
         ref(ids, tgt)[1].backward()
         model(ids.chunk(world)[rank], tgt.chunk(world)[rank])[1].backward()
+    model.wait_gradients()  # the last bucket is deferred (defer_last_buckets=2)
     torch.cuda.synchronize()
     for (n, p), (_, q) in zip(model.module.named_parameters(), ref.named_parameters()):
         err = ((p.grad - q.grad).abs().max() / q.grad.abs().max().clamp(min=1e-8)).item()
