@@ -2,6 +2,7 @@
 """Row-parallel linear with its all-reduce: fused kernel vs GEMM + NCCL.
 
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 benchmarks/bench_tp_gemm.py
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 benchmarks/bench_tp_gemm.py --sweep baseline
 
 For each shape (M tokens, K = input features per rank, N = output features)
 it times, on the device (CUDA events, max over ranks, after warm-up):
@@ -75,16 +76,20 @@ def main() -> None:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--k-scale", type=float, default=None,
-                   help="multiply K by 8/W so the per-rank K matches tp=W (default: on)")
+    p.add_argument("--sweep", default="gpt", choices=["gpt", "baseline"],
+                   help="gpt: GPT-2 small / 6.7B layer shapes (K per rank as at tp=8); "
+                        "baseline: M in {2048, 8192, 32768}, K = N = 4096 (K split over the ranks)")
     args = p.parse_args()
     rank, world, device = init_distributed(backend="nccl")
     peak = _peak_tflops() * 1e12
     print_rank0(f"\n  row-parallel GEMM + all-reduce, W={world}  (times: max over ranks)")
     print_rank0(f"  {'M':>6}{'K':>6}{'N':>6}{'fused us':>10}{'nccl us':>10}{'speedup':>9}{'roofline us':>13}{'frac':>7}"
                 f"{'host us (fused/nccl)':>22}")
-    for M, K8, N in SHAPES:
-        K = max(64, K8 * 8 // world)
+    if args.sweep == "baseline":
+        shapes = [(M, 4096 // world, 4096) for M in (2048, 8192, 32768)]
+    else:
+        shapes = [(M, max(64, K8 * 8 // world), N) for M, K8, N in SHAPES]
+    for M, K, N in shapes:
         g = torch.Generator(device="cuda").manual_seed(rank)
         x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
         w = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
