@@ -98,6 +98,17 @@ class ParallelMesh:
                 g = dist.new_group(ranks)
                 if self.rank in ranks:
                     self._groups[axis] = g
+        # A second pipeline group carries the backward (gradient) traffic, so on
+        # NCCL the two directions run on separate communicator streams: a send of
+        # the next activation can then never sit in front of the receive of the
+        # current gradient.  Created after every reference group, so the order of
+        # the groups above is unchanged.
+        self._groups["pp_grad"] = self._groups["pp"]
+        if self.pp_size > 1:
+            for ranks in self._axis_rank_lists("pp"):
+                g = dist.new_group(ranks)
+                if self.rank in ranks:
+                    self._groups["pp_grad"] = g
 
     def axis_ranks(self, axis: str) -> list[int]:
         """Global ranks of this rank's group along ``axis`` ("tp", "dp" or "pp"), in axis order."""
@@ -114,6 +125,11 @@ class ParallelMesh:
     @property
     def pp_group(self):
         return self._groups["pp"]
+
+    @property
+    def pp_grad_group(self):
+        """Same ranks as :attr:`pp_group`; the pipeline sends gradients on it."""
+        return self._groups["pp_grad"]
 
     @property
     def is_first_stage(self) -> bool:
