@@ -1,0 +1,144 @@
+#!/usr/bin/env python3
+"""Single-GPU driver of the fused collective kernels, for ncu captures.
+
+    python benchmarks/fused_kernels_1gpu.py --kernel gemm_ar --iters 3
+    python benchmarks/fused_kernels_1gpu.py --kernel ddp_ar --iters 3
+    python benchmarks/fused_kernels_1gpu.py --kernel fsdp_rs --iters 3
+
+ncu profiles one process on one GPU, so this runs each kernel with a group of
+one rank on ordinary device buffers (every "peer" pointer is this rank's own
+buffer): the GEMM, epilogue, staging and memory structure are the real
+kernels'; the NVLink side is measured on several GPUs by
+benchmarks/bench_tp_gemm.py and benchmarks/bench_collectives.py.
+
+* ``gemm_ar``  -- md_gemm_ar (GEMM + tensor-parallel all-reduce), M=8192,
+  K=512, N=4096 (the 6.7B attention projection at tp=8), bias + residual.
+* ``ddp_ar``   -- md_ar_bucket_kernel on a 25 MB fp32 bucket (1/W scale).
+* ``fsdp_rs``  -- md_rs_shard_kernel with the in-kernel AdamW on a 40 M-element shard.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import sys
+from pathlib import Path
+
+import torch
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+
+from minidist.ops import _native as nat  # noqa: E402
+from minidist.ops import gemm as G  # noqa: E402
+from minidist.parallel import collectives as C  # noqa: E402
+
+
+def timed(fn, iters: int) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    b.synchronize()
+    return a.elapsed_time(b) / iters / 1e3
+
+
+def run_gemm_ar(iters: int) -> None:
+    M, K, N = 8192, 512, 4096
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    bias = torch.randn(N, device="cuda")
+    resid = torch.randn(M, N, device="cuda").bfloat16()
+    part = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    fin = torch.empty_like(part)
+    chunks = (M + 31) // 32 * ((N + 255) // 256)
+    flags = torch.zeros(2 * chunks, dtype=torch.int32, device="cuda")
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ar = C.TpArParams()
+    ar.partial[0], ar.fin[0], ar.flags[0] = part.data_ptr(), fin.data_ptr(), flags.data_ptr()
+    ar.ldp, ar.out, ar.ldo = N, out.data_ptr(), N
+    ar.bias, ar.resid, ar.ldr = bias.data_ptr(), resid.data_ptr(), N
+    ar.world, ar.rank, ar.max_chunks, ar.timeout_ns = 1, 0, chunks, 10**10
+    gp = nat.GemmParams()
+    gp.A, gp.B, gp.lda, gp.ldb = x.data_ptr(), w.data_ptr(), K, K
+    gp.M, gp.N, gp.K, gp.epi, gp.alpha = M, N, K, G.EPI_BF16, 1.0
+    gp.status = nat.status_ptr()
+    state = {"epoch": 0}
+
+    def call():
+        state["epoch"] += 1
+        ar.epoch = state["epoch"]
+        nat.check(nat.lib().md_gemm_ar(ctypes.byref(gp), ctypes.byref(ar), ctypes.c_void_p(nat.stream_ptr())),
+                  "md_gemm_ar")
+
+    t = timed(call, iters)
+    nat.check_status()
+    want = (x.float() @ w.float().t() + bias + resid.float())
+    err = ((out.float() - want).abs().max() / want.abs().max()).item()
+    print(f"md_gemm_ar world=1 M={M} K={K} N={N}: {t * 1e6:.1f} us, {2 * M * N * K / t / 1e12:.0f} TFLOP/s, "
+          f"rel err {err:.2e}")
+
+
+def run_ddp_ar(iters: int) -> None:
+    n = 25 * 1024 * 1024 // 4 // 64 * 64
+    buf = torch.randn(n, device="cuda")
+    flags = torch.zeros(int(nat.lib().md_symm_flag_bytes()) // 4, dtype=torch.int32, device="cuda")
+    p = C.ArParams()
+    p.bufs[0], p.flags[0] = buf.data_ptr(), flags.data_ptr()
+    p.offset, p.n, p.world, p.rank, p.scale, p.channel = 0, n, 1, 0, 1.0, 0
+    p.timeout_ns, p.status = 10**10, nat.status_ptr()
+    ctas = nat.lib().md_allreduce_ctas(n, 1)
+    state = {"epoch": 0}
+
+    def call():
+        state["epoch"] += 1
+        p.epoch = state["epoch"]
+        nat.check(nat.lib().md_allreduce(ctypes.byref(p), ctas, ctypes.c_void_p(nat.stream_ptr())), "md_allreduce")
+
+    t = timed(call, iters)
+    nat.check_status()
+    print(f"md_ar_bucket world=1 25 MB: {t * 1e6:.1f} us, {2 * n * 4 / t / 1e9:.0f} GB/s (read + write)")
+
+
+def run_fsdp_rs(iters: int) -> None:
+    shard = 40 * 1024 * 1024
+    grads = torch.randn(shard, device="cuda")
+    flags = torch.zeros(int(nat.lib().md_symm_flag_bytes()) // 4, dtype=torch.int32, device="cuda")
+    pmv = [torch.randn(shard, device="cuda") for _ in range(2)] + [torch.rand(shard, device="cuda")]
+    r = C.RsParams()
+    r.bufs[0], r.flags[0] = grads.data_ptr(), flags.data_ptr()
+    r.offset, r.shard, r.world, r.rank, r.scale, r.channel = 0, shard, 1, 0, 1.0, 4
+    r.timeout_ns, r.status = 10**10, nat.status_ptr()
+    r.p, r.m, r.v = (t.data_ptr() for t in pmv)
+    r.lr, r.b1, r.b2, r.eps, r.wd, r.bc1, r.bc2_sqrt = 1e-4, 0.9, 0.999, 1e-8, 0.01, 0.1, 0.0316
+    state = {"epoch": 0}
+
+    def call():
+        state["epoch"] += 1
+        r.epoch = state["epoch"]
+        nat.check(nat.lib().md_rs_shard(ctypes.byref(r), nat.num_sms(), ctypes.c_void_p(nat.stream_ptr())), "md_rs_shard")
+
+    t = timed(call, iters)
+    nat.check_status()
+    print(f"md_rs_shard+AdamW world=1 {shard / 1e6:.0f} M elements: {t * 1e6:.1f} us, "
+          f"{7 * shard * 4 / t / 1e9:.0f} GB/s (g, p, m, v read + p, m, v write)")
+
+
+def main() -> None:
+    a = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    a.add_argument("--kernel", default="all", choices=["all", "gemm_ar", "ddp_ar", "fsdp_rs"])
+    a.add_argument("--iters", type=int, default=20)
+    args = a.parse_args()
+    if args.kernel in ("all", "gemm_ar"):
+        run_gemm_ar(args.iters)
+    if args.kernel in ("all", "ddp_ar"):
+        run_ddp_ar(args.iters)
+    if args.kernel in ("all", "fsdp_rs"):
+        run_fsdp_rs(args.iters)
+
+
+if __name__ == "__main__":
+    main()

@@ -31,7 +31,8 @@ namespace md {
 namespace symm {
 
 constexpr int kMaxWorld = 8;
-constexpr int kMaxCtas = 64;
+constexpr int kMaxCtas = 160;     // flag slots per channel (one CTA per SM for the shard kernel)
+constexpr int kArMaxCtas = 64;    // bucket all-reduce: leaves SMs to the backward it overlaps
 constexpr int kChannels = 8;
 
 }  // namespace symm
@@ -187,20 +188,9 @@ __global__ void __launch_bounds__(512) md_rs_shard_kernel(const __grid_constant_
 #pragma unroll
   for (int r = 0; r < kMaxWorld; ++r) srcs[r] = r < p.world ? reinterpret_cast<const float4*>(p.bufs[r]) + base : nullptr;
   const float step = p.lr / p.bc1, decay = 1.f - p.lr * p.wd;
-  for (long long u = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; u < n4; u += stride) {
-    float4 v[kMaxWorld];
-#pragma unroll
-    for (int r = 0; r < kMaxWorld; ++r)
-      if (r < p.world) v[r] = __ldcg(srcs[r] + u);
-    float4 s = v[0];
-#pragma unroll
-    for (int r = 1; r < kMaxWorld; ++r)
-      if (r < p.world) {
-        s.x += v[r].x;
-        s.y += v[r].y;
-        s.z += v[r].z;
-        s.w += v[r].w;
-      }
+  // Two vectors per thread per step (all loads of both issued first) to keep
+  // enough bytes in flight for a streaming kernel.
+  auto finish = [&](long long u, float4 s) {
     s.x *= p.scale;
     s.y *= p.scale;
     s.z *= p.scale;
@@ -232,6 +222,32 @@ __global__ void __launch_bounds__(512) md_rs_shard_kernel(const __grid_constant_
       }
       *g = s;
     }
+  };
+  for (long long u = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; u < n4; u += 2 * stride) {
+    const long long u2 = u + stride;
+    const bool two = u2 < n4;
+    float4 v[kMaxWorld], w[kMaxWorld];
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r)
+      if (r < p.world) {
+        v[r] = __ldcg(srcs[r] + u);
+        if (two) w[r] = __ldcg(srcs[r] + u2);
+      }
+    float4 s = v[0], t = w[0];
+#pragma unroll
+    for (int r = 1; r < kMaxWorld; ++r)
+      if (r < p.world) {
+        s.x += v[r].x;
+        s.y += v[r].y;
+        s.z += v[r].z;
+        s.w += v[r].w;
+        t.x += w[r].x;
+        t.y += w[r].y;
+        t.z += w[r].z;
+        t.w += w[r].w;
+      }
+    finish(u, s);
+    if (two) finish(u2, t);
   }
   // No rank rewrites its gradient buffer before every peer has read it.
   cta_barrier(p, depart, 111);
@@ -287,7 +303,7 @@ int md_allreduce_ctas(long long n, int world) {
   const long long per4 = (n / 4 + world - 1) / world;
   long long g = (per4 + 512 * 4 - 1) / (512 * 4);
   if (g < 1) g = 1;
-  if (g > md::symm::kMaxCtas) g = md::symm::kMaxCtas;
+  if (g > md::symm::kArMaxCtas) g = md::symm::kArMaxCtas;
   return static_cast<int>(g);
 }
 

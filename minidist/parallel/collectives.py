@@ -333,7 +333,7 @@ def reduce_scatter_shard(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_of
     else:
         prm.grad_out = grad_out.data_ptr()
         prm.accumulate = int(accumulate)
-    ctas = min(64, max(1, shard // (4 * 512 * 4)))
+    ctas = min(nat.num_sms(), 160, max(1, shard // (4 * 512 * 8)))
     rc = nat.lib().md_rs_shard(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr(None)))
     nat.check(rc, "md_rs_shard")
     n = shard * comm_.world * 4
