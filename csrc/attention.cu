@@ -259,6 +259,42 @@ __global__ void __launch_bounds__(256) fwd_kernel(const __nv_bfloat16* __restric
 template <int D>
 __global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, long long ldo, const __nv_bfloat16* __restrict__ dout,
                              long long lddo, float* __restrict__ delta, int B, int H, int S) {
+  if constexpr (D == 64 || D == 128) {
+    // D/8 lanes per (row, head): each lane one 16-byte vector of O and dO
+    // (consecutive lanes, consecutive bytes), then a shuffle reduction.
+    constexpr int L = D / 8;
+    constexpr int kItemsPerWarp = 32 / L;
+    const long long total = static_cast<long long>(B) * H * S;
+    const int lane = threadIdx.x & 31, sub = lane % L;
+    const long long warp_id = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) / 32;
+    const long long warps = static_cast<long long>(gridDim.x) * blockDim.x / 32;
+    // Warp-uniform loop (the shuffle needs every lane), predicated per item.
+    for (long long base = warp_id * kItemsPerWarp; base < total; base += warps * kItemsPerWarp) {
+      const long long i = base + lane / L;
+      const bool valid = i < total;
+      float acc = 0.f;
+      long long bh = 0;
+      int q = 0;
+      if (valid) {
+        q = static_cast<int>(i % S);
+        bh = i / S;
+        const int h = static_cast<int>(bh % H);
+        const long long row = (bh / H) * S + q;
+        const uint4 a = reinterpret_cast<const uint4*>(o + row * ldo + h * D)[sub];
+        const uint4 c = reinterpret_cast<const uint4*>(dout + row * lddo + h * D)[sub];
+        const uint32_t as[4] = {a.x, a.y, a.z, a.w}, cs[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 fa = unpack_bf16x2(as[e]), fc = unpack_bf16x2(cs[e]);
+          acc += fa.x * fc.x + fa.y * fc.y;
+        }
+      }
+#pragma unroll
+      for (int off = L / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off);
+      if (valid && sub == 0) delta[bh * S + q] = acc;
+    }
+    return;
+  }
   const long long total = static_cast<long long>(B) * H * S;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -288,6 +324,26 @@ __global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, long long ldo,
 template <int D>
 __global__ void dq_convert_kernel(const float* __restrict__ dqacc, long long lda, __nv_bfloat16* __restrict__ dqkv,
                                   long long lddq, int M, int H, float scale) {
+  if constexpr (D % 8 == 0) {
+    // Eight elements per thread: two 16-byte loads, one 16-byte store.
+    const long long total = static_cast<long long>(M) * H * (D / 8);
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+      const int c8 = static_cast<int>(i % (D / 8));
+      const long long rh = i / (D / 8);
+      const int h = static_cast<int>(rh % H);
+      const long long row = rh / H;
+      const float4* src = reinterpret_cast<const float4*>(dqacc + row * lda + h * D + 8 * c8);
+      const float4 v0 = src[0], v1 = src[1];
+      uint4 w;
+      w.x = pack_bf16x2(v0.x * scale, v0.y * scale);
+      w.y = pack_bf16x2(v0.z * scale, v0.w * scale);
+      w.z = pack_bf16x2(v1.x * scale, v1.y * scale);
+      w.w = pack_bf16x2(v1.z * scale, v1.w * scale);
+      *reinterpret_cast<uint4*>(dqkv + row * lddq + h * 3 * D + 8 * c8) = w;
+    }
+    return;
+  }
   const long long total = static_cast<long long>(M) * H * (D / 2);
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {

@@ -268,3 +268,28 @@ def broadcast(tensor, src: int, group=None, async_op: bool = False):
     n = _nbytes(tensor)
     comm_stats.add("broadcast", n, n)
     return dist.broadcast(tensor, src=src, group=group, async_op=async_op)
+
+
+def check_same_layout(params, group=None, what: str = "module") -> None:
+    """Raise on every rank if the parameter layout (shapes, dtypes, order) differs across ``group``.
+
+    DDP and FSDP call this before their first collective: with mismatched
+    layouts the parameter broadcast and the bucket / shard collectives would
+    otherwise fail in confusing ways or wait until the process-group timeout.
+    One 64-bit digest per rank is all-gathered.
+    """
+    import hashlib
+
+    if not is_distributed() or get_world_size(group) == 1:
+        return
+    desc = repr([(tuple(p.shape), str(p.dtype)) for p in params]).encode()
+    digest = int.from_bytes(hashlib.sha256(desc).digest()[:8], "little", signed=True)
+    dev = current_device() if dist.get_backend(group) == "nccl" else torch.device("cpu")
+    mine = torch.tensor([digest], dtype=torch.int64, device=dev)
+    out = torch.empty(get_world_size(group), dtype=torch.int64, device=dev)
+    dist.all_gather_into_tensor(out, mine, group=group)
+    vals = out.tolist()
+    if any(v != vals[0] for v in vals):
+        bad = [r for r, v in enumerate(vals) if v != vals[0]]
+        raise RuntimeError(f"{what}: parameter layout differs across ranks (ranks {bad} differ from rank 0); "
+                           "every rank must build the same model")

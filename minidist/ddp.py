@@ -97,6 +97,7 @@ class DistributedDataParallel(nn.Module):
         super().__init__()
         self.defer_last_buckets = int(defer_last_buckets)
         self._deferred: list = []
+        comm.check_same_layout(list(module.parameters()), process_group, "DistributedDataParallel")
         self.module = module
         self.process_group = process_group
         self.world_size = comm.get_world_size(process_group)

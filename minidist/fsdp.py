@@ -271,6 +271,7 @@ class FullyShardedDataParallel(nn.Module):
         each shard inside the gradient reduce-scatter kernel, right when the unit's gradients are
         complete (peer-memory path only; no separate optimizer for these parameters)."""
         super().__init__()
+        comm.check_same_layout(list(module.parameters()), process_group, "FullyShardedDataParallel")
         self.module = module
         self.process_group = process_group
         self.world_size = comm.get_world_size(process_group)
