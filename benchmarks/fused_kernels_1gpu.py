@@ -4,6 +4,7 @@
     python benchmarks/fused_kernels_1gpu.py --kernel gemm_ar --iters 3
     python benchmarks/fused_kernels_1gpu.py --kernel ddp_ar --iters 3
     python benchmarks/fused_kernels_1gpu.py --kernel fsdp_rs --iters 3
+    python benchmarks/fused_kernels_1gpu.py --kernel fsdp_ag --iters 3
 
 ncu profiles one process on one GPU, so this runs each kernel with a group of
 one rank on ordinary device buffers (every "peer" pointer is this rank's own
@@ -15,6 +16,7 @@ benchmarks/bench_tp_gemm.py and benchmarks/bench_collectives.py.
   K=512, N=4096 (the 6.7B attention projection at tp=8), bias + residual.
 * ``ddp_ar``   -- md_ar_bucket_kernel on a 25 MB fp32 bucket (1/W scale).
 * ``fsdp_rs``  -- md_rs_shard_kernel with the in-kernel AdamW on a 40 M-element shard.
+* ``fsdp_ag``  -- md_ag_shards_kernel: a 40 M-element fp32 shard gathered as bf16.
 """
 
 from __future__ import annotations
@@ -62,6 +64,8 @@ def run_gemm_ar(iters: int) -> None:
     ar.ldp, ar.out, ar.ldo = N, out.data_ptr(), N
     ar.bias, ar.resid, ar.ldr = bias.data_ptr(), resid.data_ptr(), N
     ar.world, ar.rank, ar.max_chunks, ar.timeout_ns = 1, 0, chunks, 10**10
+    claim = torch.zeros(2, dtype=torch.int32, device="cuda")
+    ar.claim = claim.data_ptr()
     gp = nat.GemmParams()
     gp.A, gp.B, gp.lda, gp.ldb = x.data_ptr(), w.data_ptr(), K, K
     gp.M, gp.N, gp.K, gp.epi, gp.alpha = M, N, K, G.EPI_BF16, 1.0
@@ -78,6 +82,7 @@ def run_gemm_ar(iters: int) -> None:
     nat.check_status()
     want = (x.float() @ w.float().t() + bias + resid.float())
     err = ((out.float() - want).abs().max() / want.abs().max()).item()
+    assert claim.tolist() == [0, 0], "cluster-order counters not reset"
     print(f"md_gemm_ar world=1 M={M} K={K} N={N}: {t * 1e6:.1f} us, {2 * M * N * K / t / 1e12:.0f} TFLOP/s, "
           f"rel err {err:.2e}")
 
@@ -127,9 +132,33 @@ def run_fsdp_rs(iters: int) -> None:
           f"{7 * shard * 4 / t / 1e9:.0f} GB/s (g, p, m, v read + p, m, v write)")
 
 
+def run_fsdp_ag(iters: int) -> None:
+    shard = 40 * 1024 * 1024
+    src = torch.randn(shard, device="cuda")
+    out = torch.empty(shard, dtype=torch.bfloat16, device="cuda")
+    flags = torch.zeros(int(nat.lib().md_symm_flag_bytes()) // 4, dtype=torch.int32, device="cuda")
+    a = C.AgParams()
+    a.bufs[0], a.flags[0] = src.data_ptr(), flags.data_ptr()
+    a.offset, a.shard, a.world, a.rank, a.channel = 0, shard, 1, 0, 5
+    a.timeout_ns, a.status = 10**10, nat.status_ptr()
+    a.out, a.out_bf16 = out.data_ptr(), 1
+    state = {"epoch": 0}
+
+    def call():
+        state["epoch"] += 1
+        a.epoch = state["epoch"]
+        nat.check(nat.lib().md_ag_shards(ctypes.byref(a), 64, ctypes.c_void_p(nat.stream_ptr())), "md_ag_shards")
+
+    t = timed(call, iters)
+    nat.check_status()
+    assert torch.equal(out, src.bfloat16())
+    print(f"md_ag_shards world=1 {shard / 1e6:.0f} M elements fp32->bf16: {t * 1e6:.1f} us, "
+          f"{6 * shard / t / 1e9:.0f} GB/s (read + write)")
+
+
 def main() -> None:
     a = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    a.add_argument("--kernel", default="all", choices=["all", "gemm_ar", "ddp_ar", "fsdp_rs"])
+    a.add_argument("--kernel", default="all", choices=["all", "gemm_ar", "ddp_ar", "fsdp_rs", "fsdp_ag"])
     a.add_argument("--iters", type=int, default=20)
     args = a.parse_args()
     if args.kernel in ("all", "gemm_ar"):
@@ -138,6 +167,8 @@ def main() -> None:
         run_ddp_ar(args.iters)
     if args.kernel in ("all", "fsdp_rs"):
         run_fsdp_rs(args.iters)
+    if args.kernel in ("all", "fsdp_ag"):
+        run_fsdp_ag(args.iters)
 
 
 if __name__ == "__main__":

@@ -133,6 +133,12 @@ struct MdTpArParams {
   int max_chunks;
   unsigned long long timeout_ns;
   unsigned long long* trace;  // optional analysis trace ([64][8] %globaltimer stamps of CTA 0), or null
+  // This rank's {claimed, finished} cluster counters (2 x u32, zero between
+  // launches), or null for blockIdx order.  Clusters take their tile-walk
+  // index in the order they become resident, so when another kernel holds
+  // some SMs the resident clusters of every rank are the same prefix 0..k-1
+  // and pair up across ranks instead of waiting on clusters not yet running.
+  unsigned* claim;
 };
 
 namespace md {
@@ -705,13 +711,14 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
   uint64_t* drain_bar = bars + 2 * kStages + 4;
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * kStages + 6);
+  int* vcid_slot = reinterpret_cast<int*>(bars + 2 * kStages + 7);
 
   const MdGemmParams& p = kp.p;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t crank = CG == 2 ? cluster_ctarank() : 0u;
   const bool leader = crank == 0;
-  const int cluster_id = CG == 2 ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  int cluster_id = CG == 2 ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int nclusters = CG == 2 ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
@@ -725,6 +732,13 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
+    if constexpr (AR) {
+      if (kp.ar.claim != nullptr && leader) {
+        const unsigned v = atomicAdd(kp.ar.claim, 1u);
+        *vcid_slot = v < static_cast<unsigned>(nclusters) ? static_cast<int>(v) : nclusters;
+        if (v >= static_cast<unsigned>(nclusters)) report(p.status, kTimeoutPeer, 49, v);
+      }
+    }
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -744,6 +758,18 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
   if constexpr (CG == 2) cluster_sync();  // peer barriers exist before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
+  if constexpr (AR) {
+    if (kp.ar.claim != nullptr) {
+      if constexpr (CG == 2) {
+        // The follower reads the leader's claim (written before the cluster barrier).
+        uint32_t v;
+        asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(map_to_cta(smem_u32(vcid_slot), 0)) : "memory");
+        cluster_id = static_cast<int>(v);
+      } else {
+        cluster_id = *vcid_slot;
+      }
+    }
+  }
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
@@ -971,6 +997,14 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
   if (warp == 1) {
     if constexpr (CG == 2) tmem_dealloc_pair(tmem_base, kTmemCols);
     else tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if constexpr (AR) {
+    // The launch's last cluster resets the counters for the next launch.
+    if (kp.ar.claim != nullptr && leader && threadIdx.x == 0 &&
+        atomicAdd(kp.ar.claim + 1, 1u) == static_cast<unsigned>(nclusters - 1)) {
+      atomicExch(kp.ar.claim, 0u);
+      atomicExch(kp.ar.claim + 1, 0u);
+    }
   }
 }
 

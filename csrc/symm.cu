@@ -19,7 +19,15 @@
 //   3. depart : flags again, so no rank reads its buffer before every slice has
 //               landed.
 // Flags carry monotonically increasing epochs (2e+1 arrive, 2e+2 depart), so
-// nothing is ever reset.  Every wait is bounded by a %globaltimer deadline; a
+// nothing is ever reset.
+//
+// CTA pairing uses a *virtual* CTA index, taken from a per-channel counter in
+// this rank's flag page in the order the CTAs become resident (the last CTA of
+// a launch resets the counter).  Pairing by blockIdx.x would deadlock when
+// another cross-rank kernel holds some SMs: rank A could have CTAs 0..k
+// resident while rank B has CTAs k+1.. resident, each waiting for the other.
+// With claimed indices the resident CTAs of every rank are always 0..k-1 for
+// some k, so they pair up, finish and make room for the rest.  Every wait is bounded by a %globaltimer deadline; a
 // wait that expires records kTimeoutPeer in the status word and the kernel
 // returns.
 //
@@ -77,6 +85,27 @@ struct MdRsParams {
   float lr, b1, b2, eps, wd, bc1, bc2_sqrt;
 };
 
+// All-gather of FSDP parameter shards (md_ag_shards): every rank's fp32 shard
+// of a unit sits at `offset` of its symmetric shard buffer; after an arrive
+// barrier (every rank's shard is final) each rank copies all W shards into its
+// own gathered buffer `out` (shard r at out[r * shard]), casting to bf16 when
+// out_bf16 is set -- the reference's cast-then-all-gather (fsdp.py:172-182) as
+// one pass of peer loads.  A depart barrier keeps any rank from updating its
+// shard while a peer may still be reading it.
+struct MdAgParams {
+  const float* bufs[md::symm::kMaxWorld];
+  uint32_t* flags[md::symm::kMaxWorld];
+  long long offset;      // element offset of the unit's shard in every buffer
+  long long shard;       // elements per rank (multiple of 4)
+  int world, rank;
+  uint32_t epoch;
+  int channel;
+  unsigned long long timeout_ns;
+  md::Status* status;
+  void* out;             // world * shard elements, fp32 or bf16
+  int out_bf16;
+};
+
 namespace md {
 namespace symm {
 
@@ -94,10 +123,43 @@ __device__ __forceinline__ size_t flag_idx(int channel, int cta, int src) {
   return (static_cast<size_t>(channel) * kMaxCtas + cta) * kMaxWorld + src;
 }
 
-// Per-CTA all-to-all barrier with the same-index CTA of every rank.
+// {claimed, finished} counters of `channel`, behind the flag slots of this rank's page.
+template <typename P>
+__device__ __forceinline__ uint32_t* vcta_counter(const P& p) {
+  return p.flags[p.rank] + static_cast<size_t>(kChannels) * kMaxCtas * kMaxWorld + 2 * p.channel;
+}
+
+// Virtual index of this CTA (claim order); -1 if the counter is out of step.
+template <typename P>
+__device__ int vcta_claim(const P& p) {
+  __shared__ int v_sh;
+  if (threadIdx.x == 0) {
+    const uint32_t v = atomicAdd(vcta_counter(p), 1u);
+    v_sh = v < gridDim.x ? static_cast<int>(v) : -1;
+    if (v_sh < 0) report(p.status, kTimeoutPeer, 199, v);
+  }
+  __syncthreads();
+  return v_sh;
+}
+
+// Every CTA calls this once on every exit path; the launch's last CTA resets
+// the counters for the next launch on this channel (stream-ordered after it).
+template <typename P>
+__device__ void vcta_release(const P& p) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* c = vcta_counter(p);
+    if (atomicAdd(c + 1, 1u) == gridDim.x - 1) {
+      atomicExch(c, 0u);
+      atomicExch(c + 1, 0u);
+    }
+  }
+}
+
+// Per-CTA all-to-all barrier with the same virtual CTA `v` of every rank.
 // Returns false on timeout (status recorded).
 template <typename P>
-__device__ bool cta_barrier(const P& p, uint32_t value, uint32_t where) {
+__device__ bool cta_barrier(const P& p, int v, uint32_t value, uint32_t where) {
   __shared__ int ok_sh;
   if (threadIdx.x == 0) ok_sh = 1;
   __syncthreads();
@@ -105,8 +167,8 @@ __device__ bool cta_barrier(const P& p, uint32_t value, uint32_t where) {
   if (peer < p.world) {
     // The release store orders this CTA's earlier writes (ordered before it by
     // the __syncthreads above) at system scope; no separate fence needed.
-    st_release_sys(p.flags[peer] + flag_idx(p.channel, blockIdx.x, p.rank), value);
-    const uint32_t* mine = p.flags[p.rank] + flag_idx(p.channel, blockIdx.x, peer);
+    st_release_sys(p.flags[peer] + flag_idx(p.channel, v, p.rank), value);
+    const uint32_t* mine = p.flags[p.rank] + flag_idx(p.channel, v, peer);
     const uint64_t t0 = globaltimer_ns();
     uint32_t it = 0;
     while (static_cast<int32_t>(ld_acquire_sys(mine) - value) < 0) {
@@ -123,7 +185,8 @@ __device__ bool cta_barrier(const P& p, uint32_t value, uint32_t where) {
 
 __global__ void __launch_bounds__(512) md_ar_bucket_kernel(const __grid_constant__ MdArParams p) {
   const uint32_t arrive = 2u * p.epoch + 1u, depart = 2u * p.epoch + 2u;
-  if (!cta_barrier(p, arrive, 100)) return;
+  const int vc = vcta_claim(p);
+  if (vc >= 0 && cta_barrier(p, vc, arrive, 100)) {
 
   const long long n4 = p.n / 4;
   const long long per = (n4 + p.world - 1) / p.world;
@@ -137,7 +200,7 @@ __global__ void __launch_bounds__(512) md_ar_bucket_kernel(const __grid_constant
 
   // Two vectors per thread per step, every rank's loads of both issued before
   // any sum: twice the bytes in flight per thread (NVLink latency is ~us).
-  for (long long u = lo + static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; u < hi; u += 2 * stride) {
+  for (long long u = lo + static_cast<long long>(vc) * blockDim.x + threadIdx.x; u < hi; u += 2 * stride) {
     const long long u2 = u + stride;
     const bool two = u2 < hi;
     float4 v[kMaxWorld], w[kMaxWorld];
@@ -175,12 +238,15 @@ __global__ void __launch_bounds__(512) md_ar_bucket_kernel(const __grid_constant
         if (two) __stcg(bases[r] + u2, t);
       }
   }
-  cta_barrier(p, depart, 101);
+  cta_barrier(p, vc, depart, 101);
+  }
+  vcta_release(p);
 }
 
 __global__ void __launch_bounds__(512) md_rs_shard_kernel(const __grid_constant__ MdRsParams p) {
   const uint32_t arrive = 2u * p.epoch + 1u, depart = 2u * p.epoch + 2u;
-  if (!cta_barrier(p, arrive, 110)) return;
+  const int vc = vcta_claim(p);
+  if (vc >= 0 && cta_barrier(p, vc, arrive, 110)) {
   const long long n4 = p.shard / 4;
   const long long base = (p.offset + static_cast<long long>(p.rank) * p.shard) / 4;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
@@ -223,7 +289,7 @@ __global__ void __launch_bounds__(512) md_rs_shard_kernel(const __grid_constant_
       *g = s;
     }
   };
-  for (long long u = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; u < n4; u += 2 * stride) {
+  for (long long u = static_cast<long long>(vc) * blockDim.x + threadIdx.x; u < n4; u += 2 * stride) {
     const long long u2 = u + stride;
     const bool two = u2 < n4;
     float4 v[kMaxWorld], w[kMaxWorld];
@@ -250,13 +316,55 @@ __global__ void __launch_bounds__(512) md_rs_shard_kernel(const __grid_constant_
     if (two) finish(u2, t);
   }
   // No rank rewrites its gradient buffer before every peer has read it.
-  cta_barrier(p, depart, 111);
+  cta_barrier(p, vc, depart, 111);
+  }
+  vcta_release(p);
+}
+
+__global__ void __launch_bounds__(512) md_ag_shards_kernel(const __grid_constant__ MdAgParams p) {
+  const uint32_t arrive = 2u * p.epoch + 1u, depart = 2u * p.epoch + 2u;
+  const int vc = vcta_claim(p);
+  if (vc >= 0 && cta_barrier(p, vc, arrive, 120)) {
+  const long long n4 = p.shard / 4;
+  const long long total = n4 * p.world;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  // Two vectors per thread in flight; item i = (rank r, vector j).
+  for (long long i = static_cast<long long>(vc) * blockDim.x + threadIdx.x; i < total; i += 2 * stride) {
+    const long long i2 = i + stride;
+    const bool two = i2 < total;
+    const int r1 = static_cast<int>(i / n4), r2 = two ? static_cast<int>(i2 / n4) : 0;
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(p.bufs[r1] + p.offset) + (i - r1 * n4));
+    float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (two) b = __ldcg(reinterpret_cast<const float4*>(p.bufs[r2] + p.offset) + (i2 - r2 * n4));
+    if (p.out_bf16) {
+      uint2* o = reinterpret_cast<uint2*>(p.out);
+      o[i] = make_uint2(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w));
+      if (two) o[i2] = make_uint2(pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
+    } else {
+      float4* o = reinterpret_cast<float4*>(p.out);
+      o[i] = a;
+      if (two) o[i2] = b;
+    }
+  }
+  cta_barrier(p, vc, depart, 121);
+  }
+  vcta_release(p);
 }
 
 }  // namespace symm
 }  // namespace md
 
 extern "C" {
+
+// Launch md_ag_shards_kernel with `ctas` CTAs (<= 160).
+int md_ag_shards(const MdAgParams* prm, int ctas, cudaStream_t s) {
+  if (prm == nullptr || prm->world < 1 || prm->world > md::symm::kMaxWorld || (prm->shard % 4) || (prm->offset % 4) ||
+      prm->out == nullptr)
+    return -1;
+  if (ctas < 1 || ctas > md::symm::kMaxCtas || prm->channel < 0 || prm->channel >= md::symm::kChannels) return -2;
+  md::symm::md_ag_shards_kernel<<<ctas, 512, 0, s>>>(*prm);
+  return static_cast<int>(cudaGetLastError());
+}
 
 // Launch md_rs_shard_kernel with `ctas` CTAs (<= 64).
 int md_rs_shard(const MdRsParams* prm, int ctas, cudaStream_t s) {
@@ -271,7 +379,9 @@ int md_rs_shard(const MdRsParams* prm, int ctas, cudaStream_t s) {
 
 int md_symm_max_world() { return md::symm::kMaxWorld; }
 long long md_symm_flag_bytes() {
-  return static_cast<long long>(md::symm::kChannels) * md::symm::kMaxCtas * md::symm::kMaxWorld * sizeof(uint32_t);
+  // Flag slots plus one {claimed, finished} counter pair per channel.
+  return (static_cast<long long>(md::symm::kChannels) * md::symm::kMaxCtas * md::symm::kMaxWorld +
+          2 * md::symm::kChannels) * sizeof(uint32_t);
 }
 
 // Allocate `bytes` of zeroed device memory and export its IPC handle (64 bytes into handle_out).

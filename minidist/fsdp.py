@@ -26,7 +26,12 @@ reduce-scatter of gradients is one peer-memory kernel (md_rs_shard in
 csrc/symm.cu: sum of this rank's shard over every rank's fp32 full gradient,
 1/W scale, accumulate into the shard gradient -- or, with ``fused_adamw``, the
 AdamW update of the shard) when every rank of the group is on this node; NCCL
-otherwise.  The gather is NCCL's all-gather on the prefetch stream.
+otherwise.  On the same path the fp32 shards live in a symmetric buffer and the
+gather is md_ag_shards (csrc/symm.cu): one kernel that reads every rank's shard
+over NVLink and writes the gathered unit in ``param_dtype`` (the reference's
+cast + all-gather, fsdp.py:172-182, as one pass).  A reduce-scatter kernel is
+ordered after any gather still in flight, so the two cross-rank kernels never
+hold SMs against each other.
 """
 
 from __future__ import annotations
@@ -95,6 +100,9 @@ class _FSDPUnit:
         self._hook_handles: list = []
         # Peer-memory reduce-scatter: (communicator, symmetric buffer, element offset) or None.
         self._peer: tuple | None = None
+        # Peer-memory gather: (communicator, symmetric shard buffer, element offset) or None.
+        self._peer_shard: tuple | None = None
+        self._owner_state: dict | None = None  # shared with the FSDP module: last gather event
         self._adam: dict | None = None  # fused AdamW: hyper-parameters, m, v, step
 
     # -- gather / free -------------------------------------------------------------
@@ -105,6 +113,12 @@ class _FSDPUnit:
 
     def _gather_into_full(self) -> None:
         self._full.untyped_storage().resize_(self.padded_numel * self._full.element_size())
+        if self._peer_shard is not None:
+            from .parallel import collectives
+
+            comm_, buf, off = self._peer_shard
+            collectives.all_gather_shards(buf, comm_, off, self.shard_numel, self._full)
+            return
         src = self.flat_shard.detach()
         if src.dtype != self.policy.param_dtype:
             src = src.to(self.policy.param_dtype)
@@ -130,6 +144,8 @@ class _FSDPUnit:
             ev.record(stream)
         self._full.record_stream(torch.cuda.current_stream())
         self._gather_event = ev
+        if self._owner_state is not None:
+            self._owner_state["last_gather"] = ev
         self._unsharded = True
 
     def reshard(self) -> None:
@@ -188,6 +204,12 @@ class _FSDPUnit:
 
         comm_, buf, off = self._peer
         full = self._full_grad_buffer()
+        st = self._owner_state
+        if st is not None and st.get("last_gather") is not None:
+            # A prefetch gather (another cross-rank kernel) may still be running on the side
+            # stream: start the reduce-scatter only after it, on every rank.
+            torch.cuda.current_stream().wait_event(st["last_gather"])
+            st["last_gather"] = None
         o = 0
         with torch.no_grad():
             for p, n in zip(self.params, self.numels, strict=True):
@@ -301,6 +323,21 @@ class FullyShardedDataParallel(nn.Module):
                 u._peer = (self._peer_comm, self._grad_buf, off)
                 u._full_grad_buffer()  # fused kernels write gradients straight into the symmetric buffer
                 off += u.padded_numel
+            self._gather_state: dict = {"last_gather": None}
+            if all(u.flat_shard.dtype == torch.float32 and u.policy.param_dtype in (torch.float32, torch.bfloat16)
+                   for u in self._units) and collectives.fsdp_gather_enabled():
+                # fp32 shards move into a symmetric buffer so peers can read them.
+                total_shard = sum(u.shard_numel for u in self._units)
+                self._shard_buf = self._peer_comm.buffer(f"fsdp_shards_{id(self)}", total_shard * 4)
+                off = 0
+                for u in self._units:
+                    view = self._shard_buf.view(torch.float32, off * 4, u.shard_numel)
+                    view.copy_(u.flat_shard.data)
+                    u.flat_shard.data = view
+                    u._peer_shard = (self._peer_comm, self._shard_buf, off)
+                    u._owner_state = self._gather_state
+                    off += u.shard_numel
+                torch.cuda.synchronize(device)
         if fused_adamw is not None:
             if self._peer_comm is None or any(u.flat_shard.dtype != torch.float32 for u in self._units):
                 raise ValueError("fused_adamw needs the peer-memory reduce-scatter and fp32 shards")

@@ -157,6 +157,7 @@ class TpArParams(ctypes.Structure):
         ("max_chunks", ctypes.c_int),
         ("timeout_ns", ctypes.c_ulonglong),
         ("trace", ctypes.c_void_p),
+        ("claim", ctypes.c_void_p),
     ]
 
 
@@ -237,15 +238,18 @@ def gemm_all_reduce(x_local, w_local, bias, resid, group, b_mn: bool = False):
         ar.world, ar.rank = c.world, c.rank
         ar.max_chunks = flags.nbytes // 8
         ar.timeout_ns = _timeout_ns()
+        # Cluster-order counters (this rank only); the kernel leaves them at zero.
+        claim = torch.zeros(2, dtype=torch.int32, device=x_local.device)
+        ar.claim = claim.data_ptr()
         gp = nat.GemmParams()
         gp.M, gp.N, gp.K = M, N, K
         gp.epi = G.EPI_BF16
         gp.alpha = 1.0
         gp.b_mn_major = int(b_mn)
         gp.status = nat.status_ptr(x_local.device)
-        st = (key, ar, gp, ctypes.byref(gp), ctypes.byref(ar))
+        st = (key, ar, gp, ctypes.byref(gp), ctypes.byref(ar), claim)
         _AR_CACHE[id(c)] = st
-    _, ar, gp, gp_ref, ar_ref = st
+    _, ar, gp, gp_ref, ar_ref, _ = st
     ar.out, ar.ldo = out.data_ptr(), out.stride(0)
     ar.bias = None if bias is None else bias.data_ptr()
     if resid is not None:
@@ -308,6 +312,11 @@ def fsdp_communicator(group) -> symm.Communicator | None:
     return _group_comm(group)
 
 
+def fsdp_gather_enabled() -> bool:
+    """Peer-memory parameter all-gather for FSDP (env ``MINIDIST_FSDP_GATHER=0`` -> NCCL)."""
+    return os.environ.get("MINIDIST_FSDP_GATHER", "1") not in ("0", "false", "no")
+
+
 def reduce_scatter_shard(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offset: int, shard: int,
                          grad_out: torch.Tensor | None, accumulate: bool, scale: float,
                          adam: tuple | None = None) -> None:
@@ -338,3 +347,57 @@ def reduce_scatter_shard(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_of
     nat.check(rc, "md_rs_shard")
     n = shard * comm_.world * 4
     comm.comm_stats.add("reduce_scatter", n, int((comm_.world - 1) / comm_.world * n))
+
+
+# ---------------------------------------------------------------------------
+# FSDP: parameter all-gather over peer memory
+# ---------------------------------------------------------------------------
+_FSDP_AG_CHANNEL = 5
+
+
+class AgParams(ctypes.Structure):
+    """Mirror of ``struct MdAgParams`` (csrc/symm.cu)."""
+
+    _fields_ = [
+        ("bufs", ctypes.c_void_p * _MAXW),
+        ("flags", ctypes.c_void_p * _MAXW),
+        ("offset", ctypes.c_longlong),
+        ("shard", ctypes.c_longlong),
+        ("world", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("epoch", ctypes.c_uint32),
+        ("channel", ctypes.c_int),
+        ("timeout_ns", ctypes.c_ulonglong),
+        ("status", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("out_bf16", ctypes.c_int),
+    ]
+
+
+nat.declare("md_ag_shards", "i:pip")
+
+
+def all_gather_shards(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offset: int, shard: int,
+                      out: torch.Tensor) -> None:
+    """Every rank's fp32 shard ``buf[elem_offset : elem_offset + shard]`` into ``out`` (rank r's at
+    ``out[r*shard]``), cast to ``out.dtype`` (fp32 or bf16) on the way, on the current stream."""
+    if out.dtype not in (torch.float32, torch.bfloat16) or out.numel() < shard * comm_.world:
+        raise ValueError("all_gather_shards: out must be fp32 / bf16 with world * shard elements")
+    prm = AgParams()
+    for r in range(comm_.world):
+        prm.bufs[r] = buf.ptrs[r]
+        prm.flags[r] = buf.flag_ptrs[r]
+    prm.offset, prm.shard = elem_offset, shard
+    prm.world, prm.rank = comm_.world, comm_.rank
+    prm.epoch = comm_.next_epoch(_FSDP_AG_CHANNEL)
+    prm.channel = _FSDP_AG_CHANNEL
+    prm.timeout_ns = _timeout_ns()
+    prm.status = nat.status_ptr(buf.device)
+    prm.out = out.data_ptr()
+    prm.out_bf16 = int(out.dtype == torch.bfloat16)
+    # One CTA per 64 K output elements, at most 64: the gather overlaps the compute stream.
+    ctas = min(64, max(1, shard * comm_.world // 65536))
+    rc = nat.lib().md_ag_shards(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr(None)))
+    nat.check(rc, "md_ag_shards")
+    n = shard * comm_.world * out.element_size()
+    comm.comm_stats.add("all_gather", n, int((comm_.world - 1) / comm_.world * n))

@@ -87,6 +87,19 @@ def check_fsdp(rank, world):
     model = md.FullyShardedDataParallel(GPT(cfg, tp_group=mesh.tp_group, device="cuda"), unit_types=(Block,),
                                         process_group=mesh.dp_group)
     assert all(u._peer is not None for u in model._units), "peer-memory reduce-scatter not in use"
+    assert all(u._peer_shard is not None for u in model._units), "peer-memory gather not in use"
+    # bf16 gather (md_ag_shards): the gathered unit is exactly every rank's fp32 shard cast to bf16.
+    mp = md.FullyShardedDataParallel(GPT(cfg, tp_group=mesh.tp_group, device="cuda"), unit_types=(Block,),
+                                     process_group=mesh.dp_group,
+                                     mixed_precision=md.MixedPrecisionPolicy(param_dtype=torch.bfloat16))
+    for u in mp._units:
+        with torch.no_grad():
+            u.flat_shard.add_(torch.randn_like(u.flat_shard) * (rank + 1))  # distinct shards per rank
+        u.unshard()
+        full = torch.empty(u.padded_numel, dtype=torch.float32, device="cuda")
+        dist.all_gather_into_tensor(full, u.flat_shard.detach(), group=mesh.dp_group)
+        assert torch.equal(u._full, full.bfloat16()), f"rank {rank} unit {u.name}: bf16 gather differs"
+        u.reshard()
     g = torch.Generator().manual_seed(11)
     ids = torch.randint(0, cfg.vocab_size, (2 * world, 128), generator=g).cuda()
     tgt = torch.randint(0, cfg.vocab_size, (2 * world, 128), generator=g).cuda()

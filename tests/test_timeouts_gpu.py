@@ -46,6 +46,8 @@ def test_bucket_allreduce_times_out_when_peer_never_arrives():
     with pytest.raises(nat.CommTimeoutError):
         nat.check_status()
     nat.check_status()  # the word was reset
+    # The virtual-CTA counters of the channel were reset by the launch's last CTA.
+    assert flags[0][-16:].abs().sum().item() == 0
     _after_check()
 
 
@@ -68,6 +70,8 @@ def test_fused_gemm_allreduce_times_out_when_peer_never_publishes():
     ar.ldp, ar.out, ar.ldo = N, out.data_ptr(), N
     ar.world, ar.rank, ar.epoch, ar.max_chunks = 2, 0, 1, chunks
     ar.timeout_ns = 1_000_000
+    claim = torch.zeros(2, dtype=torch.int32, device="cuda")
+    ar.claim = claim.data_ptr()
     gp = nat.GemmParams()
     gp.A, gp.B, gp.lda, gp.ldb = x.data_ptr(), w.data_ptr(), K, K
     gp.M, gp.N, gp.K, gp.epi, gp.alpha = M, N, K, G.EPI_BF16, 1.0
@@ -77,4 +81,5 @@ def test_fused_gemm_allreduce_times_out_when_peer_never_publishes():
     with pytest.raises(nat.CommTimeoutError):
         nat.check_status()
     nat.check_status()
+    assert claim.tolist() == [0, 0], "cluster-order counters not reset"
     _after_check()
