@@ -18,6 +18,11 @@ working set (about 6 GB of activations plus 0.6 GB of fp32 weights) is far
 larger than the 126 MB L2, so no explicit flush is needed.  SM clocks and
 throttle reasons are sampled with nvidia-smi during the timed region.
 
+Our arm runs the step as one CUDA graph (minidist.GraphedStep: forward,
+backward, gradient all-reduce and FusedAdamW(capturable=True) captured once,
+replayed per step, the step's token batch copied into the graph's input
+buffers first); ``--no-graph`` runs the same step eagerly.
+
 The ``e2e`` block repeats the K steps through the same public API with the
 inputs copied from pinned host memory each step and the loss read back to the
 host each step (wall clock, max over ranks).
@@ -44,11 +49,12 @@ METRIC = "GPT train tokens/s/box at 1/2/4/8 B200 (DDP,FSDP,TP×PP×DP), max over
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-graph", action="store_true", help="our arm: run the step eagerly (no CUDA graph)")
     return p.parse_args()
 
 
@@ -60,7 +66,7 @@ _REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_pow
 
 
 class ClockSampler:
-    """One ``nvidia-smi -lms 200`` process per node, over every GPU of the run.
+    """One ``nvidia-smi -lms 100`` process per node, over every GPU of the run.
 
     Started before the warm-up steps (its NVML start-up takes host CPU and must
     not overlap the timed window); each sample is stamped on arrival and
@@ -79,7 +85,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100",
                  "-i", ",".join(self.gpu_ids)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
@@ -112,7 +118,7 @@ class ClockSampler:
                 return None
 
         # Samples inside the timed window (a sample arrives up to one period after it was taken).
-        window = [r for t, r in self.rows if t0 <= t <= t1 + 0.25]
+        window = [r for t, r in self.rows if t0 <= t <= t1 + 0.15]
         if not window:  # window shorter than the sampling period: take the samples closest to it
             near = sorted(self.rows, key=lambda tr: abs(tr[0] - (t0 + t1) / 2))
             window = [r for _, r in near[: len(self.gpu_ids)]]
@@ -176,7 +182,7 @@ def barrier(world: int) -> None:
 # ---------------------------------------------------------------------------
 
 
-def build(impl: str, world: int, seed: int):
+def build(impl: str, world: int, seed: int, graph: bool = False):
     """Model, optimizer and a step function through each framework's public API."""
     import torch
 
@@ -196,7 +202,7 @@ def build(impl: str, world: int, seed: int):
         from minidist.optim import FusedAdamW
 
         assert os.path.realpath(md.__file__).startswith(os.path.realpath(os.path.join(ROOT, "minidist")))
-        make_opt = lambda params: FusedAdamW(params, lr=3e-4)  # noqa: E731
+        make_opt = lambda params: FusedAdamW(params, lr=3e-4, capturable=graph)  # noqa: E731
 
     cfg = GPTConfig(vocab_size=MODEL["vocab"], block_size=MODEL["seq"], n_layer=MODEL["layers"],
                     n_head=MODEL["heads"], n_embd=MODEL["embd"], seed=seed)
@@ -214,7 +220,9 @@ def build(impl: str, world: int, seed: int):
 
     def step(ids, tgt):
         opt.zero_grad(set_to_none=True)
-        with torch.autocast("cuda", dtype=torch.bfloat16):
+        # (No autocast weight-cast cache: a cached cast made during a graph capture
+        # would outlive the capture.)
+        with torch.autocast("cuda", dtype=torch.bfloat16, cache_enabled=not graph):
             _, loss = model(ids, tgt)
         loss.backward()
         opt.step()
@@ -258,9 +266,19 @@ def main() -> int:
         print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
         return 0
     rank, world, local = setup(args)
-    cfg, model, opt, step = build(args.impl, world, args.seed)
+    graph = args.impl == "ours" and not args.no_graph
+    cfg, model, opt, step = build(args.impl, world, args.seed, graph)
     K, W = args.steps, args.warmup
     dev_batches = make_batches(K + W, rank, args.seed, cfg.vocab_size, pinned=False)
+    graphed = None
+    raw_step = step
+    if graph:
+        import minidist as md
+
+        # Two eager steps (lazy initialisation), then one capture; the W warm-up
+        # steps below are replays.
+        graphed = md.GraphedStep(step, dev_batches[0], warmup=2, optimizers=[opt])
+        step = graphed
 
     # Clock sampling: one nvidia-smi per node (local rank 0) over every GPU of
     # this node's ranks, started before the warm-up so its start-up is over
@@ -324,7 +342,12 @@ def main() -> int:
 
     launches = 0
     if args.impl == "ours":
-        launches = count_our_kernels(step, dev_batches[0]) * K
+        per_step = count_our_kernels(step, dev_batches[0])
+        if per_step == 0 and graphed is not None:  # the profiler did not see inside the graph
+            per_step = count_our_kernels(raw_step, dev_batches[0])
+        launches = per_step * K
+    if graphed is not None:
+        graphed.release()
 
     tokens_per_step = MODEL["batch"] * MODEL["seq"] * world
     value = tokens_per_step / (ms / 1e3)
@@ -351,6 +374,7 @@ def main() -> int:
             "parallelism": f"dp{world}",
             "strategy": "ddp, 25 MB buckets overlapped with backward",
             "optimizer": "AdamW lr 3e-4",
+            "cuda_graph": graph,
             "l2": "no flush: per-step working set (~6 GB activations + weights) >> 126 MB L2",
         },
         "clocks": clocks,

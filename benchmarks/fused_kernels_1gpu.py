@@ -64,17 +64,13 @@ def run_gemm_ar(iters: int) -> None:
     ar.ldp, ar.out, ar.ldo = N, out.data_ptr(), N
     ar.bias, ar.resid, ar.ldr = bias.data_ptr(), resid.data_ptr(), N
     ar.world, ar.rank, ar.max_chunks, ar.timeout_ns = 1, 0, chunks, 10**10
-    claim = torch.zeros(2, dtype=torch.int32, device="cuda")
+    claim = torch.zeros(3, dtype=torch.int32, device="cuda")
     ar.claim = claim.data_ptr()
     gp = nat.GemmParams()
     gp.A, gp.B, gp.lda, gp.ldb = x.data_ptr(), w.data_ptr(), K, K
     gp.M, gp.N, gp.K, gp.epi, gp.alpha = M, N, K, G.EPI_BF16, 1.0
     gp.status = nat.status_ptr()
-    state = {"epoch": 0}
-
     def call():
-        state["epoch"] += 1
-        ar.epoch = state["epoch"]
         nat.check(nat.lib().md_gemm_ar(ctypes.byref(gp), ctypes.byref(ar), ctypes.c_void_p(nat.stream_ptr())),
                   "md_gemm_ar")
 
@@ -82,7 +78,7 @@ def run_gemm_ar(iters: int) -> None:
     nat.check_status()
     want = (x.float() @ w.float().t() + bias + resid.float())
     err = ((out.float() - want).abs().max() / want.abs().max()).item()
-    assert claim.tolist() == [0, 0], "cluster-order counters not reset"
+    assert claim.tolist()[:2] == [0, 0], "cluster-order counters not reset"
     print(f"md_gemm_ar world=1 M={M} K={K} N={N}: {t * 1e6:.1f} us, {2 * M * N * K / t / 1e12:.0f} TFLOP/s, "
           f"rel err {err:.2e}")
 
@@ -96,11 +92,7 @@ def run_ddp_ar(iters: int) -> None:
     p.offset, p.n, p.world, p.rank, p.scale, p.channel = 0, n, 1, 0, 1.0, 0
     p.timeout_ns, p.status = 10**10, nat.status_ptr()
     ctas = nat.lib().md_allreduce_ctas(n, 1)
-    state = {"epoch": 0}
-
     def call():
-        state["epoch"] += 1
-        p.epoch = state["epoch"]
         nat.check(nat.lib().md_allreduce(ctypes.byref(p), ctas, ctypes.c_void_p(nat.stream_ptr())), "md_allreduce")
 
     t = timed(call, iters)
@@ -119,11 +111,7 @@ def run_fsdp_rs(iters: int) -> None:
     r.timeout_ns, r.status = 10**10, nat.status_ptr()
     r.p, r.m, r.v = (t.data_ptr() for t in pmv)
     r.lr, r.b1, r.b2, r.eps, r.wd, r.bc1, r.bc2_sqrt = 1e-4, 0.9, 0.999, 1e-8, 0.01, 0.1, 0.0316
-    state = {"epoch": 0}
-
     def call():
-        state["epoch"] += 1
-        r.epoch = state["epoch"]
         nat.check(nat.lib().md_rs_shard(ctypes.byref(r), nat.num_sms(), ctypes.c_void_p(nat.stream_ptr())), "md_rs_shard")
 
     t = timed(call, iters)
@@ -142,11 +130,7 @@ def run_fsdp_ag(iters: int) -> None:
     a.offset, a.shard, a.world, a.rank, a.channel = 0, shard, 1, 0, 5
     a.timeout_ns, a.status = 10**10, nat.status_ptr()
     a.out, a.out_bf16 = out.data_ptr(), 1
-    state = {"epoch": 0}
-
     def call():
-        state["epoch"] += 1
-        a.epoch = state["epoch"]
         nat.check(nat.lib().md_ag_shards(ctypes.byref(a), 64, ctypes.c_void_p(nat.stream_ptr())), "md_ag_shards")
 
     t = timed(call, iters)

@@ -133,8 +133,10 @@ struct MdTpArParams {
   int max_chunks;
   unsigned long long timeout_ns;
   unsigned long long* trace;  // optional analysis trace ([64][8] %globaltimer stamps of CTA 0), or null
-  // This rank's {claimed, finished} cluster counters (2 x u32, zero between
-  // launches), or null for blockIdx order.  Clusters take their tile-walk
+  // This rank's {claimed, finished, epoch} counters (3 x u32; the first two are
+  // zero between launches), or null for blockIdx order and the host's `epoch`.
+  // With counters the epoch is the launch count + 1, read on the device, so a
+  // replayed CUDA graph advances it.  Clusters take their tile-walk
   // index in the order they become resident, so when another kernel holds
   // some SMs the resident clusters of every rank are the same prefix 0..k-1
   // and pair up across ranks instead of waiting on clusters not yet running.
@@ -627,10 +629,10 @@ __device__ __forceinline__ void ar_reduce_rows(const MdGemmParams& p, const MdTp
   }
 }
 
-__device__ __forceinline__ bool ar_reduce_chunk(const MdGemmParams& p, const MdTpArParams& ar, int chunk, int row0,
-                                                int col0, int lane, volatile int* abort_flag) {
+__device__ __forceinline__ bool ar_reduce_chunk(const MdGemmParams& p, const MdTpArParams& ar, unsigned epoch, int chunk,
+                                                int row0, int col0, int lane, volatile int* abort_flag) {
   bool ok = true;
-  if (lane < ar.world) ok = flag_wait_ge(ar.flags[lane] + chunk, ar.epoch, ar, p.status, 60, abort_flag);
+  if (lane < ar.world) ok = flag_wait_ge(ar.flags[lane] + chunk, epoch, ar, p.status, 60, abort_flag);
   if (__any_sync(0xFFFFFFFFu, !ok)) return false;
   acquire_fence();  // every lane's loads below follow the lanes' observations (ordered by the vote)
   const int col = col0 + lane * 8;
@@ -648,19 +650,20 @@ __device__ __forceinline__ bool ar_reduce_chunk(const MdGemmParams& p, const MdT
   // __syncwarp orders every lane's stores before lane 0's release (which is
   // cumulative), so one release store publishes the whole chunk.
   __syncwarp();
-  if (lane == 0) flag_release_sys(ar.flags[ar.rank] + ar.max_chunks + chunk, ar.epoch);
+  if (lane == 0) flag_release_sys(ar.flags[ar.rank] + ar.max_chunks + chunk, epoch);
   return true;
 }
 
 // Comm warp, chunk owned by `owner`: copy its final values into the output.
 // blocking = false returns false at once if the owner has not published yet.
-__device__ __forceinline__ int ar_pull_chunk(const MdGemmParams& p, const MdTpArParams& ar, int chunk, int owner,
-                                             int row0, int col0, int lane, bool blocking, volatile int* abort_flag) {
+__device__ __forceinline__ int ar_pull_chunk(const MdGemmParams& p, const MdTpArParams& ar, unsigned epoch, int chunk,
+                                             int owner, int row0, int col0, int lane, bool blocking,
+                                             volatile int* abort_flag) {
   const unsigned* f = ar.flags[owner] + ar.max_chunks + chunk;
   int ready = 0;
   if (lane == 0) {
-    if (blocking) ready = flag_wait_ge(f, ar.epoch, ar, p.status, 61, abort_flag) ? 1 : -1;
-    else ready = flag_acquire_sys(f) >= ar.epoch ? 1 : 0;
+    if (blocking) ready = flag_wait_ge(f, epoch, ar, p.status, 61, abort_flag) ? 1 : -1;
+    else ready = flag_acquire_sys(f) >= epoch ? 1 : 0;
   }
   ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
   if (ready == 1) acquire_fence();  // every lane's loads below follow the observation
@@ -737,6 +740,9 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
         const unsigned v = atomicAdd(kp.ar.claim, 1u);
         *vcid_slot = v < static_cast<unsigned>(nclusters) ? static_cast<int>(v) : nclusters;
         if (v >= static_cast<unsigned>(nclusters)) report(p.status, kTimeoutPeer, 49, v);
+        // Launch count of this communicator + 1: the epoch, kept on the device
+        // so that a replayed CUDA graph advances it.
+        vcid_slot[1] = static_cast<int>(*reinterpret_cast<volatile unsigned*>(kp.ar.claim + 2) + 1u);
       }
     }
     fence_mbar_init();
@@ -758,15 +764,21 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
   if constexpr (CG == 2) cluster_sync();  // peer barriers exist before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
+  unsigned ar_epoch = 0;
   if constexpr (AR) {
+    ar_epoch = kp.ar.epoch;
     if (kp.ar.claim != nullptr) {
       if constexpr (CG == 2) {
         // The follower reads the leader's claim (written before the cluster barrier).
-        uint32_t v;
-        asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(map_to_cta(smem_u32(vcid_slot), 0)) : "memory");
+        uint32_t v, e;
+        const uint32_t a = map_to_cta(smem_u32(vcid_slot), 0);
+        asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+        asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(e) : "r"(a + 4u) : "memory");
         cluster_id = static_cast<int>(v);
+        ar_epoch = e;
       } else {
-        cluster_id = *vcid_slot;
+        cluster_id = vcid_slot[0];
+        ar_epoch = static_cast<unsigned>(vcid_slot[1]);
       }
     }
   }
@@ -926,7 +938,7 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
           // proxy fence; the release store itself publishes them system-wide.
           asm volatile("fence.proxy.async.global;" ::: "memory");
           if (quarter == 0) MD_AR_TRACE(kp.ar, ti, 6);
-          flag_release_sys(kp.ar.flags[kp.ar.rank] + (row0 >> 5) * kp.tiles_n + tn, kp.ar.epoch);
+          flag_release_sys(kp.ar.flags[kp.ar.rank] + (row0 >> 5) * kp.tiles_n + tn, ar_epoch);
           if (quarter == 0) MD_AR_TRACE(kp.ar, ti, 1);
         }
       }
@@ -966,7 +978,7 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
         chunk_of(pull_u, row0, col0, chunk);
         const int owner = chunk % ar.world;
         if (row0 < p.M && owner != ar.rank) {
-          const int r = ar_pull_chunk(p, ar, chunk, owner, row0, col0, lane, blocking, abort_flag);
+          const int r = ar_pull_chunk(p, ar, ar_epoch, chunk, owner, row0, col0, lane, blocking, abort_flag);
           if (r < 0) ok = false;
           if (r != 1) return;
         }
@@ -979,7 +991,7 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
       const int ti = (u - cluster_id) / nclusters;
       if (quarter == 0 && lane == 0) MD_AR_TRACE(ar, ti, 2);
       if (row0 < p.M && chunk % ar.world == ar.rank) {
-        ok = ar_reduce_chunk(p, ar, chunk, row0, col0, lane, abort_flag);
+        ok = ar_reduce_chunk(p, ar, ar_epoch, chunk, row0, col0, lane, abort_flag);
         if (quarter == 0 && lane == 0) MD_AR_TRACE(ar, ti, 3);
       }
       try_pulls(u + 1, false);
@@ -1002,6 +1014,7 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
     // The launch's last cluster resets the counters for the next launch.
     if (kp.ar.claim != nullptr && leader && threadIdx.x == 0 &&
         atomicAdd(kp.ar.claim + 1, 1u) == static_cast<unsigned>(nclusters - 1)) {
+      atomicExch(kp.ar.claim + 2, ar_epoch);
       atomicExch(kp.ar.claim, 0u);
       atomicExch(kp.ar.claim + 1, 0u);
     }

@@ -35,8 +35,17 @@ __global__ void __launch_bounds__(256) adamw_kernel(const MdAdamEntry* __restric
                                                     const int2* __restrict__ chunks, float lr, float b1, float b2,
                                                     float eps, float wd, float bc1, float bc2_sqrt,
                                                     const float* __restrict__ inv_scale,
-                                                    const float* __restrict__ skip, int mode) {
+                                                    const float* __restrict__ skip, int mode,
+                                                    const float* __restrict__ hp) {
   if (mode == 0 && skip != nullptr && *skip != 0.f) return;
+  if (hp != nullptr) {
+    // Graph-replayable form: learning rate and step count come from device
+    // memory, and the bias corrections are computed here.
+    lr = hp[0];
+    const float t = hp[1];
+    bc1 = 1.f - powf(b1, t);
+    bc2_sqrt = sqrtf(1.f - powf(b2, t));
+  }
   const int2 c = chunks[blockIdx.x];
   const MdAdamEntry e = table[c.x];
   const long long lo = static_cast<long long>(c.y) * kChunk;
@@ -116,12 +125,14 @@ extern "C" {
 int md_adamw_chunk() { return md::optim::kChunk; }
 int md_adamw_entry_bytes() { return static_cast<int>(sizeof(MdAdamEntry)); }
 
+// hp: null, or device [lr, step] (then lr / bc1 / bc2_sqrt are ignored).
 int md_adamw(const void* table, const void* chunks, int num_chunks, float lr, float b1, float b2, float eps, float wd,
-             float bc1, float bc2_sqrt, const float* inv_scale, const float* skip, int mode, cudaStream_t s) {
+             float bc1, float bc2_sqrt, const float* inv_scale, const float* skip, int mode, cudaStream_t s,
+             const float* hp) {
   if (num_chunks <= 0) return 0;
   md::optim::adamw_kernel<<<num_chunks, 256, 0, s>>>(reinterpret_cast<const MdAdamEntry*>(table),
                                                      reinterpret_cast<const int2*>(chunks), lr, b1, b2, eps, wd, bc1,
-                                                     bc2_sqrt, inv_scale, skip, mode);
+                                                     bc2_sqrt, inv_scale, skip, mode, hp);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -19,7 +19,8 @@
 //   3. depart : flags again, so no rank reads its buffer before every slice has
 //               landed.
 // Flags carry monotonically increasing epochs (2e+1 arrive, 2e+2 depart), so
-// nothing is ever reset.
+// nothing is ever reset; the epoch is counted on the device per (flag page,
+// channel), so kernels captured in a CUDA graph stay correct on replay.
 //
 // CTA pairing uses a *virtual* CTA index, taken from a per-channel counter in
 // this rank's flag page in the order the CTAs become resident (the last CTA of
@@ -53,7 +54,6 @@ struct MdArParams {
   long long n;                           // elements (multiple of 4)
   int world, rank;
   float scale;
-  uint32_t epoch;
   int channel;                           // flag region (independent streams use different channels)
   unsigned long long timeout_ns;
   md::Status* status;
@@ -73,7 +73,6 @@ struct MdRsParams {
   long long shard;       // elements per rank (multiple of 4)
   int world, rank;
   float scale;
-  uint32_t epoch;
   int channel;
   unsigned long long timeout_ns;
   md::Status* status;
@@ -98,7 +97,6 @@ struct MdAgParams {
   long long offset;      // element offset of the unit's shard in every buffer
   long long shard;       // elements per rank (multiple of 4)
   int world, rank;
-  uint32_t epoch;
   int channel;
   unsigned long long timeout_ns;
   md::Status* status;
@@ -123,33 +121,46 @@ __device__ __forceinline__ size_t flag_idx(int channel, int cta, int src) {
   return (static_cast<size_t>(channel) * kMaxCtas + cta) * kMaxWorld + src;
 }
 
-// {claimed, finished} counters of `channel`, behind the flag slots of this rank's page.
+// {claimed, finished, launches} counters of `channel`, behind the flag slots
+// of this rank's page.
 template <typename P>
 __device__ __forceinline__ uint32_t* vcta_counter(const P& p) {
-  return p.flags[p.rank] + static_cast<size_t>(kChannels) * kMaxCtas * kMaxWorld + 2 * p.channel;
+  return p.flags[p.rank] + static_cast<size_t>(kChannels) * kMaxCtas * kMaxWorld + 3 * p.channel;
 }
 
-// Virtual index of this CTA (claim order); -1 if the counter is out of step.
+// Virtual index of this CTA (claim order; -1 if the counter is out of step)
+// and the launch's epoch = launches on this (page, channel) so far + 1.  The
+// epoch lives on the device so that a replayed CUDA graph advances it; every
+// rank launches on a channel equally often, so the epochs agree across ranks.
+struct VCta {
+  int v;
+  uint32_t epoch;
+};
 template <typename P>
-__device__ int vcta_claim(const P& p) {
+__device__ VCta vcta_claim(const P& p) {
   __shared__ int v_sh;
+  __shared__ uint32_t e_sh;
   if (threadIdx.x == 0) {
-    const uint32_t v = atomicAdd(vcta_counter(p), 1u);
+    uint32_t* c = vcta_counter(p);
+    const uint32_t v = atomicAdd(c, 1u);
     v_sh = v < gridDim.x ? static_cast<int>(v) : -1;
     if (v_sh < 0) report(p.status, kTimeoutPeer, 199, v);
+    e_sh = *reinterpret_cast<volatile uint32_t*>(c + 2) + 1u;
   }
   __syncthreads();
-  return v_sh;
+  return VCta{v_sh, e_sh};
 }
 
-// Every CTA calls this once on every exit path; the launch's last CTA resets
-// the counters for the next launch on this channel (stream-ordered after it).
+// Every CTA calls this once on every exit path; the launch's last CTA records
+// the epoch and resets the claim counters for the next launch on this channel
+// (stream-ordered after it).
 template <typename P>
-__device__ void vcta_release(const P& p) {
+__device__ void vcta_release(const P& p, uint32_t epoch) {
   __syncthreads();
   if (threadIdx.x == 0) {
     uint32_t* c = vcta_counter(p);
     if (atomicAdd(c + 1, 1u) == gridDim.x - 1) {
+      atomicExch(c + 2, epoch);
       atomicExch(c, 0u);
       atomicExch(c + 1, 0u);
     }
@@ -184,8 +195,9 @@ __device__ bool cta_barrier(const P& p, int v, uint32_t value, uint32_t where) {
 }
 
 __global__ void __launch_bounds__(512) md_ar_bucket_kernel(const __grid_constant__ MdArParams p) {
-  const uint32_t arrive = 2u * p.epoch + 1u, depart = 2u * p.epoch + 2u;
-  const int vc = vcta_claim(p);
+  const VCta vct = vcta_claim(p);
+  const int vc = vct.v;
+  const uint32_t arrive = 2u * vct.epoch + 1u, depart = 2u * vct.epoch + 2u;
   if (vc >= 0 && cta_barrier(p, vc, arrive, 100)) {
 
   const long long n4 = p.n / 4;
@@ -240,12 +252,13 @@ __global__ void __launch_bounds__(512) md_ar_bucket_kernel(const __grid_constant
   }
   cta_barrier(p, vc, depart, 101);
   }
-  vcta_release(p);
+  vcta_release(p, vct.epoch);
 }
 
 __global__ void __launch_bounds__(512) md_rs_shard_kernel(const __grid_constant__ MdRsParams p) {
-  const uint32_t arrive = 2u * p.epoch + 1u, depart = 2u * p.epoch + 2u;
-  const int vc = vcta_claim(p);
+  const VCta vct = vcta_claim(p);
+  const int vc = vct.v;
+  const uint32_t arrive = 2u * vct.epoch + 1u, depart = 2u * vct.epoch + 2u;
   if (vc >= 0 && cta_barrier(p, vc, arrive, 110)) {
   const long long n4 = p.shard / 4;
   const long long base = (p.offset + static_cast<long long>(p.rank) * p.shard) / 4;
@@ -318,37 +331,43 @@ __global__ void __launch_bounds__(512) md_rs_shard_kernel(const __grid_constant_
   // No rank rewrites its gradient buffer before every peer has read it.
   cta_barrier(p, vc, depart, 111);
   }
-  vcta_release(p);
+  vcta_release(p, vct.epoch);
 }
 
 __global__ void __launch_bounds__(512) md_ag_shards_kernel(const __grid_constant__ MdAgParams p) {
-  const uint32_t arrive = 2u * p.epoch + 1u, depart = 2u * p.epoch + 2u;
-  const int vc = vcta_claim(p);
+  const VCta vct = vcta_claim(p);
+  const int vc = vct.v;
+  const uint32_t arrive = 2u * vct.epoch + 1u, depart = 2u * vct.epoch + 2u;
   if (vc >= 0 && cta_barrier(p, vc, arrive, 120)) {
   const long long n4 = p.shard / 4;
-  const long long total = n4 * p.world;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  // Two vectors per thread in flight; item i = (rank r, vector j).
-  for (long long i = static_cast<long long>(vc) * blockDim.x + threadIdx.x; i < total; i += 2 * stride) {
-    const long long i2 = i + stride;
-    const bool two = i2 < total;
-    const int r1 = static_cast<int>(i / n4), r2 = two ? static_cast<int>(i2 / n4) : 0;
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(p.bufs[r1] + p.offset) + (i - r1 * n4));
-    float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (two) b = __ldcg(reinterpret_cast<const float4*>(p.bufs[r2] + p.offset) + (i2 - r2 * n4));
-    if (p.out_bf16) {
-      uint2* o = reinterpret_cast<uint2*>(p.out);
-      o[i] = make_uint2(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w));
-      if (two) o[i2] = make_uint2(pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
-    } else {
-      float4* o = reinterpret_cast<float4*>(p.out);
-      o[i] = a;
-      if (two) o[i2] = b;
+  // Rank by rank, starting at this rank's own shard so that at any time the W
+  // ranks read from W different sources (no peer's links serve every reader);
+  // four vectors per thread in flight (peer loads have ~us latency).
+  constexpr int U = 4;
+  for (int step = 0; step < p.world; ++step) {
+    const int r = (p.rank + step) % p.world;
+    const float4* src = reinterpret_cast<const float4*>(p.bufs[r] + p.offset);
+    const long long ob = static_cast<long long>(r) * n4;
+    for (long long j = static_cast<long long>(vc) * blockDim.x + threadIdx.x; j < n4; j += U * stride) {
+      float4 a[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k)
+        if (j + k * stride < n4) a[k] = __ldcg(src + j + k * stride);
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        const long long o = ob + j + k * stride;
+        if (j + k * stride >= n4) break;
+        if (p.out_bf16)
+          reinterpret_cast<uint2*>(p.out)[o] = make_uint2(pack_bf16x2(a[k].x, a[k].y), pack_bf16x2(a[k].z, a[k].w));
+        else
+          reinterpret_cast<float4*>(p.out)[o] = a[k];
+      }
     }
   }
   cta_barrier(p, vc, depart, 121);
   }
-  vcta_release(p);
+  vcta_release(p, vct.epoch);
 }
 
 }  // namespace symm
@@ -379,9 +398,9 @@ int md_rs_shard(const MdRsParams* prm, int ctas, cudaStream_t s) {
 
 int md_symm_max_world() { return md::symm::kMaxWorld; }
 long long md_symm_flag_bytes() {
-  // Flag slots plus one {claimed, finished} counter pair per channel.
+  // Flag slots plus {claimed, finished, launches} counters per channel.
   return (static_cast<long long>(md::symm::kChannels) * md::symm::kMaxCtas * md::symm::kMaxWorld +
-          2 * md::symm::kChannels) * sizeof(uint32_t);
+          3 * md::symm::kChannels) * sizeof(uint32_t);
 }
 
 // Allocate `bytes` of zeroed device memory and export its IPC handle (64 bytes into handle_out).

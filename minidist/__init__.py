@@ -30,6 +30,7 @@ from .comm import (
 )
 from .ddp import DDP, DistributedDataParallel
 from .fsdp import FSDP, FullyShardedDataParallel, MixedPrecisionPolicy
+from .graphs import GraphedStep
 from .mesh import ParallelMesh
 from .pipeline import PipelineStage, build_schedule, partition_layers, theoretical_bubble_fraction
 from .profiling import analyze_trace, format_collective_table, profile_steps, summarize_collectives
@@ -43,6 +44,7 @@ from .tensor_parallel import (
 __version__ = "0.1.0"
 
 __all__ = [
+    "GraphedStep",
     "DDP",
     "DistributedDataParallel",
     "FSDP",

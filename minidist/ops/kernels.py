@@ -33,7 +33,7 @@ _SIGS = {
     "md_colsum": "i:pliippip",
     "md_ce_stats": "i:ppiipppppp",
     "md_ce_backward": "i:plpplpfpliip",
-    "md_adamw": "i:ppifffffffppip",
+    "md_adamw": "i:ppifffffffppipp",
     "md_adamw_chunk": "i:",
     "md_adamw_entry_bytes": "i:",
 }

@@ -6,6 +6,12 @@ as one multi-tensor sm_100a kernel per parameter group (csrc/optim.cu).  The
 kernel also refreshes the bf16 shadow weights the fused GEMMs read, so the
 next forward does not pay for a separate cast.  Off CUDA it runs the same
 arithmetic with torch ops, so CPU tests exercise identical semantics.
+
+``capturable=True`` keeps each group's learning rate and step count in device
+memory ([lr, t]; the kernel computes the bias corrections), so a training step
+captured in a CUDA graph (:class:`minidist.graphs.GraphedStep`) advances the
+step on every replay; :meth:`FusedAdamW.sync_hyperparams` refreshes the device
+learning rate from ``param_groups`` between replays.
 """
 
 from __future__ import annotations
@@ -22,11 +28,33 @@ __all__ = ["FusedAdamW"]
 
 class FusedAdamW(torch.optim.Optimizer):
     def __init__(self, params, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
-                 weight_decay: float = 1e-2):
+                 weight_decay: float = 1e-2, capturable: bool = False):
         if lr < 0 or eps < 0 or not (0 <= betas[0] < 1 and 0 <= betas[1] < 1):
             raise ValueError("invalid AdamW hyper-parameters")
         super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay))
         self._tables: dict[int, tuple] = {}
+        self.capturable = capturable
+        self._hp: dict[int, torch.Tensor] = {}  # capturable: device [lr, step] per group
+        self._hp_lr: dict[int, float] = {}
+
+    def sync_hyperparams(self) -> None:
+        """Copy each group's current ``lr`` into its device slot (capturable mode; call between
+        graph replays -- it launches work, so not while a graph is being captured)."""
+        for gi, hp in self._hp.items():
+            lr = float(self.param_groups[gi]["lr"])
+            if self._hp_lr.get(gi) != lr:
+                hp[0:1].fill_(lr)
+                self._hp_lr[gi] = lr
+
+    def state_dict(self):
+        # In capturable mode the step count advances on the device; bring it to the host state.
+        for gi, hp in self._hp.items():
+            t = float(hp[1].item())
+            for p in self.param_groups[gi]["params"]:
+                st = self.state.get(p)
+                if st and "step" in st:
+                    st["step"].fill_(t)
+        return super().state_dict()
 
     # -- state ----------------------------------------------------------------------
 
@@ -62,6 +90,19 @@ class FusedAdamW(torch.optim.Optimizer):
             cuda = [p.is_cuda and p.dtype == torch.float32 and p.grad.dtype == torch.float32 for p in params]
             fused = [p for p, c in zip(params, cuda) if c]
             rest = [p for p, c in zip(params, cuda) if not c]
+            hp = None
+            if self.capturable and fused:
+                hp = self._hp.get(gi)
+                if hp is None:
+                    if torch.cuda.is_current_stream_capturing():
+                        raise RuntimeError("FusedAdamW(capturable=True) needs one eager step before capture")
+                    hp = torch.tensor([lr, t - 1.0], dtype=torch.float32, device=fused[0].device)
+                    self._hp[gi], self._hp_lr[gi] = hp, float(lr)
+                if not torch.cuda.is_current_stream_capturing():
+                    self.sync_hyperparams()
+                hp[1:2].add_(1.0)
+            if rest and torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("FusedAdamW: only CUDA fp32 parameters can be stepped inside a CUDA graph")
             if fused:
                 # Parameters whose gradient all-reduce is still in flight (DDP with
                 # defer_last_buckets) are updated last, after waiting on its event.
@@ -69,14 +110,14 @@ class FusedAdamW(torch.optim.Optimizer):
                 if late:
                     early = [p for p in fused if getattr(p, "_md_grad_event", None) is None]
                     if early:
-                        self._fused_update((gi, 0), early, lr, b1, b2, eps, wd, bc1, bc2_sqrt)
+                        self._fused_update((gi, 0), early, lr, b1, b2, eps, wd, bc1, bc2_sqrt, hp)
                     for ev in {id(p._md_grad_event): p._md_grad_event for p in late}.values():
                         torch.cuda.current_stream().wait_event(ev)
                     for p in late:
                         p._md_grad_event = None
-                    self._fused_update((gi, 1), late, lr, b1, b2, eps, wd, bc1, bc2_sqrt)
+                    self._fused_update((gi, 1), late, lr, b1, b2, eps, wd, bc1, bc2_sqrt, hp)
                 else:
-                    self._fused_update(gi, fused, lr, b1, b2, eps, wd, bc1, bc2_sqrt)
+                    self._fused_update(gi, fused, lr, b1, b2, eps, wd, bc1, bc2_sqrt, hp)
                 self._ensure_grad_buffers()
             for p in rest:
                 st = self.state[p]
@@ -116,7 +157,7 @@ class FusedAdamW(torch.optim.Optimizer):
             off += n
         self._grad_flat = flat
 
-    def _fused_update(self, gi, params, lr, b1, b2, eps, wd, bc1, bc2_sqrt) -> None:
+    def _fused_update(self, gi, params, lr, b1, b2, eps, wd, bc1, bc2_sqrt, hp=None) -> None:
         from .models.fused_gpt import _SHADOW, _SHADOW_VER
 
         lib = nat.lib()
@@ -136,14 +177,17 @@ class FusedAdamW(torch.optim.Optimizer):
         dev = params[0].device
         if cached is None or cached[0] != key:
             chunk = lib.md_adamw_chunk()
-            table = torch.tensor(rows, dtype=torch.int64).to(dev)
             chunks = [(i, c) for i, p in enumerate(params) for c in range(-(-p.numel() // chunk))]
-            chunk_t = torch.tensor(chunks, dtype=torch.int32).to(dev)
-            cached = (key, table, chunk_t, len(chunks))
+            # Pinned sources: a copy from pageable memory is not allowed inside a graph capture.
+            table_h = torch.tensor(rows, dtype=torch.int64).pin_memory()
+            chunk_h = torch.tensor(chunks, dtype=torch.int32).pin_memory()
+            table = table_h.to(dev, non_blocking=True)
+            chunk_t = chunk_h.to(dev, non_blocking=True)
+            cached = (key, table, chunk_t, len(chunks), table_h, chunk_h)
             self._tables[gi] = cached
-        _, table, chunk_t, n = cached
+        table, chunk_t, n = cached[1], cached[2], cached[3]
         rc = lib.md_adamw(table.data_ptr(), chunk_t.data_ptr(), n, lr, b1, b2, eps, wd, bc1, bc2_sqrt,
-                          None, None, 0, nat.stream_ptr())
+                          None, None, 0, nat.stream_ptr(), None if hp is None else hp.data_ptr())
         nat.check(rc, "md_adamw")
         for p in params:
             if getattr(p, _SHADOW, None) is not None:

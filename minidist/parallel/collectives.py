@@ -42,7 +42,6 @@ class ArParams(ctypes.Structure):
         ("world", ctypes.c_int),
         ("rank", ctypes.c_int),
         ("scale", ctypes.c_float),
-        ("epoch", ctypes.c_uint32),
         ("channel", ctypes.c_int),
         ("timeout_ns", ctypes.c_ulonglong),
         ("status", ctypes.c_void_p),
@@ -67,7 +66,6 @@ def allreduce_fp32_(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offset:
     p.offset, p.n = elem_offset, n
     p.world, p.rank = buf.world, buf.rank
     p.scale = scale
-    p.epoch = comm_.next_epoch(channel) & 0x7FFFFFFF
     p.channel = channel
     p.timeout_ns = _timeout_ns()
     p.status = nat.status_ptr()
@@ -135,7 +133,6 @@ def all_reduce_(t: torch.Tensor, group) -> torch.Tensor:
     return t
 
 
-_TP_CHANNEL = 3
 
 
 class TpArParams(ctypes.Structure):
@@ -238,8 +235,11 @@ def gemm_all_reduce(x_local, w_local, bias, resid, group, b_mn: bool = False):
         ar.world, ar.rank = c.world, c.rank
         ar.max_chunks = flags.nbytes // 8
         ar.timeout_ns = _timeout_ns()
-        # Cluster-order counters (this rank only); the kernel leaves them at zero.
-        claim = torch.zeros(2, dtype=torch.int32, device=x_local.device)
+        # {claimed, finished, launches} counters of this rank: one set per communicator for
+        # its whole life, since the launch count is the flags' epoch.
+        claim = getattr(c, "tp_claim", None)
+        if claim is None:
+            claim = c.tp_claim = torch.zeros(3, dtype=torch.int32, device=x_local.device)
         ar.claim = claim.data_ptr()
         gp = nat.GemmParams()
         gp.M, gp.N, gp.K = M, N, K
@@ -256,7 +256,6 @@ def gemm_all_reduce(x_local, w_local, bias, resid, group, b_mn: bool = False):
         ar.resid, ar.ldr = resid.data_ptr(), resid.stride(0)
     else:
         ar.resid = None
-    ar.epoch = c.next_epoch(_TP_CHANNEL)
     gp.A, gp.B = x_local.data_ptr(), w_local.data_ptr()
     gp.lda, gp.ldb = x_local.stride(0), w_local.stride(0)
     rc = _LIB_GEMM_AR(gp_ref, ar_ref, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
@@ -283,7 +282,6 @@ class RsParams(ctypes.Structure):
         ("world", ctypes.c_int),
         ("rank", ctypes.c_int),
         ("scale", ctypes.c_float),
-        ("epoch", ctypes.c_uint32),
         ("channel", ctypes.c_int),
         ("timeout_ns", ctypes.c_ulonglong),
         ("status", ctypes.c_void_p),
@@ -329,7 +327,6 @@ def reduce_scatter_shard(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_of
     prm.offset, prm.shard = elem_offset, shard
     prm.world, prm.rank = comm_.world, comm_.rank
     prm.scale = scale
-    prm.epoch = comm_.next_epoch(_FSDP_CHANNEL)
     prm.channel = _FSDP_CHANNEL
     prm.timeout_ns = _timeout_ns()
     prm.status = nat.status_ptr(buf.device)
@@ -365,7 +362,6 @@ class AgParams(ctypes.Structure):
         ("shard", ctypes.c_longlong),
         ("world", ctypes.c_int),
         ("rank", ctypes.c_int),
-        ("epoch", ctypes.c_uint32),
         ("channel", ctypes.c_int),
         ("timeout_ns", ctypes.c_ulonglong),
         ("status", ctypes.c_void_p),
@@ -389,7 +385,6 @@ def all_gather_shards(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offse
         prm.flags[r] = buf.flag_ptrs[r]
     prm.offset, prm.shard = elem_offset, shard
     prm.world, prm.rank = comm_.world, comm_.rank
-    prm.epoch = comm_.next_epoch(_FSDP_AG_CHANNEL)
     prm.channel = _FSDP_AG_CHANNEL
     prm.timeout_ns = _timeout_ns()
     prm.status = nat.status_ptr(buf.device)

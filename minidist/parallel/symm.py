@@ -115,19 +115,15 @@ class SymmBuffer:
 
 
 class Communicator:
-    """Peer-memory state for one process group: buffers plus per-channel epoch counters."""
+    """Peer-memory state for one process group: its named symmetric buffers.  (Barrier epochs
+    are counted on the device, per flag page and channel, by the kernels themselves.)"""
 
     def __init__(self, group, ranks: list[int]):
         self.group = group
         self.ranks = list(ranks)
         self.world = comm.get_world_size(group)
         self.rank = comm.get_rank(group)
-        self.epochs = [0] * 8
         self.scratch: dict[str, SymmBuffer] = {}
-
-    def next_epoch(self, channel: int) -> int:
-        self.epochs[channel] += 1
-        return self.epochs[channel]
 
     def zeroed_buffer(self, name: str, nbytes: int) -> SymmBuffer:
         """Like :meth:`buffer`, but a new allocation is zero-filled on every rank before any

@@ -198,6 +198,55 @@ def check_tp_gpt(rank, world):
     nat.check_status()
 
 
+def _graph_vs_eager(rank, world, wrap, tp_size):
+    """Train the same model eagerly and as a replayed CUDA graph (GraphedStep); losses must agree."""
+    import minidist as md
+    from minidist.models import GPT, GPTConfig
+    from minidist.optim import FusedAdamW
+
+    cfg = GPTConfig(vocab_size=1024, block_size=128, n_layer=2, n_head=4, n_embd=256, seed=9)
+    g = torch.Generator().manual_seed(21)
+    batches = [(torch.randint(0, cfg.vocab_size, (2, 128), generator=g).cuda(),
+                torch.randint(0, cfg.vocab_size, (2, 128), generator=g).cuda()) for _ in range(6)]
+    out = []
+    for graph in (False, True):
+        mesh = md.ParallelMesh(tp_size=tp_size)
+        model = wrap(GPT(cfg, tp_group=mesh.tp_group, device="cuda"), mesh)
+        opt = FusedAdamW(model.parameters(), lr=1e-3, capturable=graph)
+
+        def step(x, y):
+            opt.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=torch.bfloat16, cache_enabled=False):
+                loss = model(x, y)[1]
+            loss.backward()
+            opt.step()
+            return loss
+
+        if graph:
+            run = md.GraphedStep(step, batches[0], warmup=2, optimizers=[opt])
+        else:
+            step(*batches[0])
+            step(*batches[0])
+            run = step
+        losses = [float(run(*b).item()) for b in batches[1:]]
+        if graph:
+            run.release()
+        out.append(losses)
+    for a, b in zip(*out, strict=True):
+        assert abs(a - b) <= 3e-3 * abs(a), (rank, out)
+    nat.check_status()
+
+
+def check_graphs(rank, world):
+    """DDP (peer-memory bucket all-reduce) and tensor parallelism (fused GEMM + all-reduce) inside
+    a CUDA graph: the device-counted barrier epochs keep replays correct."""
+    import minidist as md
+
+    _graph_vs_eager(rank, world, lambda m, mesh: md.DistributedDataParallel(
+        m, process_group=mesh.dp_group, bucket_cap_mb=1.0, defer_last_buckets=2), tp_size=1)
+    _graph_vs_eager(rank, world, lambda m, mesh: m, tp_size=world)
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
@@ -208,6 +257,7 @@ def main():
         check_ddp(rank, world)
         check_fsdp(rank, world)
         check_tp_gpt(rank, world)
+        check_graphs(rank, world)
     finally:
         symm.release_all()
         dist.barrier()

@@ -39,15 +39,17 @@ def test_bucket_allreduce_times_out_when_peer_never_arrives():
     p = C.ArParams()
     for r in range(2):
         p.bufs[r], p.flags[r] = bufs[r].data_ptr(), flags[r].data_ptr()
-    p.offset, p.n, p.world, p.rank, p.scale, p.epoch, p.channel = 0, n, 2, 0, 0.5, 1, 0
+    p.offset, p.n, p.world, p.rank, p.scale, p.channel = 0, n, 2, 0, 0.5, 0
     p.timeout_ns = 2_000_000
     p.status = nat.status_ptr()
     nat.check(nat.lib().md_allreduce(ctypes.byref(p), 4, ctypes.c_void_p(nat.stream_ptr())), "md_allreduce")
     with pytest.raises(nat.CommTimeoutError):
         nat.check_status()
     nat.check_status()  # the word was reset
-    # The virtual-CTA counters of the channel were reset by the launch's last CTA.
-    assert flags[0][-16:].abs().sum().item() == 0
+    # The claim counters of channel 0 were reset by the launch's last CTA and the
+    # launch was counted (the words behind the flag slots: 3 per channel).
+    base = flags[0].numel() - 24
+    assert flags[0][base:base + 3].tolist() == [0, 0, 1]
     _after_check()
 
 
@@ -68,9 +70,9 @@ def test_fused_gemm_allreduce_times_out_when_peer_never_publishes():
     for r in range(2):
         ar.partial[r], ar.fin[r], ar.flags[r] = part[r].data_ptr(), fin[r].data_ptr(), flags[r].data_ptr()
     ar.ldp, ar.out, ar.ldo = N, out.data_ptr(), N
-    ar.world, ar.rank, ar.epoch, ar.max_chunks = 2, 0, 1, chunks
+    ar.world, ar.rank, ar.max_chunks = 2, 0, chunks
     ar.timeout_ns = 1_000_000
-    claim = torch.zeros(2, dtype=torch.int32, device="cuda")
+    claim = torch.zeros(3, dtype=torch.int32, device="cuda")
     ar.claim = claim.data_ptr()
     gp = nat.GemmParams()
     gp.A, gp.B, gp.lda, gp.ldb = x.data_ptr(), w.data_ptr(), K, K
@@ -81,5 +83,5 @@ def test_fused_gemm_allreduce_times_out_when_peer_never_publishes():
     with pytest.raises(nat.CommTimeoutError):
         nat.check_status()
     nat.check_status()
-    assert claim.tolist() == [0, 0], "cluster-order counters not reset"
+    assert claim.tolist() == [0, 0, 1], "cluster-order counters not reset / launch not counted"
     _after_check()
