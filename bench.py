@@ -276,9 +276,26 @@ def main() -> int:
         import minidist as md
 
         # Two eager steps (lazy initialisation), then one capture; the W warm-up
-        # steps below are replays.
-        graphed = md.GraphedStep(step, dev_batches[0], warmup=2, optimizers=[opt])
-        step = graphed
+        # steps below are replays.  Every rank takes the graph or none does.
+        ok = 1
+        try:
+            graphed = md.GraphedStep(step, dev_batches[0], warmup=2, optimizers=[opt])
+        except Exception as exc:  # noqa: BLE001 -- report and run eagerly
+            print(f"bench: CUDA-graph capture failed on rank {rank} ({exc!r}); running eagerly",
+                  file=sys.stderr, flush=True)
+            ok = 0
+        if world > 1:
+            import torch.distributed as dist
+
+            flag = torch.tensor([ok], dtype=torch.int32, device="cuda")
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            ok = int(flag.item())
+        if ok:
+            step = graphed
+        else:
+            if graphed is not None:
+                graphed.release()
+            graphed, graph = None, False
 
     # Clock sampling: one nvidia-smi per node (local rank 0) over every GPU of
     # this node's ranks, started before the warm-up so its start-up is over
