@@ -659,8 +659,10 @@ int md_attn_bwd_tc(const void* qkv, long long ldq, const void* out, long long ld
   const long long nd = static_cast<long long>(B) * H * S;
   int g1 = static_cast<int>((nd + 255) / 256);
   if (g1 > 148 * 32) g1 = 148 * 32;
-  md::attn::delta_kernel<64><<<g1, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(out), ldo,
-                                                 reinterpret_cast<const __nv_bfloat16*>(dout), lddo, delta, B, H, S);
+  // out == null: delta was produced upstream (the epilogue of the GEMM that made dout).
+  if (out != nullptr)
+    md::attn::delta_kernel<64><<<g1, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(out), ldo,
+                                                   reinterpret_cast<const __nv_bfloat16*>(dout), lddo, delta, B, H, S);
   int rc = md_attn_bwd_tc_main(qkv, ldq, dout, lddo, lse, delta, dqacc, static_cast<long long>(H) * D, dqkv, lddq, B,
                                H, S, D, scale, status, st);
   if (rc != 0) return rc;

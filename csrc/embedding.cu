@@ -169,13 +169,29 @@ __global__ void __launch_bounds__(256) colsum_partial8_kernel(const __nv_bfloat1
   }
 }
 
-__global__ void colsum_final_kernel(const float* __restrict__ partial, int chunks, int N, float* __restrict__ out,
-                                    int accumulate) {
-  const int n = blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= N) return;
+// Second stage: out[n] (+)= sum over the partial rows.  A CTA covers 32
+// columns with 32 warps; warp w takes rows w, w+32, ... (a few loads each, all
+// in flight) and the 32 warp sums are added in a fixed order, so the result is
+// deterministic and the pass costs about one memory latency.
+__global__ void __launch_bounds__(1024) colsum_final_kernel(const float* __restrict__ partial, int chunks, int N,
+                                                            float* __restrict__ out, int accumulate) {
+  __shared__ float red[32][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int n = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int c = 0; c < chunks; ++c) s += partial[static_cast<long long>(c) * N + n];
-  out[n] = accumulate ? out[n] + s : s;
+  if (n < N) {
+    const float* col = partial + n;
+#pragma unroll 4
+    for (int c = w; c < chunks; c += 32) s += __ldg(col + static_cast<long long>(c) * N);
+  }
+  red[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && n < N) {
+    float t = 0.f;
+#pragma unroll
+    for (int g = 0; g < 32; ++g) t += red[g][lane];
+    out[n] = accumulate ? out[n] + t : t;
+  }
 }
 
 }  // namespace emb
@@ -247,7 +263,15 @@ int md_colsum(const void* x, long long ldx, int M, int N, float* partial, float*
     md::emb::colsum_partial_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, N,
                                                          rows_per_chunk, partial);
   }
-  md::emb::colsum_final_kernel<<<(N + 255) / 256, 256, 0, s>>>(partial, chunks, N, out, accumulate);
+  md::emb::colsum_final_kernel<<<(N + 31) / 32, 1024, 0, s>>>(partial, chunks, N, out, accumulate);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// Second stage alone: out[n] (+)= sum_c partial[c * N + n] (first stages fused
+// into producers, e.g. the GEMM's kEpiDGELU column sums).
+int md_colsum_final(const float* partial, int chunks, int N, float* out, int accumulate, cudaStream_t s) {
+  if (chunks <= 0 || N <= 0) return -1;
+  md::emb::colsum_final_kernel<<<(N + 31) / 32, 1024, 0, s>>>(partial, chunks, N, out, accumulate);
   return static_cast<int>(cudaGetLastError());
 }
 

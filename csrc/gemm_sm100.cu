@@ -109,6 +109,20 @@ struct MdGemmParams {
   md::Status* status;
   int cta_group;               // 0 = choose, 1 or 2
   int epi_warps;               // 0 = choose, 4 or 8
+  // kEpiDGELU: per-32-row column sums of the (bf16-rounded) output, fp32
+  // [ceil(M/32), N] -- the bias gradient's first stage, so the output is not
+  // read back for it -- or null.
+  float* colsum;
+  // kEpiBF16 without bias / GELU / residual: row-wise dot products of the
+  // (bf16-rounded) output with `dot_in` over groups of `dot_group` columns
+  // (32, 64 or 128), written to dot_out[((row / dot_seq) * (N / dot_group) + g)
+  // * dot_seq + row % dot_seq] -- the attention backward's
+  // delta = rowsum(dO * O) per (batch, head, query) from the GEMM producing dO.
+  const void* dot_in;          // bf16 [M, lddot] or null
+  long long lddot;
+  float* dot_out;
+  int dot_group;
+  int dot_seq;
 };
 
 // Fused tensor-parallel all-reduce of the GEMM output (md_gemm_ar): the
@@ -356,6 +370,9 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
   if (EPI == kEpiBF16 && p.resid != nullptr) {
     in_base = reinterpret_cast<const __nv_bfloat16*>(p.resid);
     in_ld = p.ldres;
+  } else if (EPI == kEpiBF16 && p.dot_out != nullptr) {
+    in_base = reinterpret_cast<const __nv_bfloat16*>(p.dot_in);
+    in_ld = p.lddot;
   } else if (EPI == kEpiDGELU) {
     in_base = reinterpret_cast<const __nv_bfloat16*>(p.aux);
     in_ld = p.ldaux;
@@ -370,6 +387,7 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
     }
   };
   load_in(c_begin);
+  float dot_acc = 0.f;
 #pragma unroll 1
   for (int slab = c_begin / 4; slab < c_end / 4; ++slab) {
     float ce_m = -INFINITY, ce_s = 0.f;
@@ -417,6 +435,29 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
           // GELU of the bf16-rounded pre-activation: exactly what backward differentiates.
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+        }
+        if (p.dot_out != nullptr) {
+          // Dot product of this row's bf16 output with dot_in over the group.
+          if (row_ok && full) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 w = cur[q];
+              const float2 f0 = unpack_bf16x2(w.x), f1 = unpack_bf16x2(w.y), f2 = unpack_bf16x2(w.z),
+                           f3 = unpack_bf16x2(w.w);
+              const float o[8] = {f0.x, f0.y, f1.x, f1.y, f2.x, f2.y, f3.x, f3.y};
+#pragma unroll
+              for (int e = 0; e < 8; ++e) dot_acc += __bfloat162float(__float2bfloat16_rn(v[q * 8 + e])) * o[e];
+            }
+          }
+          const int gsz = p.dot_group >> 5;  // chunks per group
+          if ((c + 1) % gsz == 0) {
+            if (row_ok) {
+              const int g = (n0 + 32) / p.dot_group - 1;
+              const long long b = row / p.dot_seq, q = row % p.dot_seq;
+              p.dot_out[(b * (p.N / p.dot_group) + g) * p.dot_seq + q] = dot_acc;
+            }
+            dot_acc = 0.f;
+          }
         }
         if (p.resid != nullptr && row_ok) {
           const __nv_bfloat16* rs = reinterpret_cast<const __nv_bfloat16*>(p.resid) + row * p.ldres + n0;
@@ -504,6 +545,28 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
                        "r"(pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5])), "r"(pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]))
                        : "memory");
         if ((c & 1) == 1 || n0 + 32 >= p.N) {
+          if (EPI == kEpiDGELU && p.colsum != nullptr && row0 < p.M) {  // warp-uniform
+            // Bias-gradient first stage from the staged bf16 slab (32 rows x 64
+            // columns): lane l sums columns 2l, 2l+1 down the rows, one
+            // conflict-free 128-byte row per load.
+            __syncwarp();
+            const int sn0 = n0 - (c & 1) * 32;
+            const int rows = min(32, p.M - row0);
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll 8
+            for (int r = 0; r < rows; ++r) {
+              uint32_t w;
+              asm volatile("ld.shared.b32 %0, [%1];"
+                           : "=r"(w)
+                           : "r"(smem_u32(sb + sw128_off(r, lane >> 2)) + (lane & 3) * 4));
+              const float2 f = unpack_bf16x2(w);
+              s0 += f.x;
+              s1 += f.y;
+            }
+            float* dst = p.colsum + static_cast<long long>(row0 >> 5) * p.N;
+            if (sn0 + 2 * lane < p.N) dst[sn0 + 2 * lane] = s0;
+            if (sn0 + 2 * lane + 1 < p.N) dst[sn0 + 2 * lane + 1] = s1;
+          }
           slab_issue(es, tmD, sb, 0, 2, n0 - (c & 1) * 32, row0, 0);
           if (two) slab_issue(es, tmX, es.base + kSlabBytes, 0, 2, n0 - (c & 1) * 32, row0, 0);
         }
@@ -1169,6 +1232,11 @@ extern "C" int md_gemm(const MdGemmParams* prm, cudaStream_t stream) {
   if (p.gelu && (p.aux == nullptr || !aligned16(p.aux) || (p.ldaux % 8))) return -7;
   if (p.epi == kEpiDGELU && (p.aux == nullptr || !aligned16(p.aux) || (p.ldaux % 8))) return -7;
   if (p.resid != nullptr && (!aligned16(p.resid) || (p.ldres % 8))) return -8;
+  if (p.dot_out != nullptr &&
+      (p.epi != kEpiBF16 || p.gelu || p.resid != nullptr || p.k_splits != 1 || p.dot_in == nullptr ||
+       !aligned16(p.dot_in) || (p.lddot % 8) || !(p.dot_group == 32 || p.dot_group == 64 || p.dot_group == 128) ||
+       (p.N % p.dot_group) || p.dot_seq <= 0 || (p.M % p.dot_seq)))
+    return -10;
   if (p.epi == kEpiCE && (p.ce_target == nullptr || p.ce_max == nullptr || p.ce_sum == nullptr || p.ce_tgt == nullptr))
     return -9;
   if (p.k_splits < 1) p.k_splits = 1;

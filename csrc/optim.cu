@@ -29,7 +29,7 @@ struct MdAdamEntry {
 namespace md {
 namespace optim {
 
-constexpr int kChunk = 32768;
+constexpr int kChunk = 8192;  // ~13 waves at GPT-2 size: a short tail wave
 
 __global__ void __launch_bounds__(256) adamw_kernel(const MdAdamEntry* __restrict__ table,
                                                     const int2* __restrict__ chunks, float lr, float b1, float b2,

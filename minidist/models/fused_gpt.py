@@ -263,14 +263,19 @@ class _BlockFn(torch.autograd.Function):
         if t_mw is not None:
             G.linear_wgrad(dx2, a, t_mw.dst, accumulate=t_mw.accumulate)
             t_mw.commit()
-        dh = G.linear_dgrad(dx2, w_mproj, gelu_preact=hpre)
-        # MLP fc (column-parallel)
+        # MLP fc (column-parallel); its bias gradient's first stage comes out of the
+        # dGELU epilogue (per-32-row column sums), so dh is not read back for it.
         t_fw, t_fb = _targets(mlp.fc.weight, mlp.fc.bias)
+        fb_part = None
+        if t_fb is not None:
+            fb_part = torch.empty(-(-dx2.shape[0] // 32) * w_mproj.shape[1], dtype=torch.float32,
+                                  device=dx2.device)
+        dh = G.linear_dgrad(dx2, w_mproj, gelu_preact=hpre, colsum_partial=fb_part)
         if t_fw is not None:
             G.linear_wgrad(dh, h2, t_fw.dst, accumulate=t_fw.accumulate)
             t_fw.commit()
         if t_fb is not None:
-            K.colsum(dh, t_fb.dst, accumulate=t_fb.accumulate)
+            K.colsum_final(fb_part, -(-dx2.shape[0] // 32), t_fb.dst, accumulate=t_fb.accumulate)
             t_fb.commit()
         dh2 = _dgrad_all_reduce(dh, w_fc, group)  # f: gradient of the replicated LN2 output
         # LN2 backward + residual, with both row-parallel bias gradients fused.
@@ -289,8 +294,14 @@ class _BlockFn(torch.autograd.Function):
         if t_pw is not None:
             G.linear_wgrad(dx1, y, t_pw.dst, accumulate=t_pw.accumulate)
             t_pw.commit()
-        dy = G.linear_dgrad(dx1, w_proj)
-        dqkv = K.attention_bwd(qkv, y, dy, lse, B, S, H, D)
+        # dO, with the attention backward's delta = rowsum(dO * O) from the same epilogue.
+        delta = None
+        if D == 64 and K.attention_bwd_impl() == "tc":
+            delta = torch.empty(B * H * S, dtype=torch.float32, device=dx1.device)
+            dy = G.linear_dgrad(dx1, w_proj, dot=(y, delta, D, S))
+        else:
+            dy = G.linear_dgrad(dx1, w_proj)
+        dqkv = K.attention_bwd(qkv, y, dy, lse, B, S, H, D, delta=delta)
         # QKV (column-parallel)
         t_qw, t_qb = _targets(attn.qkv.weight, attn.qkv.bias)
         if t_qw is not None:

@@ -133,6 +133,12 @@ class GemmParams(ctypes.Structure):
         ("status", ctypes.c_void_p),
         ("cta_group", ctypes.c_int),
         ("epi_warps", ctypes.c_int),
+        ("colsum", ctypes.c_void_p),
+        ("dot_in", ctypes.c_void_p),
+        ("lddot", ctypes.c_longlong),
+        ("dot_out", ctypes.c_void_p),
+        ("dot_group", ctypes.c_int),
+        ("dot_seq", ctypes.c_int),
     ]
 
 

@@ -66,6 +66,8 @@ def gemm(
     num_sms: int = 0,
     cta_group: int = 0,
     epi_warps: int = 0,
+    colsum: torch.Tensor | None = None,
+    dot: tuple | None = None,
     stream: torch.cuda.Stream | None = None,
 ) -> None:
     """Raw launcher; see ``struct MdGemmParams`` for the meaning of each field."""
@@ -98,6 +100,11 @@ def gemm(
     p.num_sms = num_sms
     p.cta_group = cta_group or _ENV_CG
     p.epi_warps = epi_warps or _ENV_EW
+    p.colsum = None if colsum is None else colsum.data_ptr()
+    if dot is not None:
+        dot_in, dot_out, group, seq = dot
+        p.dot_in, p.lddot, p.dot_out, p.dot_group, p.dot_seq = (
+            dot_in.data_ptr(), _ld(dot_in), dot_out.data_ptr(), group, seq)
     p.status = nat.status_ptr(D.device)
     rc = nat.lib().md_gemm(ctypes.byref(p), ctypes.c_void_p(nat.stream_ptr(stream)))
     nat.check(rc, f"md_gemm(M={M},N={N},K={K},a_mn={a_mn},b_mn={b_mn},epi={epi})")
@@ -165,15 +172,27 @@ def linear_dgrad(
     *,
     gelu_preact: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
+    colsum_partial: torch.Tensor | None = None,
+    dot: tuple | None = None,
 ) -> torch.Tensor:
-    """``dx = dy @ w`` (bf16); with ``gelu_preact`` returns ``(dy @ w) * gelu'(preact)``."""
+    """``dx = dy @ w`` (bf16); with ``gelu_preact`` returns ``(dy @ w) * gelu'(preact)``.
+
+    ``colsum_partial`` (with ``gelu_preact``): fp32 ``[ceil(M/32) * K]`` that receives the
+    per-32-row column sums of the result (finish with ``kernels.colsum_final``).
+    ``dot = (o, out, group, seq)`` (without ``gelu_preact``): also writes the row-wise dot products
+    of the result with ``o`` over each ``group`` columns (32 / 64 / 128) to
+    ``out[((row // seq) * (K // group) + g) * seq + row % seq]`` (fp32) -- the attention
+    backward's ``delta`` when the result is dO and ``o`` the attention output."""
     M, N = dy.shape
     K = w.shape[1]
     if out is None:
         out = empty_padded(M, K, device=dy.device)
     epi = EPI_DGELU if gelu_preact is not None else EPI_BF16
+    if colsum_partial is not None and (epi != EPI_DGELU or colsum_partial.numel() < -(-M // 32) * K):
+        raise ValueError("colsum_partial needs gelu_preact and ceil(M/32) * K elements")
     gemm(dy, w, out, M=M, N=K, K=N, lda=_ld(dy), ldb=_ld(w), ldd=_ld(out), b_mn=True, epi=epi,
-         aux=gelu_preact, ldaux=_ld(gelu_preact) if gelu_preact is not None else 0)
+         aux=gelu_preact, ldaux=_ld(gelu_preact) if gelu_preact is not None else 0, colsum=colsum_partial,
+         dot=dot)
     return out
 
 

@@ -31,6 +31,7 @@ _SIGS = {
     "md_embed_bwd_wpe": "i:plpliiiip",
     "md_colsum_chunks": "i:ii",
     "md_colsum": "i:pliippip",
+    "md_colsum_final": "i:piipip",
     "md_ce_stats": "i:ppiipppppp",
     "md_ce_backward": "i:plpplpfpliip",
     "md_adamw": "i:ppifffffffppipp",
@@ -124,16 +125,27 @@ def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int, D: int, impl: str |
     return out, lse
 
 
+def attention_bwd_impl() -> str:
+    """The attention backward in use: ``"tc"`` (tcgen05, d = 64) or ``"mma"``."""
+    return _ATTN_BWD
+
+
 def attention_bwd(qkv, out, dout, lse, B: int, S: int, H: int, D: int, dqkv: torch.Tensor | None = None,
-                  impl: str | None = None):
-    """Gradients w.r.t. ``qkv`` in the same interleaved layout."""
+                  impl: str | None = None, delta: torch.Tensor | None = None):
+    """Gradients w.r.t. ``qkv`` in the same interleaved layout.
+
+    ``delta``: ``rowsum(dout * out)`` per (batch, head, query), fp32 ``[B*H*S]``, when the caller
+    already has it (the dO-producing GEMM's dot epilogue, ``gemm.linear_dgrad(dot=...)``)."""
     if dqkv is None:
         dqkv = empty_padded(B * S, 3 * H * D, device=qkv.device)
-    delta = torch.empty(B * H * S, dtype=torch.float32, device=qkv.device)
+    have_delta = delta is not None
+    if delta is None:
+        delta = torch.empty(B * H * S, dtype=torch.float32, device=qkv.device)
     dqacc = torch.empty(B * S, H * D, dtype=torch.float32, device=qkv.device)
     impl = impl or _ATTN_BWD
     if impl == "tc" and D == 64:
-        rc = nat.lib().md_attn_bwd_tc(qkv.data_ptr(), _ld(qkv), out.data_ptr(), _ld(out), dout.data_ptr(), _ld(dout),
+        rc = nat.lib().md_attn_bwd_tc(qkv.data_ptr(), _ld(qkv), None if have_delta else out.data_ptr(), _ld(out),
+                                      dout.data_ptr(), _ld(dout),
                                       lse.data_ptr(), delta.data_ptr(), dqacc.data_ptr(), dqkv.data_ptr(), _ld(dqkv),
                                       B, H, S, D, 1.0 / math.sqrt(D), nat.status_ptr(qkv.device), _s())
         nat.check(rc, f"md_attn_bwd_tc(D={D})")
@@ -184,6 +196,14 @@ def colsum(x: torch.Tensor, out: torch.Tensor, accumulate: bool = False) -> torc
     partial = torch.empty(lib.md_colsum_chunks(M, N) * N, dtype=torch.float32, device=x.device)
     rc = lib.md_colsum(x.data_ptr(), _ld(x), M, N, partial.data_ptr(), out.data_ptr(), int(accumulate), _s())
     nat.check(rc, "md_colsum")
+    return out
+
+
+def colsum_final(partial: torch.Tensor, chunks: int, out: torch.Tensor, accumulate: bool = False) -> torch.Tensor:
+    """``out[n] (+)= sum_c partial[c, n]`` over ``chunks`` fp32 partial rows (fixed order)."""
+    N = out.numel()
+    rc = nat.lib().md_colsum_final(partial.data_ptr(), chunks, N, out.data_ptr(), int(accumulate), _s())
+    nat.check(rc, "md_colsum_final")
     return out
 
 

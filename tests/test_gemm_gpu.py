@@ -112,3 +112,38 @@ def test_cta_group_variants(cg, a_mn, b_mn):
     Bf = B.float() if b_mn else B.float().t()
     nat.check_status()
     assert _rel(D, Af @ Bf) < 1e-4
+
+
+@pytest.mark.parametrize("M,N,K", [(1000, 384, 640), (4096, 768, 3072), (333, 256, 200)])
+def test_dgrad_gelu_fused_bias_colsum(M, N, K):
+    """kEpiDGELU's per-32-row column sums + colsum_final equal the column sum of the output."""
+    from minidist.ops import kernels as Kn
+
+    dy = torch.randn(M, N, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    h = torch.randn(M, K, device="cuda").bfloat16()
+    chunks = -(-M // 32)
+    part = torch.full((chunks * K,), float("nan"), device="cuda")
+    dx = G.linear_dgrad(dy, w, gelu_preact=h, colsum_partial=part)
+    out = torch.full((K,), 0.5, device="cuda")
+    Kn.colsum_final(part, chunks, out, accumulate=True)
+    want = dx.float().sum(0) + 0.5
+    torch.testing.assert_close(out, want, rtol=1e-4, atol=1e-3)
+    # The same output as without the fused sums.
+    torch.testing.assert_close(dx, G.linear_dgrad(dy, w, gelu_preact=h), rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("M,N,K,group,seq", [(2048, 768, 768, 64, 1024), (512, 384, 256, 128, 128),
+                                             (1024, 256, 96, 32, 256)])
+def test_dgrad_fused_rowwise_dot(M, N, K, group, seq):
+    """The dot epilogue: delta[(b*G + g)*S + q] = sum over group g of bf16(dy @ w)[row] * o[row]."""
+    dy = torch.randn(M, N, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    o = torch.randn(M, K, device="cuda").bfloat16()
+    delta = torch.full((M * (K // group),), float("nan"), device="cuda")
+    dx = G.linear_dgrad(dy, w, dot=(o, delta, group, seq))
+    nat.check_status()
+    prod = (dx.float() * o.float()).reshape(M // seq, seq, K // group, group).sum(-1)  # [B, S, G]
+    want = prod.permute(0, 2, 1).reshape(-1)
+    torch.testing.assert_close(delta, want, rtol=1e-4, atol=1e-3)
+    torch.testing.assert_close(dx, G.linear_dgrad(dy, w), rtol=0, atol=0)
