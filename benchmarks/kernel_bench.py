@@ -61,6 +61,26 @@ def bench_gemm(M, N, K, iters, cta_group=0, which="fwd,dgrad,wgrad"):
         t = timed(lambda: G.gemm(dy, w, dx, M=M, N=K, K=N, lda=dy.stride(0), ldb=K, ldd=K, b_mn=True, cta_group=cta_group), iters)
         tc = timed(lambda: torch.matmul(dy, w), iters)
         rows.append(("dgrad", t, tc))
+    if "gelu" in which.split(","):
+        # fc forward: bias + GELU epilogue storing both the activation and the pre-activation
+        bias = torch.randn(N, device="cuda")
+        pre = G.empty_padded(M, N, device="cuda")
+        t = timed(lambda: G.linear_fwd(x, w, bias, gelu=True, out=out, preact_out=pre), iters)
+        bb = bias.bfloat16()
+        tc = timed(lambda: F.gelu(torch.addmm(bb, x, w.t()), approximate="tanh"), iters)
+        rows.append(("gelu", t, tc))
+    if "dgelu" in which.split(","):
+        # MLP backward: dgrad with the GELU derivative fused (pre-activation [M, K] read in the epilogue)
+        h = torch.randn(M, K, device="cuda").bfloat16()
+        t = timed(lambda: G.linear_dgrad(dy, w, gelu_preact=h, out=dx), iters)
+        hf = h.float()
+
+        def ref():
+            g = torch.matmul(dy, w).float()
+            th = torch.tanh(0.7978845608 * (hf + 0.044715 * hf ** 3))
+            return g * (0.5 * (1 + th) + 0.5 * hf * (1 - th * th) * 0.7978845608 * (1 + 3 * 0.044715 * hf * hf))
+        tc = timed(ref, iters)
+        rows.append(("dgelu", t, tc))
     if "wgrad" in which:
         t = timed(lambda: G.linear_wgrad(dy, x, dw), iters)
         tc = timed(lambda: torch.matmul(dy.t(), x), iters)

@@ -387,6 +387,9 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
     }
   };
   load_in(c_begin);
+  // The chunk's bias is loaded before its TMEM load, so the two latencies
+  // overlap (a load at the point of use stalled every chunk on it).
+  const bool bias_vec = EPI == kEpiBF16 && p.bias != nullptr && (reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0;
   float dot_acc = 0.f;
 #pragma unroll 1
   for (int slab = c_begin / 4; slab < c_end / 4; ++slab) {
@@ -400,22 +403,51 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
 #pragma unroll
       for (int q = 0; q < 4; ++q) cur[q] = nxt[q];
       load_in(c + 1);
+      float4 bcur[8];
+      if (bias_vec) {
+        if (n0 + 32 <= p.N) {
+          const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) bcur[q] = __ldg(b4 + q);
+        } else {
+          float* bf = reinterpret_cast<float*>(bcur);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) bf[j] = n0 + j < p.N ? __ldg(p.bias + n0 + j) : 0.f;
+        }
+      }
       uint32_t r[32];
       tmem_ld_32x32b_x32(t_row + c * 32, r);
       tmem_ld_wait();
       const bool full = (n0 + 32 <= p.N);
       float v[32];
+      if (p.alpha != 1.f) {  // warp-uniform
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      }
 
       if (EPI == kEpiBF16) {
-        if (p.bias != nullptr) {
+        if (bias_vec) {
+          const float* bf = reinterpret_cast<const float*>(bcur);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += bf[j];
+        } else if (p.bias != nullptr) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] += (n0 + j < p.N) ? p.bias[n0 + j] : 0.f;
         }
         if (p.gelu) {
+          // The pre-activation, rounded to bf16 once: packed pairs are stored
+          // and unpacked back, so backward differentiates exactly this value.
+          uint32_t pk[16];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
+          for (int q = 0; q < 16; ++q) pk[q] = pack_bf16x2(v[2 * q], v[2 * q + 1]);
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            v[2 * q] = __uint_as_float(pk[q] << 16);
+            v[2 * q + 1] = __uint_as_float(pk[q] & 0xFFFF0000u);
+          }
           // The pre-activation goes out through the second slab of this warp
           // (TMA store on tmX at the end of the slab); see the staging below.
           if ((c & 1) == 0) {
@@ -429,8 +461,7 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
           for (int q = 0; q < 4; ++q)
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
                              smem_u32(es.base + kSlabBytes + sw128_off(lane, (c & 1) * 4 + q))),
-                         "r"(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1])), "r"(pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3])),
-                         "r"(pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5])), "r"(pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]))
+                         "r"(pk[4 * q]), "r"(pk[4 * q + 1]), "r"(pk[4 * q + 2]), "r"(pk[4 * q + 3])
                          : "memory");
           // GELU of the bf16-rounded pre-activation: exactly what backward differentiates.
 #pragma unroll
@@ -980,9 +1011,39 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
     es.lane = lane;
     int acc = 0;
     uint32_t acc_phase = 0;
+    // The epilogue's second input (pre-activation, residual or dot operand) is
+    // streamed from HBM one chunk ahead; an L2 prefetch of this thread's row
+    // segment of the NEXT tile gives those loads a whole tile of lead time.
+    const __nv_bfloat16* pf_base = nullptr;
+    long long pf_ld = 0;
+    if (EPI == kEpiDGELU) {
+      pf_base = reinterpret_cast<const __nv_bfloat16*>(p.aux);
+      pf_ld = p.ldaux;
+    } else if (EPI == kEpiBF16 && p.resid != nullptr) {
+      pf_base = reinterpret_cast<const __nv_bfloat16*>(p.resid);
+      pf_ld = p.ldres;
+    } else if (EPI == kEpiBF16 && p.dot_out != nullptr) {
+      pf_base = reinterpret_cast<const __nv_bfloat16*>(p.dot_in);
+      pf_ld = p.lddot;
+    }
+    auto prefetch_in = [&](int uu) {
+      if (pf_base == nullptr || uu >= kp.units) return;
+      int tm2, tn2, sp2;
+      decode_unit(kp, uu, tm2, tn2, sp2);
+      const long long row = tm2 * (CG * BM) + static_cast<int>(crank) * BM + quarter * 32 + lane;
+      const int col0 = tn2 * BN + c_begin * 32;
+      const int col1 = min(p.N, tn2 * BN + c_end * 32);
+      if (row >= p.M || col0 >= col1) return;
+      const char* a = reinterpret_cast<const char*>(pf_base + row * pf_ld + col0);
+      const char* e = reinterpret_cast<const char*>(pf_base + row * pf_ld + col1) - 1;
+      for (const char* q = a; q < e; q += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(q));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(e));
+    };
+    prefetch_in(cluster_id);
     for (int u = cluster_id; u < kp.units; u += nclusters) {
       int tm, tn, split;
       decode_unit(kp, u, tm, tn, split);
+      prefetch_in(u + nclusters);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, p.status, 30, abort_flag)) break;
       tc_fence_after();
       const int row0 = tm * (CG * BM) + static_cast<int>(crank) * BM + quarter * 32;

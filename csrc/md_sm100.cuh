@@ -311,21 +311,25 @@ __device__ __forceinline__ float tanh_fast(float x) {
 }
 
 // GELU, tanh form (Hendrycks & Gimpel 2016): 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
+// gelu_tanh(x) = 0.5 x (1 + tanh(u)), u = k0 (x + k1 x^3) = x (k0 + k0 k1 x^2),
+// written as fused multiply-adds (six operations with the tanh).
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
-  const float k1 = 0.044715f;
-  float u = k0 * (x + k1 * x * x * x);
-  return 0.5f * x * (1.0f + tanh_fast(u));
+  const float k0k1 = 0.7978845608028654f * 0.044715f;
+  const float u = x * fmaf(x * x, k0k1, k0);
+  const float h = 0.5f * x;
+  return fmaf(h, tanh_fast(u), h);
 }
 
-// d/dx of gelu_tanh.
+// d/dx of gelu_tanh = 0.5 (1 + t) + 0.5 x (1 - t^2) k0 (1 + 3 k1 x^2), t = tanh(u).
 __device__ __forceinline__ float gelu_tanh_grad(float x) {
   const float k0 = 0.7978845608028654f;
-  const float k1 = 0.044715f;
-  float x2 = x * x;
-  float u = k0 * (x + k1 * x2 * x);
-  float t = tanh_fast(u);
-  return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * k0 * (1.0f + 3.0f * k1 * x2);
+  const float k0k1 = 0.7978845608028654f * 0.044715f;
+  const float x2 = x * x;
+  const float t = tanh_fast(x * fmaf(x2, k0k1, k0));
+  const float a = fmaf(0.5f, t, 0.5f);
+  const float b = x * fmaf(x2, 1.5f * k0k1, 0.5f * k0);  // 0.5 x k0 (1 + 3 k1 x^2)
+  return fmaf(b, fmaf(-t, t, 1.0f), a);
 }
 
 // Byte offset of (row, 16-byte chunk) inside a tile of 128-byte rows laid
