@@ -93,6 +93,8 @@ template <int D>
 __global__ void __launch_bounds__(256) fwd_kernel(const __nv_bfloat16* __restrict__ qkv, long long ldq,
                                                   __nv_bfloat16* __restrict__ out, long long ldo,
                                                   float* __restrict__ lse_out, int H, int S, float scale_log2) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   constexpr int BM = 128, BN = 64, DP = D + 8, NT = D / 8, KS = D / 16;
   extern __shared__ __align__(16) __nv_bfloat16 fsm[];
   __nv_bfloat16* sQ = fsm;
@@ -259,6 +261,8 @@ __global__ void __launch_bounds__(256) fwd_kernel(const __nv_bfloat16* __restric
 template <int D>
 __global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, long long ldo, const __nv_bfloat16* __restrict__ dout,
                              long long lddo, float* __restrict__ delta, int B, int H, int S) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   if constexpr (D == 64 || D == 128) {
     // D/8 lanes per (row, head): each lane one 16-byte vector of O and dO
     // (consecutive lanes, consecutive bytes), then a shuffle reduction.
@@ -324,6 +328,8 @@ __global__ void delta_kernel(const __nv_bfloat16* __restrict__ o, long long ldo,
 template <int D>
 __global__ void dq_convert_kernel(const float* __restrict__ dqacc, long long lda, __nv_bfloat16* __restrict__ dqkv,
                                   long long lddq, int M, int H, float scale) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   if constexpr (D % 8 == 0) {
     // Eight elements per thread: two 16-byte loads, one 16-byte store.
     const long long total = static_cast<long long>(M) * H * (D / 8);
@@ -370,6 +376,8 @@ __global__ void __launch_bounds__(128) bwd_kernel(const __nv_bfloat16* __restric
                                                   float* __restrict__ dqacc, long long ldacc,
                                                   __nv_bfloat16* __restrict__ dqkv, long long lddq, int H, int S,
                                                   float scale, float scale_log2) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   constexpr int BN = 64, BM = 64, DP = D + 8, NT = D / 8, KS = D / 16, SP = BM + 8;
   extern __shared__ __align__(16) __nv_bfloat16 bsm[];
   __nv_bfloat16* sK = bsm;                 // [BN][DP]
@@ -569,8 +577,8 @@ int fwd_launch(const void* qkv, long long ldq, void* out, long long ldo, float* 
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return static_cast<int>(e);
   dim3 grid((S + 127) / 128, B * H);
-  k<<<grid, 256, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(qkv), ldq, reinterpret_cast<__nv_bfloat16*>(out),
-                             ldo, lse, H, S, scale * md::attn::kLog2e);
+  md::launch_pdl(k, dim3(grid), dim3(256), smem, st, reinterpret_cast<const __nv_bfloat16*>(qkv), ldq, reinterpret_cast<__nv_bfloat16*>(out),
+      ldo, lse, H, S, scale * md::attn::kLog2e);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -584,23 +592,23 @@ int bwd_launch(const void* qkv, long long ldq, const void* out, long long ldo, c
   const long long nd = static_cast<long long>(B) * H * S;
   int g1 = static_cast<int>((nd + 255) / 256);
   if (g1 > 148 * 32) g1 = 148 * 32;
-  md::attn::delta_kernel<D><<<g1, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(out), ldo,
-                                                reinterpret_cast<const __nv_bfloat16*>(dout), lddo, delta, B, H, S);
+  md::launch_pdl(md::attn::delta_kernel<D>, dim3(g1), dim3(256), 0, st, reinterpret_cast<const __nv_bfloat16*>(out), ldo,
+      reinterpret_cast<const __nv_bfloat16*>(dout), lddo, delta, B, H, S);
   auto k = md::attn::bwd_kernel<D>;
   const size_t smem = bwd_smem<D>();
   e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return static_cast<int>(e);
   dim3 grid((S + 63) / 64, B * H);
-  k<<<grid, 128, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(qkv), ldq,
-                             reinterpret_cast<const __nv_bfloat16*>(dout), lddo, lse, delta, dqacc,
-                             static_cast<long long>(H) * D, reinterpret_cast<__nv_bfloat16*>(dqkv), lddq, H, S, scale,
-                             scale * md::attn::kLog2e);
+  md::launch_pdl(k, dim3(grid), dim3(128), smem, st, reinterpret_cast<const __nv_bfloat16*>(qkv), ldq,
+      reinterpret_cast<const __nv_bfloat16*>(dout), lddo, lse, delta, dqacc,
+      static_cast<long long>(H) * D, reinterpret_cast<__nv_bfloat16*>(dqkv), lddq, H, S, scale,
+      scale * md::attn::kLog2e);
   const long long nq = rows * H * (D / 2);
   int g2 = static_cast<int>((nq + 255) / 256);
   if (g2 > 148 * 32) g2 = 148 * 32;
-  md::attn::dq_convert_kernel<D><<<g2, 256, 0, st>>>(dqacc, static_cast<long long>(H) * D,
-                                                     reinterpret_cast<__nv_bfloat16*>(dqkv), lddq,
-                                                     static_cast<int>(rows), H, scale);
+  md::launch_pdl(md::attn::dq_convert_kernel<D>, dim3(g2), dim3(256), 0, st, dqacc, static_cast<long long>(H) * D,
+      reinterpret_cast<__nv_bfloat16*>(dqkv), lddq,
+      static_cast<int>(rows), H, scale);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -661,17 +669,17 @@ int md_attn_bwd_tc(const void* qkv, long long ldq, const void* out, long long ld
   if (g1 > 148 * 32) g1 = 148 * 32;
   // out == null: delta was produced upstream (the epilogue of the GEMM that made dout).
   if (out != nullptr)
-    md::attn::delta_kernel<64><<<g1, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(out), ldo,
-                                                   reinterpret_cast<const __nv_bfloat16*>(dout), lddo, delta, B, H, S);
+    md::launch_pdl(md::attn::delta_kernel<64>, dim3(g1), dim3(256), 0, st, reinterpret_cast<const __nv_bfloat16*>(out), ldo,
+        reinterpret_cast<const __nv_bfloat16*>(dout), lddo, delta, B, H, S);
   int rc = md_attn_bwd_tc_main(qkv, ldq, dout, lddo, lse, delta, dqacc, static_cast<long long>(H) * D, dqkv, lddq, B,
                                H, S, D, scale, status, st);
   if (rc != 0) return rc;
   const long long nq = rows * H * (64 / 2);
   int g2 = static_cast<int>((nq + 255) / 256);
   if (g2 > 148 * 32) g2 = 148 * 32;
-  md::attn::dq_convert_kernel<64><<<g2, 256, 0, st>>>(dqacc, static_cast<long long>(H) * 64,
-                                                      reinterpret_cast<__nv_bfloat16*>(dqkv), lddq,
-                                                      static_cast<int>(rows), H, scale);
+  md::launch_pdl(md::attn::dq_convert_kernel<64>, dim3(g2), dim3(256), 0, st, dqacc, static_cast<long long>(H) * 64,
+      reinterpret_cast<__nv_bfloat16*>(dqkv), lddq,
+      static_cast<int>(rows), H, scale);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -166,6 +166,9 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Prologue done: the next kernel may launch; global memory only after the previous one finished.
+  pdl_trigger();
+  pdl_wait();
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -557,6 +560,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Prologue done: the next kernel may launch; global memory only after the previous one finished.
+  pdl_trigger();
+  pdl_wait();
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -1012,7 +1018,7 @@ int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, floa
   if (e != cudaSuccess) return static_cast<int>(e);
   const int slots = g_sms * C::kCtasPerSm;
   const int grid = p.items < slots ? p.items : slots;
-  k<<<grid, md::attn_tc::kThreads, C::kSmemBytes, st>>>(tm, p);
+  md::launch_pdl(k, grid, dim3(md::attn_tc::kThreads), C::kSmemBytes, st, tm, p);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -1057,7 +1063,7 @@ int bwd_tc_launch(const void* qkv, long long ldq, const void* dout, long long ld
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
   const int grid = p.items < g_sms ? p.items : g_sms;
-  k<<<grid, md::attn_tc::kBwdThreads, C::kSmemBytes, st>>>(tq, tdo, tdq, p);
+  md::launch_pdl(k, grid, dim3(md::attn_tc::kBwdThreads), C::kSmemBytes, st, tq, tdo, tdq, p);
   return static_cast<int>(cudaGetLastError());
 }
 

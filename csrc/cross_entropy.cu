@@ -27,6 +27,8 @@ __global__ void stats_kernel(const float* __restrict__ tmax, const float* __rest
                              float* __restrict__ row_max, float* __restrict__ row_sum,
                              const float* __restrict__ tgt_logit, float* __restrict__ lse_out,
                              float* __restrict__ loss_out) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   if (m >= M) return;
   float mx = -INFINITY;
@@ -50,6 +52,8 @@ __global__ void backward_kernel(const __nv_bfloat16* __restrict__ logits, long l
                                 const float* __restrict__ lse, const long long* __restrict__ target,
                                 long long col_offset, const float* __restrict__ grad_out, float scale,
                                 __nv_bfloat16* __restrict__ dlogits, long long ldd, int M, int V) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   const float g = scale * (grad_out != nullptr ? grad_out[0] : 1.f);
   const int nvec = (V + 7) / 8;
   for (int m = blockIdx.x; m < M; m += gridDim.x) {
@@ -103,8 +107,8 @@ extern "C" {
 int md_ce_stats(const float* tmax, const float* tsum, int tiles, int M, float* row_max, float* row_sum,
                 const float* tgt_logit, float* lse_out, float* loss_out, cudaStream_t s) {
   if (M <= 0 || tiles <= 0) return -1;
-  md::ce::stats_kernel<<<(M + 255) / 256, 256, 0, s>>>(tmax, tsum, tiles, M, row_max, row_sum, tgt_logit, lse_out,
-                                                       loss_out);
+  md::launch_pdl(md::ce::stats_kernel, dim3((M + 255) / 256), dim3(256), 0, s, tmax, tsum, tiles, M, row_max, row_sum, tgt_logit, lse_out,
+      loss_out);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -114,9 +118,9 @@ int md_ce_backward(const void* logits, long long ldl, const float* lse, const lo
       (reinterpret_cast<uintptr_t>(dlogits) & 15u))
     return -1;
   int grid = M < 148 * 16 ? M : 148 * 16;
-  md::ce::backward_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(logits), ldl, lse, target,
-                                               col_offset, grad_out, scale, reinterpret_cast<__nv_bfloat16*>(dlogits),
-                                               ldd, M, V);
+  md::launch_pdl(md::ce::backward_kernel, dim3(grid), dim3(256), 0, s, reinterpret_cast<const __nv_bfloat16*>(logits), ldl, lse, target,
+      col_offset, grad_out, scale, reinterpret_cast<__nv_bfloat16*>(dlogits),
+      ldd, M, V);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -20,6 +20,8 @@ __global__ void embed_fwd_kernel(const long long* __restrict__ ids, const __nv_b
                                  long long ldw, const __nv_bfloat16* __restrict__ wpe, long long ldp,
                                  __nv_bfloat16* __restrict__ out, long long ldo, int M, int S, int C,
                                  long long vocab_start, long long vocab_rows, int add_pos) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nvec = C / 8;
@@ -65,6 +67,8 @@ __global__ void embed_fwd_kernel(const long long* __restrict__ ids, const __nv_b
 __global__ void embed_bwd_wte_kernel(const long long* __restrict__ ids, const __nv_bfloat16* __restrict__ dx,
                                      long long ldx, float* __restrict__ dwte, long long ldg, int M, int C,
                                      long long vocab_start, long long vocab_rows) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nvec = C / 8;
@@ -84,6 +88,8 @@ __global__ void embed_bwd_wte_kernel(const long long* __restrict__ ids, const __
 // d_wpe[s, c] (+)= sum_b dx[b*S + s, c]; one thread per (s, pair of columns).
 __global__ void embed_bwd_wpe_kernel(const __nv_bfloat16* __restrict__ dx, long long ldx, float* __restrict__ dwpe,
                                      long long ldg, int B, int S, int C, int accumulate) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   const int pairs = C / 2;
   const long long total = static_cast<long long>(S) * pairs;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -111,6 +117,8 @@ __global__ void embed_bwd_wpe_kernel(const __nv_bfloat16* __restrict__ dx, long 
 // Stage 1 writes one partial row per row-chunk, stage 2 adds them in order.
 __global__ void colsum_partial_kernel(const __nv_bfloat16* __restrict__ x, long long ldx, int M, int N,
                                       int rows_per_chunk, float* __restrict__ partial) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   const int c2 = blockIdx.x * blockDim.x + threadIdx.x;  // column pair
   const int chunk = blockIdx.y;
   if (2 * c2 >= N) return;
@@ -137,6 +145,8 @@ __global__ void colsum_partial_kernel(const __nv_bfloat16* __restrict__ x, long 
 __global__ void __launch_bounds__(256) colsum_partial8_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
                                                               int M, int N, int rows_per_chunk,
                                                               float* __restrict__ partial) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   __shared__ float red[8][256 + 4];
   const int cgp = threadIdx.x & 31, rg = threadIdx.x >> 5;
   const int col = blockIdx.x * 256 + cgp * 8;
@@ -175,6 +185,8 @@ __global__ void __launch_bounds__(256) colsum_partial8_kernel(const __nv_bfloat1
 // deterministic and the pass costs about one memory latency.
 __global__ void __launch_bounds__(1024) colsum_final_kernel(const float* __restrict__ partial, int chunks, int N,
                                                             float* __restrict__ out, int accumulate) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   __shared__ float red[32][33];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int n = blockIdx.x * 32 + lane;
@@ -211,7 +223,7 @@ int md_embed_fwd(const long long* ids, const void* wte, long long ldw, const voi
   const int warps = 8;
   int grid = (M + warps - 1) / warps;
   if (grid > 148 * 16) grid = 148 * 16;
-  md::emb::embed_fwd_kernel<<<grid, warps * 32, 0, s>>>(
+  md::launch_pdl(md::emb::embed_fwd_kernel, dim3(grid), dim3(warps * 32), 0, s,
       ids, reinterpret_cast<const __nv_bfloat16*>(wte), ldw, reinterpret_cast<const __nv_bfloat16*>(wpe), ldp,
       reinterpret_cast<__nv_bfloat16*>(out), ldo, M, S, C, vocab_start, vocab_rows, add_pos);
   return static_cast<int>(cudaGetLastError());
@@ -224,8 +236,8 @@ int md_embed_bwd_wte(const long long* ids, const void* dx, long long ldx, float*
   const int warps = 8;
   int grid = (M + warps - 1) / warps;
   if (grid > 148 * 16) grid = 148 * 16;
-  md::emb::embed_bwd_wte_kernel<<<grid, warps * 32, 0, s>>>(ids, reinterpret_cast<const __nv_bfloat16*>(dx), ldx,
-                                                            dwte, ldg, M, C, vocab_start, vocab_rows);
+  md::launch_pdl(md::emb::embed_bwd_wte_kernel, dim3(grid), dim3(warps * 32), 0, s, ids, reinterpret_cast<const __nv_bfloat16*>(dx), ldx,
+      dwte, ldg, M, C, vocab_start, vocab_rows);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -235,8 +247,8 @@ int md_embed_bwd_wpe(const void* dx, long long ldx, float* dwpe, long long ldg, 
   const long long total = static_cast<long long>(S) * (C / 2);
   int grid = static_cast<int>((total + 255) / 256);
   if (grid > 148 * 16) grid = 148 * 16;
-  md::emb::embed_bwd_wpe_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(dx), ldx, dwpe, ldg, B, S,
-                                                     C, accumulate);
+  md::launch_pdl(md::emb::embed_bwd_wpe_kernel, dim3(grid), dim3(256), 0, s, reinterpret_cast<const __nv_bfloat16*>(dx), ldx, dwpe, ldg, B, S,
+      C, accumulate);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -256,14 +268,14 @@ int md_colsum(const void* x, long long ldx, int M, int N, float* partial, float*
   const int rows_per_chunk = (M + chunks - 1) / chunks;
   if ((N % 8) == 0 && (ldx % 8) == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
     dim3 grid((N + 255) / 256, chunks);
-    md::emb::colsum_partial8_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, N,
-                                                          rows_per_chunk, partial);
+    md::launch_pdl(md::emb::colsum_partial8_kernel, dim3(grid), dim3(256), 0, s, reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, N,
+        rows_per_chunk, partial);
   } else {
     dim3 grid((N / 2 + 1 + 255) / 256, chunks);
-    md::emb::colsum_partial_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, N,
-                                                         rows_per_chunk, partial);
+    md::launch_pdl(md::emb::colsum_partial_kernel, dim3(grid), dim3(256), 0, s, reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, N,
+        rows_per_chunk, partial);
   }
-  md::emb::colsum_final_kernel<<<(N + 31) / 32, 1024, 0, s>>>(partial, chunks, N, out, accumulate);
+  md::launch_pdl(md::emb::colsum_final_kernel, dim3((N + 31) / 32), dim3(1024), 0, s, partial, chunks, N, out, accumulate);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -271,7 +283,7 @@ int md_colsum(const void* x, long long ldx, int M, int N, float* partial, float*
 // into producers, e.g. the GEMM's kEpiDGELU column sums).
 int md_colsum_final(const float* partial, int chunks, int N, float* out, int accumulate, cudaStream_t s) {
   if (chunks <= 0 || N <= 0) return -1;
-  md::emb::colsum_final_kernel<<<(N + 31) / 32, 1024, 0, s>>>(partial, chunks, N, out, accumulate);
+  md::launch_pdl(md::emb::colsum_final_kernel, dim3((N + 31) / 32), dim3(1024), 0, s, partial, chunks, N, out, accumulate);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -45,6 +45,8 @@
 // _VocabParallelCrossEntropy (tensor_parallel.py:451-479).
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+
 #include "md_sm100.cuh"
 
 namespace md {
@@ -158,6 +160,15 @@ struct MdTpArParams {
 };
 
 namespace md {
+
+bool pdl_enabled() {
+  static const int on = [] {
+    const char* e = getenv("MINIDIST_PDL");
+    return (e == nullptr || (e[0] != '0' && e[0] != 'n' && e[0] != 'f')) ? 1 : 0;
+  }();
+  return on != 0;
+}
+
 namespace gemm {
 
 struct KParams {
@@ -419,6 +430,7 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
       tmem_ld_32x32b_x32(t_row + c * 32, r);
       tmem_ld_wait();
       const bool full = (n0 + 32 <= p.N);
+      uint32_t ce_pk[EPI == kEpiCE ? 16 : 1];
       float v[32];
       if (p.alpha != 1.f) {  // warp-uniform
 #pragma unroll
@@ -528,14 +540,25 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
           }
         }
       } else if (EPI == kEpiCE) {
-        // Statistics use the bf16-rounded logits the backward pass reads back.
+        // Statistics use the bf16-rounded logits the backward pass reads back:
+        // pairs are packed once (also the stored values) and unpacked.
         constexpr float kLog2e = 1.4426950408889634f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
-        float cm = -INFINITY;
+        for (int q = 0; q < 16; ++q) ce_pk[q] = pack_bf16x2(v[2 * q], v[2 * q + 1]);
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (n0 + j < p.N) cm = fmaxf(cm, v[j]);
+        for (int q = 0; q < 16; ++q) {
+          v[2 * q] = __uint_as_float(ce_pk[q] << 16);
+          v[2 * q + 1] = __uint_as_float(ce_pk[q] & 0xFFFF0000u);
+        }
+        float cm = -INFINITY;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) cm = fmaxf(cm, v[j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) cm = fmaxf(cm, v[j]);
+        }
         if (cm > ce_m) {
           ce_s = ce_any ? ce_s * ex2_approx((ce_m - cm) * kLog2e) : 0.f;
           ce_m = cm;
@@ -543,9 +566,14 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
         ce_any = true;
         const float mb = ce_m * kLog2e;
         float s = 0.f;
+        if (full) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (n0 + j < p.N) s += ex2_approx(fmaf(v[j], kLog2e, -mb));
+          for (int j = 0; j < 32; ++j) s += ex2_approx(fmaf(v[j], kLog2e, -mb));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) s += ex2_approx(fmaf(v[j], kLog2e, -mb));
+        }
         ce_s += s;
         if (row_ok && tgt >= n0 && tgt < n0 + 32) {
           float tv = 0.f;
@@ -568,13 +596,22 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
       } else {
         const bool two = EPI == kEpiBF16 && p.gelu;  // output + pre-activation slabs (four epilogue warps)
         if ((c & 1) == 0 && !two) sb = slab_acquire(es);
+        if (EPI == kEpiCE) {  // already packed
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
-                           smem_u32(sb + sw128_off(lane, (c & 1) * 4 + q))),
-                       "r"(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1])), "r"(pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3])),
-                       "r"(pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5])), "r"(pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]))
-                       : "memory");
+          for (int q = 0; q < 4; ++q)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                             smem_u32(sb + sw128_off(lane, (c & 1) * 4 + q))),
+                         "r"(ce_pk[4 * q]), "r"(ce_pk[4 * q + 1]), "r"(ce_pk[4 * q + 2]), "r"(ce_pk[4 * q + 3])
+                         : "memory");
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                             smem_u32(sb + sw128_off(lane, (c & 1) * 4 + q))),
+                         "r"(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1])), "r"(pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3])),
+                         "r"(pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5])), "r"(pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]))
+                         : "memory");
+        }
         if ((c & 1) == 1 || n0 + 32 >= p.N) {
           if (EPI == kEpiDGELU && p.colsum != nullptr && row0 < p.M) {  // warp-uniform
             // Bias-gradient first stage from the staged bf16 slab (32 rows x 64
@@ -858,6 +895,12 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
   if constexpr (CG == 2) cluster_sync();  // peer barriers exist before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
+  if constexpr (!AR) {
+    // Prologue done (barriers, TMEM): let the next kernel launch, then wait
+    // for the previous one before touching global memory.
+    pdl_trigger();
+    pdl_wait();
+  }
   unsigned ar_epoch = 0;
   if constexpr (AR) {
     ar_epoch = kp.ar.epoch;
@@ -1233,15 +1276,22 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   cfg.blockDim = dim3(64 + 32 * kEW + (AR ? 128 : 0));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  cfg.attrs = attr;
   cfg.numAttrs = 0;
   if (CG == 2) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+    attr[cfg.numAttrs].val.clusterDim.x = 2;
+    attr[cfg.numAttrs].val.clusterDim.y = 1;
+    attr[cfg.numAttrs].val.clusterDim.z = 1;
+    ++cfg.numAttrs;
+  }
+  // The fused all-reduce variant waits on peers: never launched early next to
+  // its predecessor (it keeps plain stream order).
+  if (!AR && md::pdl_enabled()) {
+    attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+    ++cfg.numAttrs;
   }
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, td, tx, kp);
 }
@@ -1389,6 +1439,9 @@ extern "C" int md_gemm(const MdGemmParams* prm, cudaStream_t stream) {
   }
   return 0;
 }
+
+// 1 when kernels are launched with programmatic dependent launch (MINIDIST_PDL).
+extern "C" int md_pdl_enabled() { return md::pdl_enabled() ? 1 : 0; }
 
 // Width of the column slabs the kEpiCE epilogue keeps statistics for.
 extern "C" int md_gemm_ce_slab() { return md::gemm::kCeSlab; }

@@ -56,6 +56,8 @@ __global__ void __launch_bounds__(kThreads) ln_fwd_kernel(const __nv_bfloat16* _
                                                          __nv_bfloat16* __restrict__ y, long long ldy,
                                                          float* __restrict__ mean_out, float* __restrict__ rstd_out,
                                                          int M, int C, float eps) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   __shared__ float scratch[kThreads / 32];
   const int teams_per_cta = kThreads / T;
   const int team = threadIdx.x / T;
@@ -135,6 +137,8 @@ __global__ void __launch_bounds__(kThreads) ln_bwd_kernel(
     const float* __restrict__ mean_in, const float* __restrict__ rstd_in, const float* __restrict__ gamma,
     const __nv_bfloat16* __restrict__ resid_grad, long long ldr, __nv_bfloat16* __restrict__ dx, long long lddx,
     float* __restrict__ partials, int M, int C) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   extern __shared__ float smem_f[];  // [teams][NACC][C] then scratch
   const int teams_per_cta = kThreads / T;
   const int team = threadIdx.x / T;
@@ -285,6 +289,8 @@ __global__ void __launch_bounds__(kThreads, 2) ln_fwd_pipe_kernel(const __nv_bfl
                                                               __nv_bfloat16* __restrict__ y, long long ldy,
                                                               float* __restrict__ mean_out, float* __restrict__ rstd_out,
                                                               int M, int C, float eps) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   extern __shared__ __align__(16) uint8_t smem_u8[];
   constexpr int kWarps = kThreads / 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -391,6 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1) ln_bwd_pipe_kernel(
     const float* __restrict__ mean_in, const float* __restrict__ rstd_in, const float* __restrict__ gamma,
     const __nv_bfloat16* __restrict__ resid_grad, long long ldr, __nv_bfloat16* __restrict__ dx, long long lddx,
     float* __restrict__ partials, int M, int C) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   extern __shared__ __align__(16) uint8_t smem_u8[];
   constexpr int kWarps = kThreads / 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -564,6 +572,8 @@ __global__ void __launch_bounds__(kThreads, 1) ln_bwd_pipe_kernel(
 __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ partials, int nblocks,
                                                               int nacc, int C, float* d0, float* d1, float* d2,
                                                               float* d3, int accumulate_mask) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   __shared__ float red[8][33];
   const int col = threadIdx.x & 31, grp = threadIdx.x >> 5;
   const int idx = blockIdx.x * 32 + col;
@@ -608,7 +618,7 @@ cudaError_t ln_fwd_launch(const void* x, long long ldx, const float* g, const fl
   int grid = (M + teams - 1) / teams;
   const int cap = sms() * 8;
   if (grid > cap) grid = cap;
-  md::ln::ln_fwd_kernel<T, V><<<grid, md::ln::kThreads, 0, s>>>(
+  md::launch_pdl(md::ln::ln_fwd_kernel<T, V>, dim3(grid), dim3(md::ln::kThreads), 0, s,
       reinterpret_cast<const __nv_bfloat16*>(x), ldx, g, b, reinterpret_cast<__nv_bfloat16*>(y), ldy, mean, rstd, M,
       C, eps);
   return cudaGetLastError();
@@ -623,7 +633,7 @@ cudaError_t ln_bwd_launch(const void* dy, long long lddy, const void* x, long lo
   auto kern = md::ln::ln_bwd_kernel<T, V, NACC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  kern<<<grid, md::ln::kThreads, smem, s>>>(
+  md::launch_pdl(kern, dim3(grid), dim3(md::ln::kThreads), smem, s,
       reinterpret_cast<const __nv_bfloat16*>(dy), lddy, reinterpret_cast<const __nv_bfloat16*>(x), ldx, mean, rstd, g,
       reinterpret_cast<const __nv_bfloat16*>(rg), ldr, reinterpret_cast<__nv_bfloat16*>(dx), lddx, partials, M, C);
   return cudaGetLastError();
@@ -640,8 +650,8 @@ cudaError_t ln_fwd_pipe_launch(const void* x, long long ldx, const float* g, con
   int grid = (M + kWarps - 1) / kWarps;
   const int cap = sms() * 2;  // 2 CTAs (16 warps) per SM: 48 rows in flight per SM
   if (grid > cap) grid = cap;
-  kern<<<grid, md::ln::kThreads, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, g, b,
-                                            reinterpret_cast<__nv_bfloat16*>(y), ldy, mean, rstd, M, C, eps);
+  md::launch_pdl(kern, dim3(grid), dim3(md::ln::kThreads), smem, s, reinterpret_cast<const __nv_bfloat16*>(x), ldx, g, b,
+      reinterpret_cast<__nv_bfloat16*>(y), ldy, mean, rstd, M, C, eps);
   return cudaGetLastError();
 }
 
@@ -656,7 +666,7 @@ cudaError_t ln_bwd_pipe_launch(const void* dy, long long lddy, const void* x, lo
   auto kern = md::ln::ln_bwd_pipe_kernel<V, NACC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  kern<<<grid, md::ln::kThreads, smem, s>>>(
+  md::launch_pdl(kern, dim3(grid), dim3(md::ln::kThreads), smem, s,
       reinterpret_cast<const __nv_bfloat16*>(dy), lddy, reinterpret_cast<const __nv_bfloat16*>(x), ldx, mean, rstd, g,
       reinterpret_cast<const __nv_bfloat16*>(rg), ldr, reinterpret_cast<__nv_bfloat16*>(dx), lddx, partials, M, C);
   return cudaGetLastError();
@@ -755,8 +765,8 @@ int md_ln_bwd(const void* dy, long long lddy, const void* x, long long ldx, cons
 int md_ln_reduce(const float* partials, int nblocks, int nacc, int C, float* d0, float* d1, float* d2, float* d3,
                  int accumulate_mask, cudaStream_t s) {
   const int total = nacc * C;
-  md::ln::reduce_partials_kernel<<<(total + 31) / 32, 256, 0, s>>>(partials, nblocks, nacc, C, d0, d1, d2, d3,
-                                                                     accumulate_mask);
+  md::launch_pdl(md::ln::reduce_partials_kernel, dim3((total + 31) / 32), dim3(256), 0, s, partials, nblocks, nacc, C, d0, d1, d2, d3,
+      accumulate_mask);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -13,6 +13,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace md {
 
 // ---------------------------------------------------------------------------
@@ -42,6 +44,35 @@ __device__ __forceinline__ void report(Status* st, uint32_t code, uint32_t where
     st->detail = detail;
     __threadfence_system();
   }
+}
+
+// Programmatic dependent launch.  A kernel launched with launch_pdl() may
+// start while the previous kernel on its stream is still finishing: its CTAs
+// run their prologue (barrier init, TMEM allocation) on SMs the predecessor
+// has already left, then pdl_wait() blocks until the predecessor has completed
+// and its memory is visible.  Every such kernel calls pdl_wait() before its
+// first global-memory access; pdl_trigger() lets the NEXT kernel launch early.
+// (Both are no-ops for a kernel launched without the attribute.)
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Whether launch_pdl() sets the attribute (environment MINIDIST_PDL=0 turns it off).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {

@@ -37,6 +37,8 @@ __global__ void __launch_bounds__(256) adamw_kernel(const MdAdamEntry* __restric
                                                     const float* __restrict__ inv_scale,
                                                     const float* __restrict__ skip, int mode,
                                                     const float* __restrict__ hp) {
+  pdl_trigger();  // the next kernel may launch now
+  pdl_wait();     // global memory only after the previous kernel completed
   if (mode == 0 && skip != nullptr && *skip != 0.f) return;
   if (hp != nullptr) {
     // Graph-replayable form: learning rate and step count come from device
@@ -130,9 +132,9 @@ int md_adamw(const void* table, const void* chunks, int num_chunks, float lr, fl
              float bc1, float bc2_sqrt, const float* inv_scale, const float* skip, int mode, cudaStream_t s,
              const float* hp) {
   if (num_chunks <= 0) return 0;
-  md::optim::adamw_kernel<<<num_chunks, 256, 0, s>>>(reinterpret_cast<const MdAdamEntry*>(table),
-                                                     reinterpret_cast<const int2*>(chunks), lr, b1, b2, eps, wd, bc1,
-                                                     bc2_sqrt, inv_scale, skip, mode, hp);
+  md::launch_pdl(md::optim::adamw_kernel, dim3(num_chunks), dim3(256), 0, s, reinterpret_cast<const MdAdamEntry*>(table),
+      reinterpret_cast<const int2*>(chunks), lr, b1, b2, eps, wd, bc1,
+      bc2_sqrt, inv_scale, skip, mode, hp);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -53,7 +53,11 @@ def test_graphed_step_matches_eager():
     # Same trajectory: the replayed optimizer advances its step and follows the lr change.
     for a, b in zip(eager, graphed, strict=True):
         assert abs(a - b) <= 2e-3 * abs(a), (eager, graphed)
-    assert ((w_e - w_g).abs().max() / w_e.abs().max()).item() < 2e-2
+    # AdamW turns atomic-order noise in tiny gradients into lr-sized steps, so bound the
+    # element-wise difference by the steps' total learning rate, and the typical one tightly.
+    total_lr = 2 * 1e-3 + 3 * 1e-3 + 3 * 3e-4
+    assert (w_e - w_g).abs().max().item() <= 2 * total_lr
+    assert ((w_e - w_g).abs().mean() / w_e.abs().mean()).item() < 2e-2
     assert sd_step == 2 + 6, sd_step  # 2 eager warm-up steps + 6 replays, synced from the device
     assert graphed[-1] < graphed[0]
 
