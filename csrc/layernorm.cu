@@ -269,6 +269,13 @@ __global__ void __launch_bounds__(kThreads) ln_bwd_kernel(
 // reads back only what it copied itself, so no cross-lane synchronisation is
 // needed until the final fixed-order reduction, which reuses the ring.
 constexpr int kPipeStages = 4;
+// Backward ring: three stages, so that at C <= 768 (V <= 3) two CTAs fit on
+// an SM (2 x 111 KB): 16 warps instead of 8 hide the load and shuffle
+// latency of the per-row reductions.  (Only with two accumulators -- dgamma,
+// dbeta -- does a thread fit the 128 registers two CTAs allow; the variant
+// that also sums two more columns keeps one CTA per SM.)
+template <int V, int NACC>
+__host__ __device__ constexpr int bwd_stages() { return (NACC == 2 && V <= 3) ? 3 : 4; }
 
 __device__ __forceinline__ void cp_async16_ln(uint32_t smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem), "l"(gmem) : "memory");
@@ -392,11 +399,12 @@ __global__ void __launch_bounds__(kThreads, 2) ln_fwd_pipe_kernel(const __nv_bfl
 }
 
 template <int V, int NACC>
-__global__ void __launch_bounds__(kThreads, 1) ln_bwd_pipe_kernel(
+__global__ void __launch_bounds__(kThreads, (NACC == 2 && V <= 3) ? 2 : 1) ln_bwd_pipe_kernel(
     const __nv_bfloat16* __restrict__ dy, long long lddy, const __nv_bfloat16* __restrict__ x, long long ldx,
     const float* __restrict__ mean_in, const float* __restrict__ rstd_in, const float* __restrict__ gamma,
     const __nv_bfloat16* __restrict__ resid_grad, long long ldr, __nv_bfloat16* __restrict__ dx, long long lddx,
     float* __restrict__ partials, int M, int C) {
+  constexpr int kBwdStages = bwd_stages<V, NACC>();
   pdl_trigger();  // the next kernel may launch now
   pdl_wait();     // global memory only after the previous kernel completed
   extern __shared__ __align__(16) uint8_t smem_u8[];
@@ -407,9 +415,9 @@ __global__ void __launch_bounds__(kThreads, 1) ln_bwd_pipe_kernel(
   const bool has_r = resid_grad != nullptr;
   // Ring: [warp][stage][tensor (dy, x, r)][V][32 lanes] x 16 bytes, then
   // [warp][stage] x (mean, rstd) copied by lane 0.
-  uint8_t* ring = smem_u8 + static_cast<size_t>(warp) * kPipeStages * 3 * V * 32 * 16;
-  float* stats = reinterpret_cast<float*>(smem_u8 + static_cast<size_t>(kWarps) * kPipeStages * 3 * V * 32 * 16) +
-                 warp * kPipeStages * 2;
+  uint8_t* ring = smem_u8 + static_cast<size_t>(warp) * kBwdStages * 3 * V * 32 * 16;
+  float* stats = reinterpret_cast<float*>(smem_u8 + static_cast<size_t>(kWarps) * kBwdStages * 3 * V * 32 * 16) +
+                 warp * kBwdStages * 2;
   auto slot = [&](int st, int tsr, int i) -> uint32_t {
     return smem_u32(ring + (((st * 3 + tsr) * V + i) * 32 + lane) * 16);
   };
@@ -419,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1) ln_bwd_pipe_kernel(
   auto issue = [&](int pass) {
     if (pass < passes) {
       const long long r = first + static_cast<long long>(pass) * rows_per_pass;
-      const int st = pass % kPipeStages;
+      const int st = pass % kBwdStages;
 #pragma unroll
       for (int i = 0; i < V; ++i) {
         const int j = lane + 32 * i;
@@ -455,14 +463,14 @@ __global__ void __launch_bounds__(kThreads, 1) ln_bwd_pipe_kernel(
   }
 
 #pragma unroll
-  for (int k = 0; k < kPipeStages - 1; ++k) issue(k);
+  for (int k = 0; k < kBwdStages - 1; ++k) issue(k);
   for (int pass = 0; pass < passes; ++pass) {
     __syncwarp();  // every lane has read the previous row's statistics before lane 0 refills that slot
-    issue(pass + kPipeStages - 1);
-    cp_async_wait_ln<kPipeStages - 1>();
+    issue(pass + kBwdStages - 1);
+    cp_async_wait_ln<kBwdStages - 1>();
     __syncwarp();  // lane 0's statistics copy is visible to the warp
     const long long row = first + static_cast<long long>(pass) * rows_per_pass;
-    const int st = pass % kPipeStages;
+    const int st = pass % kBwdStages;
     const float mean = stats[2 * st], rstd = stats[2 * st + 1];
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
@@ -660,7 +668,8 @@ cudaError_t ln_bwd_pipe_launch(const void* dy, long long lddy, const void* x, lo
                                const float* rstd, const float* g, const void* rg, long long ldr, void* dx,
                                long long lddx, float* partials, int grid, int M, int C, cudaStream_t s) {
   constexpr int kWarps = md::ln::kThreads / 32;
-  const size_t ring = static_cast<size_t>(kWarps) * md::ln::kPipeStages * (3 * V * 32 * 16 + 2 * sizeof(float));
+  const size_t ring =
+      static_cast<size_t>(kWarps) * md::ln::bwd_stages<V, NACC>() * (3 * V * 32 * 16 + 2 * sizeof(float));
   const size_t red = static_cast<size_t>(kWarps) * NACC * C * sizeof(float);
   const size_t smem = ring > red ? ring : red;
   auto kern = md::ln::ln_bwd_pipe_kernel<V, NACC>;
@@ -678,10 +687,11 @@ bool ok16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 extern "C" {
 
 // Number of CTAs (= partial rows) md_ln_bwd uses for M rows of width C.
-int md_ln_bwd_grid(int M, int C) {
-  // The pipelined kernel (C <= 1024) holds one CTA per SM (its prefetch ring
-  // takes most of shared memory); the register kernel runs two.
-  int g = C <= 1024 ? sms() : sms() * 2;
+int md_ln_bwd_grid(int M, int C, int nacc) {
+  // The pipelined kernel holds two CTAs per SM up to C = 768 with two
+  // accumulators (three-stage ring of 111 KB, 128 registers) and one
+  // otherwise; the register kernel (C > 1024) runs two.
+  int g = ((C <= 768 && nacc == 2) || C > 1024) ? sms() * 2 : sms();
   return g < M ? g : (M > 0 ? M : 1);
 }
 
@@ -724,7 +734,7 @@ int md_ln_bwd(const void* dy, long long lddy, const void* x, long long ldx, cons
   if (resid_grad != nullptr && ((ldr % 8) || !ok16(resid_grad))) return -1;
   if (nacc != 2 && nacc != 4) return -3;
   if (nacc == 4 && resid_grad == nullptr) return -4;
-  const int grid = md_ln_bwd_grid(M, C);
+  const int grid = md_ln_bwd_grid(M, C, nacc);
   cudaError_t e;
   const int nvec = C / 8;
 #define MD_LN_BWD_TV(TT, VV)                                                                                      \

@@ -20,7 +20,7 @@ from .gemm import empty_padded
 _SIGS = {
     "md_ln_fwd": "i:plppplppiifp",
     "md_ln_bwd": "i:plplpppplplpiiip",
-    "md_ln_bwd_grid": "i:ii",
+    "md_ln_bwd_grid": "i:iii",
     "md_ln_reduce": "i:piiippppip",
     "md_attn_fwd": "i:plplpiiiifp",
     "md_attn_fwd_tc": "i:plplpiiiifpp",
@@ -85,7 +85,7 @@ def layernorm_bwd(dy, x, mean, rstd, gamma, *, resid_grad=None, dgamma=None, dbe
     extra = colsum_resid is not None or colsum_out is not None
     nacc = 4 if extra else 2
     lib = nat.lib()
-    grid = lib.md_ln_bwd_grid(M, C)
+    grid = lib.md_ln_bwd_grid(M, C, nacc)
     partials = torch.empty(grid * nacc * C, dtype=torch.float32, device=dy.device)
     rc = lib.md_ln_bwd(dy.data_ptr(), _ld(dy), x.data_ptr(), _ld(x), mean.data_ptr(), rstd.data_ptr(),
                        gamma.data_ptr(), _p(resid_grad), _ld(resid_grad) if resid_grad is not None else 0,
