@@ -104,6 +104,29 @@ struct MdAgParams {
   int out_bf16;
 };
 
+// Vocab-parallel cross-entropy statistics (md_ce_tp): each rank folds its
+// [tiles, M] per-128-column (max, sum of exp) into per-row (max, sum) and
+// publishes them with its target logit (0 where the target column belongs to
+// another rank) at [0, M), [M, 2M), [2M, 3M) of its symmetric buffer; after
+// the arrive barrier every rank combines all ranks' triples for its rows:
+// lse = max + log(sum_r s_r exp(m_r - max)), loss = lse - sum_r t_r.  The
+// reference's all_reduce(MAX) + two all_reduce(SUM) of [N]-sized tensors
+// (tensor_parallel.py:457-474) as one kernel.
+struct MdCeTpParams {
+  float* bufs[md::symm::kMaxWorld];  // every rank's symmetric buffer, >= 3 * M floats
+  uint32_t* flags[md::symm::kMaxWorld];
+  int world, rank, channel;
+  unsigned long long timeout_ns;
+  md::Status* status;
+  const float* tmax;  // this rank's [tiles, M] slab maxima
+  const float* tsum;  // this rank's [tiles, M] slab sums of exp(x - max)
+  int tiles;
+  const float* ttgt;  // this rank's [M] target logits
+  int M;
+  float* lse;   // [M] out
+  float* loss;  // [M] out (lse - target logit)
+};
+
 namespace md {
 namespace symm {
 
@@ -370,10 +393,68 @@ __global__ void __launch_bounds__(512) md_ag_shards_kernel(const __grid_constant
   vcta_release(p, vct.epoch);
 }
 
+__global__ void __launch_bounds__(256) md_ce_tp_kernel(const __grid_constant__ MdCeTpParams p) {
+  constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
+  const VCta vct = vcta_claim(p);
+  const int vc = vct.v;
+  const uint32_t arrive = 2u * vct.epoch + 1u, depart = 2u * vct.epoch + 2u;
+  if (vc >= 0) {
+    const int per = (p.M + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+    const int lo = vc * per, hi = min(p.M, lo + per);
+    float* mine = p.bufs[p.rank];
+    for (int m = lo + threadIdx.x; m < hi; m += blockDim.x) {
+      float mx = -INFINITY;
+      for (int t = 0; t < p.tiles; ++t) mx = fmaxf(mx, p.tmax[static_cast<long long>(t) * p.M + m]);
+      float s = 0.f;
+      for (int t = 0; t < p.tiles; ++t) {
+        const float tm = p.tmax[static_cast<long long>(t) * p.M + m];
+        if (tm != -INFINITY) s += p.tsum[static_cast<long long>(t) * p.M + m] * exp2f((tm - mx) * kLog2e);
+      }
+      mine[m] = mx;
+      mine[p.M + m] = s;
+      mine[2 * p.M + m] = p.ttgt[m];
+    }
+    if (cta_barrier(p, vc, arrive, 130)) {
+      for (int m = lo + threadIdx.x; m < hi; m += blockDim.x) {
+        float mr[kMaxWorld], sr[kMaxWorld], tr = 0.f;
+        float gmax = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kMaxWorld; ++r)
+          if (r < p.world) {
+            mr[r] = __ldcg(p.bufs[r] + m);
+            sr[r] = __ldcg(p.bufs[r] + p.M + m);
+            tr += __ldcg(p.bufs[r] + 2 * p.M + m);
+            gmax = fmaxf(gmax, mr[r]);
+          }
+        float sum = 0.f;
+#pragma unroll
+        for (int r = 0; r < kMaxWorld; ++r)
+          if (r < p.world && mr[r] != -INFINITY) sum += sr[r] * exp2f((mr[r] - gmax) * kLog2e);
+        const float l = gmax + log2f(sum) * kLn2;
+        p.lse[m] = l;
+        p.loss[m] = l - tr;
+      }
+      // No rank rewrites its triples (next call) before every peer has read them.
+      cta_barrier(p, vc, depart, 131);
+    }
+  }
+  vcta_release(p, vct.epoch);
+}
+
 }  // namespace symm
 }  // namespace md
 
 extern "C" {
+
+// Launch md_ce_tp_kernel with `ctas` CTAs (<= 160).
+int md_ce_tp(const MdCeTpParams* prm, int ctas, cudaStream_t s) {
+  if (prm == nullptr || prm->world < 1 || prm->world > md::symm::kMaxWorld || prm->M <= 0 || prm->tiles <= 0 ||
+      prm->lse == nullptr || prm->loss == nullptr)
+    return -1;
+  if (ctas < 1 || ctas > md::symm::kMaxCtas || prm->channel < 0 || prm->channel >= md::symm::kChannels) return -2;
+  md::symm::md_ce_tp_kernel<<<ctas, 256, 0, s>>>(*prm);
+  return static_cast<int>(cudaGetLastError());
+}
 
 // Launch md_ag_shards_kernel with `ctas` CTAs (<= 160).
 int md_ag_shards(const MdAgParams* prm, int ctas, cudaStream_t s) {

@@ -338,7 +338,16 @@ def block_forward(blk, x):
 
 
 def _ce_stats_tp(tmax, tsum, tgt, group):
-    """Per-row (max, sumexp, target logit) combined over the TP group -> (lse, loss_rows)."""
+    """Per-row (max, sumexp, target logit) combined over the TP group -> (lse, loss_rows).
+
+    One peer-memory kernel (md_ce_tp) on a single node; otherwise an all_reduce(MAX) and a
+    packed all_reduce(SUM) over NCCL (tensor_parallel.py:457-474)."""
+    from ..parallel import collectives
+
+    if _tp_world(group) > 1:
+        fused = collectives.ce_tp_stats(tmax, tsum, tgt, group)
+        if fused is not None:
+            return fused
     rmax, rsum, _, _ = K.ce_stats(tmax, tsum, finish=False)
     if _tp_world(group) > 1:
         gmax = rmax.clone()

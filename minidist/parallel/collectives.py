@@ -396,3 +396,61 @@ def all_gather_shards(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offse
     nat.check(rc, "md_ag_shards")
     n = shard * comm_.world * out.element_size()
     comm.comm_stats.add("all_gather", n, int((comm_.world - 1) / comm_.world * n))
+
+
+# ---------------------------------------------------------------------------
+# Vocab-parallel cross-entropy statistics over peer memory
+# ---------------------------------------------------------------------------
+_CE_CHANNEL = 6
+
+
+class CeTpParams(ctypes.Structure):
+    """Mirror of ``struct MdCeTpParams`` (csrc/symm.cu)."""
+
+    _fields_ = [
+        ("bufs", ctypes.c_void_p * _MAXW),
+        ("flags", ctypes.c_void_p * _MAXW),
+        ("world", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("channel", ctypes.c_int),
+        ("timeout_ns", ctypes.c_ulonglong),
+        ("status", ctypes.c_void_p),
+        ("tmax", ctypes.c_void_p),
+        ("tsum", ctypes.c_void_p),
+        ("tiles", ctypes.c_int),
+        ("ttgt", ctypes.c_void_p),
+        ("M", ctypes.c_int),
+        ("lse", ctypes.c_void_p),
+        ("loss", ctypes.c_void_p),
+    ]
+
+
+nat.declare("md_ce_tp", "i:pip")
+
+
+def ce_tp_stats(tmax: torch.Tensor, tsum: torch.Tensor, ttgt: torch.Tensor, group):
+    """``(lse, loss_rows)`` of a vocab-parallel cross-entropy from this rank's per-slab statistics
+    (``tmax``/``tsum`` ``[tiles, M]``, target logit ``ttgt`` ``[M]``) in one peer-memory kernel,
+    or ``None`` when peer memory is unavailable for ``group`` (the caller uses NCCL)."""
+    if not _tp_fused_enabled():
+        return None
+    c = _group_comm(group)
+    if c is None:
+        return None
+    tiles, M = tmax.shape
+    buf = c.buffer("tp_ce", 3 * M * 4)
+    lse = torch.empty(M, dtype=torch.float32, device=tmax.device)
+    loss = torch.empty_like(lse)
+    prm = CeTpParams()
+    for r in range(c.world):
+        prm.bufs[r], prm.flags[r] = buf.ptrs[r], buf.flag_ptrs[r]
+    prm.world, prm.rank, prm.channel = c.world, c.rank, _CE_CHANNEL
+    prm.timeout_ns, prm.status = _timeout_ns(), nat.status_ptr(tmax.device)
+    prm.tmax, prm.tsum, prm.tiles = tmax.data_ptr(), tsum.data_ptr(), tiles
+    prm.ttgt, prm.M = ttgt.data_ptr(), M
+    prm.lse, prm.loss = lse.data_ptr(), loss.data_ptr()
+    ctas = min(64, max(1, -(-M // 256)))
+    nat.check(nat.lib().md_ce_tp(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr(None))), "md_ce_tp")
+    n = 3 * M * 4
+    comm.comm_stats.add("all_gather", n * c.world, int((c.world - 1) * n))
+    return lse, loss

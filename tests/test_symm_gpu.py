@@ -96,3 +96,30 @@ def test_bucket_allreduce_world1_scale():
     nat.check_status()
     torch.testing.assert_close(buf, want, rtol=0, atol=0)
     assert _counters(flags, 0) == [0, 0, 1]
+
+
+def test_ce_tp_stats_world1():
+    """md_ce_tp as a group of one equals the single-GPU statistics kernel (lse and per-row loss)."""
+    from minidist.ops import _native as nat
+    from minidist.ops import kernels as K
+    from minidist.parallel import collectives as C
+
+    tiles, M = 7, 3000
+    tmax = torch.randn(tiles, M, device="cuda") * 3
+    tmax[2, :100] = float("-inf")  # empty slabs are skipped
+    tsum = torch.rand(tiles, M, device="cuda") * 50 + 1
+    ttgt = torch.randn(M, device="cuda")
+    buf = torch.zeros(3 * M, device="cuda")
+    flags = _flags()
+    lse, loss = torch.empty(M, device="cuda"), torch.empty(M, device="cuda")
+    p = C.CeTpParams()
+    p.bufs[0], p.flags[0] = buf.data_ptr(), flags.data_ptr()
+    p.world, p.rank, p.channel, p.timeout_ns, p.status = 1, 0, 6, 10**10, nat.status_ptr()
+    p.tmax, p.tsum, p.tiles, p.ttgt, p.M = tmax.data_ptr(), tsum.data_ptr(), tiles, ttgt.data_ptr(), M
+    p.lse, p.loss = lse.data_ptr(), loss.data_ptr()
+    nat.check(nat.lib().md_ce_tp(ctypes.byref(p), 12, ctypes.c_void_p(nat.stream_ptr())), "md_ce_tp")
+    nat.check_status()
+    _, _, want_lse, want_loss = K.ce_stats(tmax, tsum, ttgt, finish=True)
+    torch.testing.assert_close(lse, want_lse, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(loss, want_loss, rtol=1e-5, atol=1e-5)
+    assert _counters(flags, 6) == [0, 0, 1]
