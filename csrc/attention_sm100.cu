@@ -78,6 +78,11 @@ struct FwdParams {
   int items;      // n_qt * B * H
   float scale_log2;
   Status* status;
+  // Real head dimension dr <= D.  dr < D (d = 80 on the D = 128 kernel): the
+  // tensor map is 4-D [B, S, 3H head slots, dr], so the 64-column boxes read
+  // zeros past dr (they add nothing to QK^T or PV) and only dr output columns
+  // are stored.
+  int dr;
 };
 
 __device__ __forceinline__ void decode(const FwdParams& p, int w, int& qt, int& b, int& h) {
@@ -186,9 +191,12 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
       mbar_arrive_expect_tx(&q_full[qb], C::kTileBytes);
       q_armed[qb] = static_cast<int>(qph);
       const int col0 = h * 3 * D;
+      const bool map4 = p.dr != D;  // uniform
 #pragma unroll
-      for (int c = 0; c < C::kChunks; ++c)
-        tma_load_3d(&tm, &q_full[qb], sQ + qb * C::kTileBytes + c * (kBM * 128), col0 + c * 64, qt * kBM, b);
+      for (int c = 0; c < C::kChunks; ++c) {
+        if (map4) tma_load_4d(&tm, &q_full[qb], sQ + qb * C::kTileBytes + c * (kBM * 128), c * 64, 3 * h, qt * kBM, b);
+        else tma_load_3d(&tm, &q_full[qb], sQ + qb * C::kTileBytes + c * (kBM * 128), col0 + c * 64, qt * kBM, b);
+      }
       for (int j = 0; j <= qt; ++j, ++g) {
         const int st = g % KST;
         const uint32_t ph = static_cast<uint32_t>(g / KST) & 1u;
@@ -199,8 +207,10 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
         mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
         k_armed[st] = static_cast<int>(ph);
 #pragma unroll
-        for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(&tm, &k_full[st], sK + st * C::kTileBytes + c * (kBN * 128), col0 + D + c * 64, j * kBN, b);
+        for (int c = 0; c < C::kChunks; ++c) {
+          if (map4) tma_load_4d(&tm, &k_full[st], sK + st * C::kTileBytes + c * (kBN * 128), c * 64, 3 * h + 1, j * kBN, b);
+          else tma_load_3d(&tm, &k_full[st], sK + st * C::kTileBytes + c * (kBN * 128), col0 + D + c * 64, j * kBN, b);
+        }
         if (!mbar_wait(&v_empty[st], ph ^ 1u, p.status, 42, abort_flag)) {
           ok = false;
           break;
@@ -208,9 +218,11 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
         mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
         v_armed[st] = static_cast<int>(ph);
 #pragma unroll
-        for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(&tm, &v_full[st], sV + st * C::kTileBytes + c * (kBN * 128), col0 + 2 * D + c * 64,
-                      j * kBN, b);
+        for (int c = 0; c < C::kChunks; ++c) {
+          if (map4) tma_load_4d(&tm, &v_full[st], sV + st * C::kTileBytes + c * (kBN * 128), c * 64, 3 * h + 2, j * kBN, b);
+          else tma_load_3d(&tm, &v_full[st], sV + st * C::kTileBytes + c * (kBN * 128), col0 + 2 * D + c * 64,
+                           j * kBN, b);
+        }
       }
     }
     // No bulk copy into shared memory may still be in flight at exit.
@@ -384,15 +396,17 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
       const int q = qt * kBM + row;
       const float inv_l = 1.0f / l;
       uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) +
-                      (static_cast<long long>(b) * p.S + q) * p.ldo * 2 + static_cast<long long>(h) * D * 2;
+                      (static_cast<long long>(b) * p.S + q) * p.ldo * 2 + static_cast<long long>(h) * p.dr * 2;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
+        if (c * 32 >= p.dr) break;  // uniform: the padded columns are not stored
         uint32_t o[32];
         tmem_ld_32x32b_x32(tmem + lane_base + C::kOCol + static_cast<uint32_t>(c * 32), o);
         tmem_ld_wait();
         if (q < p.S) {
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
+            if (c * 32 + k * 8 >= p.dr) break;
             uint4 v;
             v.x = pack_bf16x2(__uint_as_float(o[8 * k + 0]) * inv_l, __uint_as_float(o[8 * k + 1]) * inv_l);
             v.y = pack_bf16x2(__uint_as_float(o[8 * k + 2]) * inv_l, __uint_as_float(o[8 * k + 3]) * inv_l);
@@ -976,6 +990,21 @@ bool make_map_bsc(CUtensorMap* map, const void* ptr, int B, int S, long long col
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [B, S, slots, dr] view of a [B*S, ld] bf16 matrix whose rows hold `slots`
+// consecutive dr-wide head vectors; box {64, 1, 128 rows, 1}, 128B swizzle.
+// Columns dr..63 of the last box read as zero.
+bool make_map_bshd(CUtensorMap* map, const void* ptr, int B, int S, int slots, int dr, long long ld) {
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(dr), static_cast<cuuint64_t>(slots), static_cast<cuuint64_t>(S),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(dr) * 2, static_cast<cuuint64_t>(ld) * 2,
+                           static_cast<cuuint64_t>(ld) * 2 * S};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return g_encode_attn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // [B, S, cols] view of a [B*S, ld] fp32 matrix; box {32 cols, 128 rows, 1}, 128B swizzle.
 bool make_map_f32_bsc(CUtensorMap* map, const void* ptr, int B, int S, long long cols, long long ld) {
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
@@ -992,11 +1021,15 @@ long long* g_trace = nullptr;  // device buffer set by md_attn_trace_enable (ana
 
 template <int D>
 int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, float* lse, int B, int H, int S,
-                  float scale, void* status, cudaStream_t st) {
+                  float scale, void* status, cudaStream_t st, int dr = D) {
   using C = md::attn_tc::FwdCfg<D>;
   if (!get_encoder()) return -3;
   CUtensorMap tm;
-  if (!make_map_bsc(&tm, qkv, B, S, 3LL * H * D, ldq)) return -4;
+  if (dr == D) {
+    if (!make_map_bsc(&tm, qkv, B, S, 3LL * H * D, ldq)) return -4;
+  } else {
+    if (dr % 8 || dr > D || !make_map_bshd(&tm, qkv, B, S, 3 * H, dr, ldq)) return -4;
+  }
   if (g_sms == 0) {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1013,6 +1046,7 @@ int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, floa
   p.items = p.n_qt * B * H;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = reinterpret_cast<md::Status*>(status);
+  p.dr = dr;
   auto k = md::attn_tc::fwd_kernel<D>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
@@ -1112,6 +1146,8 @@ int md_attn_fwd_tc(const void* qkv, long long ldq, void* out, long long ldo, flo
   switch (D) {
     case 64: return fwd_tc_launch<64>(qkv, ldq, out, ldo, lse, B, H, S, scale, status, st);
     case 128: return fwd_tc_launch<128>(qkv, ldq, out, ldo, lse, B, H, S, scale, status, st);
+    // d = 80 (the 2.7B model): the D = 128 kernel on zero-padded boxes.
+    case 80: return fwd_tc_launch<128>(qkv, ldq, out, ldo, lse, B, H, S, scale, status, st, 80);
     default: return -2;
   }
 }

@@ -114,7 +114,7 @@ def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int, D: int, impl: str |
     out = empty_padded(B * S, H * D, device=qkv.device)
     lse = torch.empty(B, H, S, dtype=torch.float32, device=qkv.device)
     impl = impl or _ATTN_FWD
-    if impl == "tc" and D in (64, 128):
+    if impl == "tc" and D in (64, 80, 128):  # d = 80 runs the d = 128 kernel on zero-padded boxes
         rc = nat.lib().md_attn_fwd_tc(qkv.data_ptr(), _ld(qkv), out.data_ptr(), _ld(out), lse.data_ptr(), B, H, S,
                                       D, 1.0 / math.sqrt(D), nat.status_ptr(qkv.device), _s())
         nat.check(rc, f"md_attn_fwd_tc(D={D})")
