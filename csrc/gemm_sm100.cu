@@ -825,11 +825,13 @@ __device__ __forceinline__ int ar_pull_chunk(const MdGemmParams& p, const MdTpAr
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int CG, int EW, bool A_MN, bool B_MN, int EPI, bool AR = false>
-__global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmX,
-                const __grid_constant__ KParams kp) {
+// The kernel body; gemm_kernel (plain GEMM) and md_gemm_ar_kernel (GEMM +
+// tensor-parallel all-reduce: its own name, so profiles attribute it as a
+// collective) are its two entry points.  The tensor maps stay in kernel
+// parameter space (references to the __grid_constant__ parameters).
+template <int CG, int EW, bool A_MN, bool B_MN, int EPI, bool AR>
+__device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmD,
+                                          const CUtensorMap& tmX, const KParams& kp) {
   using C = Cfg<CG, EW>;
   constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -1188,6 +1190,31 @@ __global__ void __launch_bounds__(64 + 32 * EW + (AR ? 128 : 0), 1)
   }
 }
 
+template <int CG, int EW, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmX,
+                const __grid_constant__ KParams kp) {
+  gemm_body<CG, EW, A_MN, B_MN, EPI, false>(tmA, tmB, tmD, tmX, kp);
+}
+
+template <int CG, int EW, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(64 + 32 * EW + 128, 1)
+    md_gemm_ar_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmX,
+                      const __grid_constant__ KParams kp) {
+  gemm_body<CG, EW, A_MN, B_MN, EPI, true>(tmA, tmB, tmD, tmX, kp);
+}
+
+template <int CG, int EW, bool A_MN, bool B_MN, int EPI, bool AR>
+struct KernelFor {
+  static constexpr auto fn = gemm_kernel<CG, EW, A_MN, B_MN, EPI>;
+};
+template <int CG, int EW, bool A_MN, bool B_MN, int EPI>
+struct KernelFor<CG, EW, A_MN, B_MN, EPI, true> {
+  static constexpr auto fn = md_gemm_ar_kernel<CG, EW, A_MN, B_MN, EPI>;
+};
+
 // Fixed-order sum of split-K partials: D (+)= sum_s ws[s].  Deterministic, so
 // replicated gradients stay bit-identical across ranks.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, float* __restrict__ D, long long ldd,
@@ -1257,7 +1284,7 @@ int g_num_sms = 0;
 template <int CG, int kEW, bool A_MN, bool B_MN, int EPI, bool AR = false>
 cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& tx,
                    const md::gemm::KParams& kp, int grid, cudaStream_t stream) {
-  auto kern = md::gemm::gemm_kernel<CG, kEW, A_MN, B_MN, EPI, AR>;
+  auto kern = md::gemm::KernelFor<CG, kEW, A_MN, B_MN, EPI, AR>::fn;
   constexpr int smem = md::gemm::Cfg<CG, kEW>::kSmemBytes;
   static int attr_done[64] = {0};
   int dev = 0;

@@ -23,6 +23,7 @@ and data-parallel replicas different ones; the loss should hover near
 from __future__ import annotations
 
 import argparse
+import json
 import os
 import sys
 import time
@@ -87,7 +88,28 @@ def parse_args(argv=None) -> argparse.Namespace:
                      help="AdamW implementation (fused = multi-tensor sm_100a kernel)")
     run.add_argument("--timing", default="auto", choices=["auto", "device", "host"])
     run.add_argument("--save", metavar="DIR", default=None, help="write a checkpoint here at the end")
+    run.add_argument("--kernels", default="fused", choices=["fused", "nccl"],
+                     help="fused: peer-memory collectives fused into the kernels; nccl: the same model with "
+                          "every collective through NCCL (A/B comparison)")
+    run.add_argument("--metrics-jsonl", metavar="PATH", default=None,
+                     help="append one JSON line per logged step and a summary line (rank 0)")
     return p.parse_args(argv)
+
+
+class _MetricsSink:
+    """JSON-lines metrics (rank 0 only): per logged step, then one summary record."""
+
+    def __init__(self, path: str | None, rank: int):
+        self.f = open(path, "a") if (path and rank == 0) else None
+
+    def write(self, **rec) -> None:
+        if self.f is not None:
+            self.f.write(json.dumps(rec) + "\n")
+            self.f.flush()
+
+    def close(self) -> None:
+        if self.f is not None:
+            self.f.close()
 
 
 def make_batch(config: GPTConfig, batch_size: int, dp_rank: int, step: int, seed: int, device):
@@ -173,7 +195,12 @@ def _max_over_ranks(x: float, device) -> float:
 
 def main(argv=None) -> None:
     args = parse_args(argv)
+    if args.kernels == "nccl":
+        # Read when the communicators, reducers and fused paths are first set up.
+        for var in ("MINIDIST_PEER_MEMORY", "MINIDIST_TP_FUSED", "MINIDIST_FSDP_FUSED"):
+            os.environ[var] = "0"
     rank, world, device = init_distributed(backend=args.backend)
+    metrics = _MetricsSink(args.metrics_jsonl, rank)
     torch.manual_seed(args.seed)
     mesh = ParallelMesh(tp_size=args.tp, pp_size=args.pp)
     config = GPTConfig(vocab_size=args.vocab, block_size=args.seq_len, n_layer=args.layers, n_head=args.heads,
@@ -241,6 +268,8 @@ def main(argv=None) -> None:
             el = time.perf_counter() - start
             print_rank0(f"  step {step:>4}/{args.steps}  loss {loss:>7.4f}  {el / step * 1e3:>7.1f} ms/step  "
                         f"{tokens_per_step * step / el:>9.0f} tok/s")
+            metrics.write(step=step, loss=loss, ms_per_step=el / step * 1e3, tokens_per_s=tokens_per_step * step / el,
+                          timing="host, rank 0")
     if device.type == "cuda":
         torch.cuda.synchronize()
     total = time.perf_counter() - start
@@ -252,6 +281,10 @@ def main(argv=None) -> None:
     kind = "device time, max over ranks" if device_timing else "host time, max over ranks"
     print_rank0(f"\n  {args.steps} steps in {total:.2f}s ({total / args.steps * 1e3:.1f} ms/step, "
                 f"{tokens_per_step * args.steps / total:.0f} tok/s; {kind})")
+    metrics.write(event="summary", steps=args.steps, ms_per_step=total / args.steps * 1e3,
+                  tokens_per_s=tokens_per_step * args.steps / total, timing=kind, kernels=args.kernels,
+                  peak_mem_gib=(torch.cuda.max_memory_allocated() / 1024**3 if device.type == "cuda" else None))
+    metrics.close()
     if device.type == "cuda":
         print_rank0(f"  peak memory: {torch.cuda.max_memory_allocated() / 1024**3:.2f} GiB/rank")
     if scaler.enabled:

@@ -51,6 +51,27 @@ class ArParams(ctypes.Structure):
 nat.declare("md_allreduce", "i:pip")
 
 
+_NVTX = os.environ.get("MINIDIST_NVTX", "0") not in ("0", "", "false", "no")
+
+
+class _Range:
+    """NVTX range named like the fused kernel it brackets (``MINIDIST_NVTX=1``; free otherwise), so
+    timelines attribute peer-memory collectives even where kernel names are not shown."""
+
+    __slots__ = ("name",)
+
+    def __init__(self, name: str):
+        self.name = name
+
+    def __enter__(self):
+        if _NVTX:
+            torch.cuda.nvtx.range_push(self.name)
+
+    def __exit__(self, *exc):
+        if _NVTX:
+            torch.cuda.nvtx.range_pop()
+
+
 def _timeout_ns() -> int:
     return int(float(os.environ.get("MINIDIST_PEER_TIMEOUT_S", "60")) * 1e9)
 
@@ -70,7 +91,8 @@ def allreduce_fp32_(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offset:
     p.timeout_ns = _timeout_ns()
     p.status = nat.status_ptr()
     ctas = lib.md_allreduce_ctas(n, buf.world)
-    nat.check(lib.md_allreduce(ctypes.byref(p), ctas, ctypes.c_void_p(nat.stream_ptr(stream))), "md_allreduce")
+    with _Range("md_ar_bucket"):
+        nat.check(lib.md_allreduce(ctypes.byref(p), ctas, ctypes.c_void_p(nat.stream_ptr(stream))), "md_allreduce")
 
 
 class FusedBucketReducer:
@@ -258,7 +280,8 @@ def gemm_all_reduce(x_local, w_local, bias, resid, group, b_mn: bool = False):
         ar.resid = None
     gp.A, gp.B = x_local.data_ptr(), w_local.data_ptr()
     gp.lda, gp.ldb = x_local.stride(0), w_local.stride(0)
-    rc = _LIB_GEMM_AR(gp_ref, ar_ref, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    with _Range("md_gemm_ar"):
+        rc = _LIB_GEMM_AR(gp_ref, ar_ref, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     if rc != 0:
         nat.check(rc, f"md_gemm_ar(M={M},N={N},K={K})")
     comm.comm_stats.add("all_reduce", M * N * 2, int(2 * (c.world - 1) / c.world * M * N * 2))
@@ -340,7 +363,8 @@ def reduce_scatter_shard(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_of
         prm.grad_out = grad_out.data_ptr()
         prm.accumulate = int(accumulate)
     ctas = min(nat.num_sms(), 160, max(1, shard // (4 * 512 * 8)))
-    rc = nat.lib().md_rs_shard(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr(None)))
+    with _Range("md_rs_shard"):
+        rc = nat.lib().md_rs_shard(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr(None)))
     nat.check(rc, "md_rs_shard")
     n = shard * comm_.world * 4
     comm.comm_stats.add("reduce_scatter", n, int((comm_.world - 1) / comm_.world * n))
@@ -392,7 +416,8 @@ def all_gather_shards(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offse
     prm.out_bf16 = int(out.dtype == torch.bfloat16)
     # One CTA per 64 K output elements, at most 64: the gather overlaps the compute stream.
     ctas = min(64, max(1, shard * comm_.world // 65536))
-    rc = nat.lib().md_ag_shards(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr(None)))
+    with _Range("md_ag_shards"):
+        rc = nat.lib().md_ag_shards(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr(None)))
     nat.check(rc, "md_ag_shards")
     n = shard * comm_.world * out.element_size()
     comm.comm_stats.add("all_gather", n, int((comm_.world - 1) / comm_.world * n))
@@ -450,7 +475,8 @@ def ce_tp_stats(tmax: torch.Tensor, tsum: torch.Tensor, ttgt: torch.Tensor, grou
     prm.ttgt, prm.M = ttgt.data_ptr(), M
     prm.lse, prm.loss = lse.data_ptr(), loss.data_ptr()
     ctas = min(64, max(1, -(-M // 256)))
-    nat.check(nat.lib().md_ce_tp(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr(None))), "md_ce_tp")
+    with _Range("md_ce_tp"):
+        nat.check(nat.lib().md_ce_tp(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr(None))), "md_ce_tp")
     n = 3 * M * 4
     comm.comm_stats.add("all_gather", n * c.world, int((c.world - 1) * n))
     return lse, loss

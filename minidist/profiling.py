@@ -56,6 +56,7 @@ FUSED_PATTERNS: dict[str, str] = {
     "md_ar_": "all_reduce",
     "md_rs_": "reduce_scatter",
     "md_ag_": "all_gather",
+    "md_ce_tp": "all_reduce",  # the vocab-parallel cross-entropy statistics exchange
 }
 
 _KINDS = {

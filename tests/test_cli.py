@@ -48,3 +48,17 @@ def test_benchmark_scripts_smoke():
     out = _torchrun("benchmarks/bench_collectives.py", 2, 29575, "--max-mb", "1", "--iters", "2", "--warmup", "1",
                     "--backend", "gloo")
     assert "all_reduce" in out
+
+
+def test_trainer_metrics_jsonl_and_kernels_flag(tmp_path):
+    import json
+
+    path = tmp_path / "metrics.jsonl"
+    _torchrun("examples/train_gpt.py", 2, 29576, "--strategy", "ddp", "--layers", "2", "--embd", "64", "--heads", "4",
+              "--vocab", "256", "--seq-len", "32", "--batch-size", "4", "--steps", "3", "--backend", "gloo",
+              "--kernels", "nccl", "--metrics-jsonl", str(path))
+    recs = [json.loads(line) for line in path.read_text().splitlines()]
+    steps = [r for r in recs if "step" in r]
+    summary = [r for r in recs if r.get("event") == "summary"]
+    assert steps and all(r["loss"] > 0 and r["tokens_per_s"] > 0 for r in steps)
+    assert len(summary) == 1 and summary[0]["steps"] == 3 and summary[0]["kernels"] == "nccl"
