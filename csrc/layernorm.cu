@@ -577,21 +577,28 @@ __global__ void __launch_bounds__(kThreads, (NACC == 2 && V <= 3) ? 2 : 1) ln_bw
 // out_a[c] (+)= sum_b partials[b][a][c] for each accumulator a with a non-null destination.
 // Block = 32 columns x 8 row groups; each group sums a contiguous range of
 // partial rows, then the 8 group sums are added in a fixed order.
-__global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ partials, int nblocks,
+// 32 columns per CTA, 32 warps: warp w sums a contiguous range of partial rows
+// (loads unrolled, all in flight), then the 32 warp sums are added in order --
+// a fixed summation order, so the result is the same on every rank.
+__global__ void __launch_bounds__(1024) reduce_partials_kernel(const float* __restrict__ partials, int nblocks,
                                                               int nacc, int C, float* d0, float* d1, float* d2,
                                                               float* d3, int accumulate_mask) {
   pdl_trigger();  // the next kernel may launch now
   pdl_wait();     // global memory only after the previous kernel completed
-  __shared__ float red[8][33];
+  __shared__ float red[32][33];
   const int col = threadIdx.x & 31, grp = threadIdx.x >> 5;
   const int idx = blockIdx.x * 32 + col;
   const bool ok = idx < nacc * C;
   const int a = ok ? idx / C : 0, c = ok ? idx - a * C : 0;
-  const int per = (nblocks + 7) / 8;
+  const int per = (nblocks + 31) / 32;
   const int b0 = grp * per, b1 = min(nblocks, b0 + per);
   float s = 0.f;
-  if (ok)
-    for (int b = b0; b < b1; ++b) s += partials[(static_cast<long long>(b) * nacc + a) * C + c];
+  if (ok) {
+    const float* src = partials + static_cast<long long>(a) * C + c;
+    const long long stride = static_cast<long long>(nacc) * C;
+#pragma unroll 4
+    for (int b = b0; b < b1; ++b) s += __ldg(src + b * stride);
+  }
   red[grp][col] = s;
   __syncthreads();
   if (grp == 0 && ok) {
@@ -599,7 +606,7 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __res
     if (dst != nullptr) {
       float t = 0.f;
 #pragma unroll
-      for (int g = 0; g < 8; ++g) t += red[g][col];
+      for (int g = 0; g < 32; ++g) t += red[g][col];
       dst[c] = ((accumulate_mask >> a) & 1) ? dst[c] + t : t;
     }
   }
@@ -775,7 +782,7 @@ int md_ln_bwd(const void* dy, long long lddy, const void* x, long long ldx, cons
 int md_ln_reduce(const float* partials, int nblocks, int nacc, int C, float* d0, float* d1, float* d2, float* d3,
                  int accumulate_mask, cudaStream_t s) {
   const int total = nacc * C;
-  md::launch_pdl(md::ln::reduce_partials_kernel, dim3((total + 31) / 32), dim3(256), 0, s, partials, nblocks, nacc, C, d0, d1, d2, d3,
+  md::launch_pdl(md::ln::reduce_partials_kernel, dim3((total + 31) / 32), dim3(1024), 0, s, partials, nblocks, nacc, C, d0, d1, d2, d3,
       accumulate_mask);
   return static_cast<int>(cudaGetLastError());
 }
