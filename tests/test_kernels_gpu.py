@@ -140,3 +140,27 @@ def test_fused_adamw_matches_torch():
         b.step()
     for p, q in zip(ps, qs):
         assert _rel(p, q) < 1e-5
+
+
+@pytest.mark.parametrize("M,V,col_offset", [(300, 1003, 0), (64, 50257, 0), (129, 517, 1000)])
+def test_ce_backward_matches_fp32(M, V, col_offset):
+    """(softmax - onehot) * g * scale from stored bf16 logits, incl. a ragged vocabulary and a vocab shard."""
+    from minidist.ops import gemm as G
+
+    torch.manual_seed(7)
+    logits = G.empty_padded(M, V, device="cuda")
+    logits.copy_(torch.randn(M, V, device="cuda") * 3)
+    lf = logits.float()
+    lse = torch.logsumexp(lf, dim=1)
+    # Targets inside and outside this shard's columns [col_offset, col_offset + V).
+    target = torch.randint(0, V, (M,), device="cuda") + col_offset
+    target[::5] = col_offset + V + 3 if col_offset else target[::5]
+    g = torch.tensor([0.75], device="cuda")
+    out = K.ce_backward(logits, lse, target, g, 1.0 / M, V, col_offset=col_offset)
+    nat.check_status()
+    want = torch.softmax(lf, dim=1)
+    local = target - col_offset
+    inside = (local >= 0) & (local < V)
+    want[inside.nonzero().squeeze(1), local[inside]] -= 1.0
+    want *= 0.75 / M
+    assert _rel(out, want) < 1e-2
