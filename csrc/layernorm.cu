@@ -288,12 +288,9 @@ __device__ __forceinline__ void cp_async_wait_ln() {
 
 // Forward for rows of up to 1024 columns with the same per-lane cp.async ring
 // (kPipeStages - 1 rows in flight per warp): mean and variance in two passes
-// over registers.  gamma and beta are read through L1 when each output vector
-// is formed (every row reads the same 6 KB) instead of being held in 48
-// registers, so that four CTAs (32 warps) fit on an SM: at GPT-2 size a warp
-// has only ~4 rows, and the extra warps hide the first rows' latency.
+// over registers, gamma and beta held in registers for the whole kernel.
 template <int V>
-__global__ void __launch_bounds__(kThreads, 4) ln_fwd_pipe_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+__global__ void __launch_bounds__(kThreads, 2) ln_fwd_pipe_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
                                                               const float* __restrict__ gamma,
                                                               const float* __restrict__ beta,
                                                               __nv_bfloat16* __restrict__ y, long long ldy,
@@ -322,6 +319,16 @@ __global__ void __launch_bounds__(kThreads, 4) ln_fwd_pipe_kernel(const __nv_bfl
     }
     cp_async_commit_ln();
   };
+  float gam[V][8], bet[V][8];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int j = lane + 32 * i;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      gam[i][e] = j < nvec ? gamma[8 * j + e] : 0.f;
+      bet[i][e] = j < nvec ? beta[8 * j + e] : 0.f;
+    }
+  }
 #pragma unroll
   for (int k = 0; k < kPipeStages - 1; ++k) issue(k);
   for (int pass = 0; pass < passes; ++pass) {
@@ -372,15 +379,9 @@ __global__ void __launch_bounds__(kThreads, 4) ln_fwd_pipe_kernel(const __nv_bfl
     for (int i = 0; i < V; ++i) {
       const int j = lane + 32 * i;
       if (j < nvec) {
-        const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma) + 2 * j);
-        const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma) + 2 * j + 1);
-        const float4 b0 = __ldg(reinterpret_cast<const float4*>(beta) + 2 * j);
-        const float4 b1 = __ldg(reinterpret_cast<const float4*>(beta) + 2 * j + 1);
-        const float gm[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-        const float bt[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
         float o[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = (v[i][e] - mean) * rstd * gm[e] + bt[e];
+        for (int e = 0; e < 8; ++e) o[e] = (v[i][e] - mean) * rstd * gam[i][e] + bet[i][e];
         uint4 w;
         w.x = pack_bf16x2(o[0], o[1]);
         w.y = pack_bf16x2(o[2], o[3]);
@@ -662,9 +663,7 @@ cudaError_t ln_fwd_pipe_launch(const void* x, long long ldx, const float* g, con
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   int grid = (M + kWarps - 1) / kWarps;
-  // CTAs per SM: four (32 warps, 96 rows in flight) while the ring fits (V <= 3:
-  // 4 x 48 KB), three at V = 4 (64 KB each).
-  const int cap = sms() * (V <= 3 ? 4 : 3);
+  const int cap = sms() * 2;  // 2 CTAs (16 warps) per SM: 48 rows in flight per SM
   if (grid > cap) grid = cap;
   md::launch_pdl(kern, dim3(grid), dim3(md::ln::kThreads), smem, s, reinterpret_cast<const __nv_bfloat16*>(x), ldx, g, b,
       reinterpret_cast<__nv_bfloat16*>(y), ldy, mean, rstd, M, C, eps);
