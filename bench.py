@@ -1,27 +1,43 @@
 #!/usr/bin/env python3
-"""Headline benchmark: GPT-2 small DDP training throughput (tokens/s for the whole job).
+"""Headline benchmark: GPT training throughput (tokens/s for the whole job), both frameworks.
 
-Config (the reference's DDP config): 12 layers, d_model 768, 12 heads, MLP
-3072, vocab 50257, seq 1024, micro-batch 16 sequences per GPU, bf16 compute,
-AdamW (lr 3e-4), 25 MB gradient buckets overlapped with backward, synthetic
-uniform-random tokens from a seed, random-init weights.  Weak scaling: every
-GPU runs the same per-GPU batch, data parallel over N GPUs.
+Configurations (BASELINE.json's five; ``--config``, default ``gpt2s-ddp``):
 
-    python bench.py                               # 1 GPU, our framework
-    python bench.py --impl reference              # the unmodified reference (baseline/_ref)
-    torchrun --nproc-per-node 8 bench.py --gpus 8 # one rank per GPU
+  gpt2s-ddp     GPT-2 small 12L/768d/12h, vocab 50257, seq 1024, 16 seqs/GPU, DDP with 25 MB
+                buckets overlapped with backward (weak scaling: dp = N)
+  gpt1.5b-fsdp  GPT 1.5B 48L/1600d/25h, vocab 50257, seq 1024, 8 seqs/GPU, ZeRO-3 with bf16
+                parameter gathers, fp32 master weights and fp32 gradient reduce-scatter, one
+                unit per block (weak scaling: dp = N; N = 1 trains the unwrapped model)
+  gpt2.7b-3d    GPT 2.7B 32L/2560d/32h, vocab 50304, seq 2048, tp2 x pp2 x dp(N/4), 1F1B with
+                8 microbatches (``--schedule gpipe`` for the secondary run), 32 seqs per
+                data-parallel replica (global batch 64 at N = 8)
+  gpt6.7b-tp8   GPT 6.7B 32L/4096d/32h, vocab 50304, seq 2048, 4 seqs, tensor parallel over
+                all N GPUs (strong scaling; the named config is N = 8)
+
+Every configuration runs bf16 autocast compute, AdamW (lr 3e-4), synthetic
+uniform-random tokens seeded by ``seed + step*10000 + dp_rank`` and random-init
+weights of the named architecture.
+
+    python bench.py                                      # 1 GPU, our framework, gpt2s-ddp
+    python bench.py --impl reference                     # the unmodified reference (baseline/_ref)
+    torchrun --nproc-per-node 8 bench.py --gpus 8 --config gpt6.7b-tp8
+
+Arms.  ``--impl ours`` builds the model through this repository's public API
+(GPT on the fused sm_100a path, DistributedDataParallel / FullyShardedDataParallel /
+PipelineStage + build_schedule, FusedAdamW).  ``--impl reference`` builds the same
+configuration through the reference package's own public API and stock code path
+(its GPT, DDP, FSDP, pipeline schedules and vocab-parallel cross-entropy, torch
+AdamW, bf16 autocast -- what its examples/train_gpt.py:120-218 does), imported
+from ``baseline/_ref``.
 
 Timing: W warm-up steps, then exactly K steps bracketed by a barrier and
 torch.cuda.synchronize() on both sides, timed with CUDA events on the compute
-stream; the reported step time is the maximum over ranks.  Every step's
-working set (about 6 GB of activations plus 0.6 GB of fp32 weights) is far
-larger than the 126 MB L2, so no explicit flush is needed.  SM clocks and
-throttle reasons are sampled with nvidia-smi during the timed region.
-
-Our arm runs the step as one CUDA graph (minidist.GraphedStep: forward,
-backward, gradient all-reduce and FusedAdamW(capturable=True) captured once,
-replayed per step, the step's token batch copied into the graph's input
-buffers first); ``--no-graph`` runs the same step eagerly.
+stream; the reported step time is the maximum over ranks.  Every step's working
+set (activations of several GB plus the weights) is far larger than the 126 MB
+L2, so no explicit flush is needed.  SM clocks and throttle reasons are sampled
+with nvidia-smi during the timed region.  Our arm replays data-parallel and
+tensor-parallel steps as one CUDA graph (minidist.GraphedStep; ``--no-graph``
+runs eagerly); FSDP and pipeline steps run eagerly.
 
 The ``e2e`` block repeats the K steps through the same public API with the
 inputs copied from pinned host memory each step and the loss read back to the
@@ -42,20 +58,57 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 REF_PATH = os.path.join(ROOT, "baseline", "_ref")
 
-MODEL = dict(vocab=50257, layers=12, heads=12, embd=768, seq=1024, batch=16)
 METRIC = "GPT train tokens/s/box at 1/2/4/8 B200 (DDP,FSDP,TP×PP×DP), max over ranks"
 
+# name -> model shape, per-replica batch and parallel layout.
+CONFIGS = {
+    "gpt2s-ddp": dict(model="gpt2-small 12L/768d/12h, vocab 50257 (untied head)",
+                      vocab=50257, layers=12, heads=12, embd=768, seq=1024, batch=16,
+                      strategy="ddp", tp=1, pp=1, scaling="weak"),
+    "gpt1.5b-fsdp": dict(model="gpt 1.5B 48L/1600d/25h, vocab 50257", vocab=50257, layers=48, heads=25,
+                         embd=1600, seq=1024, batch=8, strategy="fsdp", tp=1, pp=1, scaling="weak"),
+    "gpt2.7b-3d": dict(model="gpt 2.7B 32L/2560d/32h, vocab 50304", vocab=50304, layers=32, heads=32,
+                       embd=2560, seq=2048, batch=32, strategy="ddp", tp=2, pp=2, microbatches=8,
+                       scaling="weak"),
+    "gpt6.7b-tp8": dict(model="gpt 6.7B 32L/4096d/32h, vocab 50304", vocab=50304, layers=32, heads=32,
+                        embd=4096, seq=2048, batch=4, strategy="none", tp=-1, pp=1, scaling="strong"),
+}
+# Small shapes of the same layouts, for CPU wiring tests (``--tiny``; never a headline number).
+_TINY = dict(vocab=256, layers=4, heads=4, embd=64, seq=32)
 
-def parse_args():
+
+def parse_args(argv=None):
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", choices=sorted(CONFIGS), default="gpt2s-ddp")
+    p.add_argument("--schedule", choices=["1f1b", "gpipe"], default="1f1b", help="pipeline configs only")
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-graph", action="store_true", help="our arm: run the step eagerly (no CUDA graph)")
-    return p.parse_args()
+    p.add_argument("--device", choices=["cuda", "cpu"], default="cuda",
+                   help="cpu: Gloo wiring check of both arms (host timing; not a benchmark)")
+    p.add_argument("--tiny", action="store_true", help="small model of the same layout (wiring checks only)")
+    return p.parse_args(argv)
+
+
+def resolve_config(name: str, world: int, tiny: bool = False) -> dict:
+    """The configuration with its layout resolved for ``world`` ranks."""
+    c = dict(CONFIGS[name])
+    if tiny:
+        c.update(_TINY, batch=4, model=c["model"] + " [tiny]")
+        if "microbatches" in c:
+            c["microbatches"] = 2
+    if c["tp"] == -1:
+        c["tp"] = world
+    if world % (c["tp"] * c["pp"]):
+        raise SystemExit(f"--config {name} needs a multiple of tp*pp = {c['tp'] * c['pp']} ranks, got {world}")
+    c["dp"] = world // (c["tp"] * c["pp"])
+    if c["strategy"] == "none" and c["dp"] > 1:
+        raise SystemExit(f"--config {name} has no data-parallel axis; use exactly tp*pp ranks")
+    return c
 
 
 # ---------------------------------------------------------------------------
@@ -151,21 +204,24 @@ def setup(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
-    torch.cuda.set_device(local)
-    if world > 1:
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    if args.device == "cuda":
+        torch.cuda.set_device(local)
+        if world > 1:
+            dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=600),
+                                    device_id=torch.device("cuda", local))
+    elif world > 1:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=600))
     return rank, world, local
 
 
-def max_over_ranks(value: float, world: int) -> float:
+def max_over_ranks(value: float, world: int, device: str = "cuda") -> float:
     import torch
     import torch.distributed as dist
 
     if world == 1:
         return value
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -177,72 +233,165 @@ def barrier(world: int) -> None:
         dist.barrier()
 
 
+def _sync(device: str) -> None:
+    import torch
+
+    if device == "cuda":
+        torch.cuda.synchronize()
+
+
 # ---------------------------------------------------------------------------
 # The two arms
 # ---------------------------------------------------------------------------
 
 
-def build(impl: str, world: int, seed: int, graph: bool = False):
-    """Model, optimizer and a step function through each framework's public API."""
-    import torch
+class Built:
+    """What a benchmark loop needs from an arm: a step function and the layout around it."""
 
+    def __init__(self, step, mesh, opt, graphable: bool, dp_rank: int, loss_holder: bool):
+        self.step = step
+        self.mesh = mesh
+        self.opt = opt
+        self.graphable = graphable
+        self.dp_rank = dp_rank
+        self.loss_holder = loss_holder  # this rank computes the loss (last pipeline stage)
+
+
+def _import_arm(impl: str):
+    """The ``minidist`` package of the requested arm (the reference one from baseline/_ref)."""
     if impl == "reference":
-        # The unmodified reference package, installed under baseline/_ref, on
-        # its stock path: its GPT, its DDP, torch AdamW, bf16 autocast
-        # (its examples/train_gpt.py with --precision bf16).
         sys.path.insert(0, REF_PATH)
         import minidist as md
-        from minidist.models import GPT, GPTConfig
 
         assert os.path.realpath(md.__file__).startswith(os.path.realpath(REF_PATH)), md.__file__
-        make_opt = lambda params: torch.optim.AdamW(params, lr=3e-4)  # noqa: E731
     else:
         import minidist as md
-        from minidist.models import GPT, GPTConfig
-        from minidist.optim import FusedAdamW
 
         assert os.path.realpath(md.__file__).startswith(os.path.realpath(os.path.join(ROOT, "minidist")))
-        make_opt = lambda params: FusedAdamW(params, lr=3e-4, capturable=graph)  # noqa: E731
+    return md
 
-    cfg = GPTConfig(vocab_size=MODEL["vocab"], block_size=MODEL["seq"], n_layer=MODEL["layers"],
-                    n_head=MODEL["heads"], n_embd=MODEL["embd"], seed=seed)
+
+def build(impl: str, c: dict, world: int, seed: int, graph: bool = False, device: str = "cuda",
+          schedule: str = "1f1b") -> Built:
+    """Model, optimizer and one training step through each framework's public API.
+
+    Both arms follow the reference trainer's assembly (examples/train_gpt.py:120-218):
+    a (tp, pp) mesh; GPT, or on a pipeline this stage's slice of
+    ``build_pipeline_layers`` with a vocab-parallel cross-entropy on the last stage;
+    DDP (25 MB buckets) or FSDP (one unit per Block, fp32 reduce) over the
+    data-parallel group; AdamW.  Our arm differs only where its API offers the
+    B200 path: FusedAdamW, deferred tail buckets, the fused LM-head loss and the
+    in-kernel sharded AdamW of FSDP.
+    """
+    import torch
+    from torch import nn
+
+    md = _import_arm(impl)
+    from minidist.models import GPT, Block, GPTConfig, build_pipeline_layers
+    from minidist.tensor_parallel import vocab_parallel_cross_entropy
+
+    ours = impl == "ours"
+    dev = torch.device(device)
+    cfg = GPTConfig(vocab_size=c["vocab"], block_size=c["seq"], n_layer=c["layers"], n_head=c["heads"],
+                    n_embd=c["embd"], seed=seed)
     torch.manual_seed(seed)
-    # Pure data parallelism, as the reference trainer builds it: a (tp=1, pp=1)
-    # mesh whose size-1 TP group keeps the whole model on every rank.
-    mesh = md.ParallelMesh(tp_size=1, pp_size=1)
-    model = GPT(cfg, tp_group=mesh.tp_group, device=torch.device("cuda"))
-    if world > 1:
-        # The last bucket (the token-embedding gradient, produced last in backward)
-        # finishes its all-reduce while FusedAdamW updates every other parameter.
-        model = md.DistributedDataParallel(model, process_group=mesh.dp_group, bucket_cap_mb=25.0,
-                                           defer_last_buckets=2)
-    opt = make_opt(model.parameters())
+    mesh = md.ParallelMesh(tp_size=c["tp"], pp_size=c["pp"])
+    pipelined = c["pp"] > 1
+    bf16 = device == "cuda"
 
-    def step(ids, tgt):
-        opt.zero_grad(set_to_none=True)
-        # (No autocast weight-cast cache: a cached cast made during a graph capture
-        # would outlive the capture.)
-        with torch.autocast("cuda", dtype=torch.bfloat16, cache_enabled=not graph):
-            _, loss = model(ids, tgt)
-        loss.backward()
-        opt.step()
-        return loss
+    loss_fn = None
+    if pipelined:
+        layers = build_pipeline_layers(cfg, tp_group=mesh.tp_group, device=dev)
+        mine = md.partition_layers(layers, mesh.pp_size, mesh.pp_rank)
+        del layers
+        vocab_start = mesh.tp_rank * (cfg.vocab_size // mesh.tp_size)
+        if ours and mesh.is_last_stage:
+            # The LM head's LayerNorm + GEMM + cross-entropy run as one fused loss.
+            head = mine[-1]
+            head.loss_only = True
 
-    return cfg, model, opt, step
+            def loss_fn(hidden, targets):
+                return head.loss(hidden, targets)
+
+            core = nn.Sequential(*mine)
+        else:
+            def loss_fn(logits, targets):
+                return vocab_parallel_cross_entropy(logits, targets, group=mesh.tp_group, vocab_start=vocab_start)
+
+            core = nn.Sequential(*mine)
+    else:
+        core = GPT(cfg, tp_group=mesh.tp_group, device=dev)
+
+    model = core
+    if mesh.dp_size > 1 and c["strategy"] == "ddp":
+        kw = dict(process_group=mesh.dp_group, bucket_cap_mb=25.0)
+        if ours and not pipelined:
+            # The tail buckets (the token-embedding gradient, produced last) finish their
+            # all-reduce while FusedAdamW updates every other parameter.
+            kw["defer_last_buckets"] = 2
+        model = md.DistributedDataParallel(core, **kw)
+    elif mesh.dp_size > 1 and c["strategy"] == "fsdp":
+        kw = dict(unit_types=(Block,), process_group=mesh.dp_group,
+                  mixed_precision=md.MixedPrecisionPolicy(param_dtype=torch.bfloat16 if bf16 else torch.float32,
+                                                          reduce_dtype=torch.float32))
+        model = md.FullyShardedDataParallel(core, **kw)
+
+    if ours and device == "cuda":
+        from minidist.optim import FusedAdamW
+
+        opt = FusedAdamW(model.parameters(), lr=3e-4, capturable=graph)
+    else:
+        opt = torch.optim.AdamW(model.parameters(), lr=3e-4)
+
+    if pipelined:
+        stage = md.PipelineStage(model, mesh, loss_fn=loss_fn if mesh.is_last_stage else None)
+        sched = md.build_schedule(schedule, stage, mesh, c["microbatches"])
+
+        def step(ids, tgt):
+            opt.zero_grad(set_to_none=True)
+            ctx = model.no_sync() if hasattr(model, "no_sync") else _Null()
+            with ctx, torch.autocast(device, dtype=torch.bfloat16, enabled=bf16):
+                loss = sched.step(inputs=ids, targets=tgt)
+            if hasattr(model, "finish_gradient_sync"):
+                model.finish_gradient_sync()
+            opt.step()
+            return loss
+    else:
+        def step(ids, tgt):
+            opt.zero_grad(set_to_none=True)
+            # (No autocast weight-cast cache: a cached cast made during a graph capture
+            # would outlive the capture.)
+            with torch.autocast(device, dtype=torch.bfloat16, enabled=bf16, cache_enabled=not graph):
+                _, loss = model(ids, tgt)
+            loss.backward()
+            opt.step()
+            return loss
+
+    graphable = ours and device == "cuda" and not pipelined and c["strategy"] != "fsdp"
+    return Built(step, mesh, opt, graphable, mesh.dp_rank, mesh.is_last_stage)
 
 
-def make_batches(n: int, rank: int, seed: int, vocab: int, pinned: bool):
+class _Null:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
+
+
+def make_batches(n: int, c: dict, dp_rank: int, seed: int, pinned: bool, device: str = "cuda"):
+    """Token batches seeded by ``seed + step*10000 + dp_rank`` (identical across TP/PP peers)."""
     import torch
 
     out = []
     for s in range(n):
-        g = torch.Generator().manual_seed(seed + s * 10_000 + rank)
-        ids = torch.randint(0, vocab, (MODEL["batch"], MODEL["seq"]), generator=g)
-        tgt = torch.randint(0, vocab, (MODEL["batch"], MODEL["seq"]), generator=g)
-        if pinned:
+        g = torch.Generator().manual_seed(seed + s * 10_000 + dp_rank)
+        ids = torch.randint(0, c["vocab"], (c["batch"], c["seq"]), generator=g)
+        tgt = torch.randint(0, c["vocab"], (c["batch"], c["seq"]), generator=g)
+        if pinned and device == "cuda":
             out.append((ids.pin_memory(), tgt.pin_memory()))
         else:
-            out.append((ids.cuda(), tgt.cuda()))
+            out.append((ids.to(device), tgt.to(device)))
     return out
 
 
@@ -258,18 +407,39 @@ def count_our_kernels(step, batch) -> int:
                and "md::" in e.name)
 
 
-def main() -> int:
-    args = parse_args()
+def _loss_value(loss, built: Built, device: str) -> float:
+    """The step's loss on every rank (pipeline: broadcast from the last stage, as the reference trainer does)."""
+    import torch
+    import torch.distributed as dist
+
+    mesh = built.mesh
+    if mesh.pp_size == 1:
+        return float(loss.detach().float().item())
+    v = torch.zeros(1, device=device)
+    if loss is not None:
+        v[0] = loss.detach().float().sum()
+    dist.broadcast(v, src=mesh.pp_ranks[-1], group=mesh.pp_group)
+    return float(v.item())
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
     import torch
 
     if args.impl == "reference" and not os.path.isdir(os.path.join(REF_PATH, "minidist")):
         print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
         return 0
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    c = resolve_config(args.config, world_env, args.tiny)
     rank, world, local = setup(args)
-    graph = args.impl == "ours" and not args.no_graph
-    cfg, model, opt, step = build(args.impl, world, args.seed, graph)
+    dev = args.device
+    cuda = dev == "cuda"
+    graph = args.impl == "ours" and not args.no_graph and cuda
+    built = build(args.impl, c, world, args.seed, graph, dev, args.schedule)
+    graph = graph and built.graphable
+    step = built.step
     K, W = args.steps, args.warmup
-    dev_batches = make_batches(K + W, rank, args.seed, cfg.vocab_size, pinned=False)
+    dev_batches = make_batches(K + W, c, built.dp_rank, args.seed, pinned=False, device=dev)
     graphed = None
     raw_step = step
     if graph:
@@ -279,7 +449,7 @@ def main() -> int:
         # steps below are replays.  Every rank takes the graph or none does.
         ok = 1
         try:
-            graphed = md.GraphedStep(step, dev_batches[0], warmup=2, optimizers=[opt])
+            graphed = md.GraphedStep(step, dev_batches[0], warmup=2, optimizers=[built.opt])
         except Exception as exc:  # noqa: BLE001 -- report and run eagerly
             print(f"bench: CUDA-graph capture failed on rank {rank} ({exc!r}); running eagerly",
                   file=sys.stderr, flush=True)
@@ -300,65 +470,70 @@ def main() -> int:
     # Clock sampling: one nvidia-smi per node (local rank 0) over every GPU of
     # this node's ranks, started before the warm-up so its start-up is over
     # when the timed window opens.
-    uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
-    uuids = [uuid]
-    if world > 1:
-        import torch.distributed as dist
+    sampler = None
+    if cuda:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+        uuids = [uuid]
+        if world > 1:
+            import torch.distributed as dist
 
-        allu = [None] * world
-        dist.all_gather_object(allu, (os.uname().nodename, uuid))
-        uuids = [u for n, u in allu if n == os.uname().nodename]
-    sampler = ClockSampler(uuids) if local == 0 else None
-    if sampler is not None:
-        sampler.start()
+            allu = [None] * world
+            dist.all_gather_object(allu, (os.uname().nodename, uuid))
+            uuids = [u for n, u in allu if n == os.uname().nodename]
+        sampler = ClockSampler(uuids) if local == 0 else None
+        if sampler is not None:
+            sampler.start()
 
     for i in range(W):
         step(*dev_batches[i])
-    torch.cuda.synchronize()
+    _sync(dev)
     barrier(world)
-    torch.cuda.synchronize()
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _sync(dev)
+    if cuda:
+        t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t_start.record()
     host_t0 = time.time()
-    t_start.record()
     loss = None
     for i in range(K):
         loss = step(*dev_batches[W + i])
-    t_end.record()
-    torch.cuda.synchronize()
+    if cuda:
+        t_end.record()
+    _sync(dev)
     host_t1 = time.time()
     barrier(world)
-    clocks = sampler.stop(host_t0, host_t1) if sampler is not None else None
+    clocks = sampler.stop(host_t0, host_t1) if sampler is not None else {"sm_mhz": None, "reasons": ["unsampled"]}
     if world > 1:
         import torch.distributed as dist
 
         got = [None] * world
         dist.all_gather_object(got, clocks)
         clocks = got[0]
-    ms = max_over_ranks(t_start.elapsed_time(t_end) / K, world)
-    final_loss = float(loss.detach().float().item())
+    local_ms = t_start.elapsed_time(t_end) / K if cuda else (host_t1 - host_t0) * 1e3 / K
+    ms = max_over_ranks(local_ms, world, dev)
+    final_loss = _loss_value(loss, built, dev)
 
+    tokens_per_step = c["batch"] * c["seq"] * built.mesh.dp_size
     e2e = None
     if not args.no_e2e:
-        host_batches = make_batches(K, rank, args.seed + 7, cfg.vocab_size, pinned=True)
+        host_batches = make_batches(K, c, built.dp_rank, args.seed + 7, pinned=True, device=dev)
         barrier(world)
-        torch.cuda.synchronize()
+        _sync(dev)
         t0 = time.perf_counter()
         for ids_h, tgt_h in host_batches:
-            ids = ids_h.to("cuda", non_blocking=True)
-            tgt = tgt_h.to("cuda", non_blocking=True)
-            _ = step(ids, tgt).item()  # device->host read of the step's loss
-        torch.cuda.synchronize()
-        e2e_s = max_over_ranks(time.perf_counter() - t0, world)
-        tokens = MODEL["batch"] * MODEL["seq"] * world * K
+            ids = ids_h.to(dev, non_blocking=True)
+            tgt = tgt_h.to(dev, non_blocking=True)
+            _loss_value(step(ids, tgt), built, dev)  # device->host read of the step's loss
+        _sync(dev)
+        e2e_s = max_over_ranks(time.perf_counter() - t0, world, dev)
         e2e = {
-            "value": tokens / e2e_s,
+            "value": tokens_per_step * K / e2e_s,
             "unit": "tokens/s",
             "h2d_bytes_per_step": int(host_batches[0][0].numel() * 8 * 2),
             "d2h_bytes_per_step": 4,
         }
 
     launches = 0
-    if args.impl == "ours":
+    if args.impl == "ours" and cuda:
         per_step = count_our_kernels(step, dev_batches[0])
         if per_step == 0 and graphed is not None:  # the profiler did not see inside the graph
             per_step = count_our_kernels(raw_step, dev_batches[0])
@@ -366,11 +541,29 @@ def main() -> int:
     if graphed is not None:
         graphed.release()
 
-    tokens_per_step = MODEL["batch"] * MODEL["seq"] * world
     value = tokens_per_step / (ms / 1e3)
+    n, L, S, V = c["embd"], c["layers"], c["seq"], c["vocab"]
     # Training FLOPs per token: 6 x matmul parameters + causal attention (QK^T and PV, half the pairs).
-    n, L, S = MODEL["embd"], MODEL["layers"], MODEL["seq"]
-    flops_tok = 6.0 * (L * 12 * n * n + n * MODEL["vocab"]) + 6.0 * L * 2 * S * n
+    flops_tok = 6.0 * (L * 12 * n * n + n * V) + 6.0 * L * 2 * S * n
+    par = f"dp{c['dp']}" if c["tp"] == 1 and c["pp"] == 1 else f"tp{c['tp']}xpp{c['pp']}xdp{c['dp']}"
+    strategy = {"ddp": "ddp, 25 MB buckets overlapped with backward",
+                "fsdp": "fsdp (ZeRO-3), bf16 parameter all-gather, fp32 master + fp32 reduce-scatter",
+                "none": "no data parallelism"}[c["strategy"]]
+    if c["strategy"] in ("ddp", "fsdp") and c["dp"] == 1:
+        strategy += " (single replica: unwrapped)"
+    cfg_out = {
+        "name": args.config,
+        "model": c["model"],
+        "global_batch": c["batch"] * c["dp"],
+        "seq_len": S,
+        "parallelism": par,
+        "strategy": strategy,
+        "optimizer": "AdamW lr 3e-4",
+        "cuda_graph": graph,
+        "l2": "no flush: per-step working set (GBs of activations + weights) >> 126 MB L2",
+    }
+    if c["pp"] > 1:
+        cfg_out["schedule"] = f"{args.schedule}, {c['microbatches']} microbatches"
     out = {
         "metric": METRIC,
         "value": value,
@@ -380,26 +573,19 @@ def main() -> int:
         "warmup": W,
         "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": c["scaling"],
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "bf16" if cuda else "fp32",
         "data": "synthetic uniform-random tokens (seeded), random-init weights",
-        "config": {
-            "model": "gpt2-small 12L/768d/12h, vocab 50257 (untied head)",
-            "global_batch": MODEL["batch"] * world,
-            "seq_len": MODEL["seq"],
-            "parallelism": f"dp{world}",
-            "strategy": "ddp, 25 MB buckets overlapped with backward",
-            "optimizer": "AdamW lr 3e-4",
-            "cuda_graph": graph,
-            "l2": "no flush: per-step working set (~6 GB activations + weights) >> 126 MB L2",
-        },
+        "config": cfg_out,
         "clocks": clocks,
         "e2e": e2e,
         "gpu_launches": launches,
         "tflops_per_gpu": flops_tok * tokens_per_step / world / (ms / 1e3) / 1e12,
         "final_loss": final_loss,
     }
+    if args.tiny or not cuda:
+        out["note"] = "wiring check: tiny model and/or CPU; not a benchmark number"
     if args.impl == "reference":
         out["impl"] = "reference"
     if rank == 0:
@@ -407,7 +593,7 @@ def main() -> int:
     if world > 1:
         import torch.distributed as dist
 
-        if args.impl == "ours":
+        if args.impl == "ours" and cuda:
             from minidist.parallel import symm
 
             symm.release_all()

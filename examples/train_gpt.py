@@ -121,18 +121,6 @@ def make_batch(config: GPTConfig, batch_size: int, dp_rank: int, step: int, seed
     return ids.to(device, non_blocking=True), targets.to(device, non_blocking=True)
 
 
-class _HeadNorm(nn.Module):
-    """Last pipeline layer on the fused path: passes hidden states through so the
-    LM head's cross-entropy can run fused inside the loss function."""
-
-    def __init__(self, head: LMHead):
-        super().__init__()
-        self.head = head
-
-    def forward(self, x):
-        return x
-
-
 def build(args, mesh: ParallelMesh, config: GPTConfig, device, precision):
     loss_fn = None
     fused = device.type == "cuda" and precision.enabled and precision.dtype == torch.bfloat16
@@ -141,8 +129,9 @@ def build(args, mesh: ParallelMesh, config: GPTConfig, device, precision):
         mine = partition_layers(layers, mesh.pp_size, mesh.pp_rank)
         vocab_start = mesh.tp_rank * (config.vocab_size // mesh.tp_size)
         if fused and isinstance(mine[-1], LMHead):
+            # LayerNorm + head GEMM + cross-entropy as one fused loss on the last stage.
             head = mine[-1]
-            mine[-1] = _HeadNorm(head)
+            head.loss_only = True
 
             def loss_fn(hidden, targets):
                 return head.loss(hidden, targets)

@@ -154,17 +154,30 @@ class Embedding(nn.Module):
 
 
 class LMHead(nn.Module):
-    """Final LayerNorm + column-parallel projection; logits stay vocabulary-sharded."""
+    """Final LayerNorm + column-parallel projection; logits stay vocabulary-sharded.
+
+    ``loss_only=True`` is for the last pipeline stage: ``forward`` then passes the
+    hidden states through unchanged and the stage's loss function calls
+    :meth:`loss`, which runs LayerNorm, the head GEMM and the vocab-parallel
+    cross-entropy as one fused op on the B200 path (the ``[tokens, vocab]``
+    logits are never handed between modules).  Parameter names do not change.
+    """
 
     def __init__(self, config: GPTConfig, tp_group=None, device=None, dtype=None):
         super().__init__()
         self.tp_group = tp_group
         self.vocab_size = config.vocab_size
+        self.loss_only = False
         self.ln_f = nn.LayerNorm(config.n_embd, device=device, dtype=dtype)
         self.head = ColumnParallelLinear(config.n_embd, config.vocab_size, bias=False, gather_output=False,
                                          group=tp_group, seed=_seed_for(config, -1, 2), device=device, dtype=dtype)
 
     def forward(self, x):
+        if self.loss_only:
+            return x
+        return self.logits(x)
+
+    def logits(self, x):
         from . import fused_gpt
 
         if fused_gpt.should_fuse(x):
@@ -182,7 +195,8 @@ class LMHead(nn.Module):
 
         if fused_gpt.should_fuse(x):
             return fused_gpt.head_loss(self, x, targets)
-        return vocab_parallel_cross_entropy(self(x), targets, group=self.tp_group, vocab_start=self.vocab_start)
+        return vocab_parallel_cross_entropy(self.logits(x), targets, group=self.tp_group,
+                                            vocab_start=self.vocab_start)
 
 
 class GPT(nn.Module):
@@ -203,11 +217,11 @@ class GPT(nn.Module):
         for block in self.blocks:
             x = block(x)
         if targets is None:
-            return self.lm_head(x)
+            return self.lm_head.logits(x)
         if fused_gpt.should_fuse(x):
             logits, loss = fused_gpt.head_logits_and_loss(self.lm_head, x, targets)
             return logits, loss
-        logits = self.lm_head(x)
+        logits = self.lm_head.logits(x)
         return logits, self.loss(logits, targets)
 
     def loss(self, logits, targets):
