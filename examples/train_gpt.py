@@ -93,6 +93,12 @@ def parse_args(argv=None) -> argparse.Namespace:
                           "every collective through NCCL (A/B comparison)")
     run.add_argument("--metrics-jsonl", metavar="PATH", default=None,
                      help="append one JSON line per logged step and a summary line (rank 0)")
+    run.add_argument("--defer-last-buckets", type=int, default=0, metavar="K",
+                     help="DDP: let the all-reduce of the last K gradient buckets (the token embedding, "
+                          "produced last) finish under the optimizer step instead of inside backward")
+    run.add_argument("--cuda-graph", action="store_true",
+                     help="capture the whole training step (forward, backward, collectives, FusedAdamW) as "
+                          "one CUDA graph and replay it (no pipeline, no FSDP, bf16 without loss scaling)")
     return p.parse_args(argv)
 
 
@@ -145,7 +151,8 @@ def build(args, mesh: ParallelMesh, config: GPTConfig, device, precision):
     wrapped = core
     if mesh.dp_size > 1 and args.strategy == "ddp":
         wrapped = DistributedDataParallel(core, process_group=mesh.dp_group, bucket_cap_mb=args.bucket_cap_mb,
-                                          overlap_with_backward=not args.no_overlap)
+                                          overlap_with_backward=not args.no_overlap,
+                                          defer_last_buckets=args.defer_last_buckets)
     elif mesh.dp_size > 1 and args.strategy == "fsdp":
         param_dtype = {None: torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}[args.fsdp_param_dtype]
         wrapped = FullyShardedDataParallel(
@@ -156,12 +163,12 @@ def build(args, mesh: ParallelMesh, config: GPTConfig, device, precision):
 
 def make_optimizer(args, model, device):
     params = list(model.parameters())
-    use_fused = args.optimizer == "fused" or (
+    use_fused = args.optimizer == "fused" or args.cuda_graph or (
         args.optimizer == "auto" and device.type == "cuda" and all(p.dtype == torch.float32 for p in params))
     if use_fused:
         from minidist.optim import FusedAdamW
 
-        return FusedAdamW(params, lr=args.lr)
+        return FusedAdamW(params, lr=args.lr, capturable=args.cuda_graph)
     return torch.optim.AdamW(params, lr=args.lr)
 
 
@@ -219,8 +226,30 @@ def main(argv=None) -> None:
     if isinstance(model, DistributedDataParallel):
         print_rank0(f"  DDP: {len(model.bucket_summary())} buckets, reducer={model.reducer_name}")
 
+    graphed = None
+    if args.cuda_graph:
+        if schedule is not None or isinstance(model, FullyShardedDataParallel) or scaler.enabled \
+                or device.type != "cuda":
+            raise SystemExit("--cuda-graph needs CUDA, no pipeline, no FSDP and no fp16 loss scaling")
+        from minidist import GraphedStep
+
+        def graph_body(ids, targets):
+            optimizer.zero_grad(set_to_none=True)
+            # No autocast weight-cast cache: a cast cached during capture would outlive it.
+            with torch.autocast("cuda", dtype=precision.dtype, enabled=precision.enabled, cache_enabled=False):
+                _, loss = model(ids, targets)
+            loss.backward()
+            optimizer.step()
+            return loss
+
+        # Two eager steps on a side stream (lazy set-up), then one capture.
+        graphed = GraphedStep(graph_body, make_batch(config, args.batch_size, mesh.dp_rank, 0, args.seed, device),
+                              warmup=2, optimizers=[optimizer])
+
     def train_step(step: int) -> float:
         ids, targets = make_batch(config, args.batch_size, mesh.dp_rank, step, args.seed, device)
+        if graphed is not None:
+            return float(graphed(ids, targets).item())
         optimizer.zero_grad(set_to_none=True)
         if schedule is not None:
             schedule.loss_scale = scaler.scale
@@ -298,6 +327,8 @@ def main(argv=None) -> None:
         if mesh.rank == 0:
             print_rank0("\n  overlap:")
             print_rank0(analyze_trace(trace).format())
+    if graphed is not None:
+        graphed.release()  # a graph holding peer-memory or NCCL work goes before the process group
     shutdown_distributed()
 
 

@@ -140,6 +140,9 @@ class DistributedGradScaler:
             return False
         if self._step_found_inf is not None:
             return self._step_found_inf
+        from .ddp import wait_all_deferred
+
+        wait_all_deferred()  # DDP tail buckets still being reduced (defer_last_buckets)
         grads = self._grads(optimizer)
         device = grads[0].device if grads else comm.current_device()
         flag = torch.zeros(1, dtype=torch.float32, device=device)

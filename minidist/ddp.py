@@ -24,6 +24,7 @@ bucket is pre-scaled and handed to ``torch.distributed.all_reduce``.
 from __future__ import annotations
 
 import os
+import weakref
 from collections.abc import Iterator
 from contextlib import contextmanager
 
@@ -34,7 +35,7 @@ from torch import nn
 from . import comm
 from .ops import grads as gradsink
 
-__all__ = ["DistributedDataParallel", "DDP"]
+__all__ = ["DistributedDataParallel", "DDP", "wait_all_deferred"]
 
 _DEFAULT_BUCKET_CAP_MB = 25.0
 _ALIGN = 64  # elements; keeps every parameter's slice 256-byte aligned for the kernels
@@ -88,15 +89,23 @@ class DistributedDataParallel(nn.Module):
         defer_last_buckets: int = 0,
     ):
         """``defer_last_buckets = k``: backward returns without waiting for the all-reduce
-        of the last ``k`` buckets (on the fused peer-memory reducer, whose work is a CUDA
-        event).  Their parameters carry the event as ``_md_grad_event``;
+        of the last ``k`` buckets.  Their parameters carry the reduction's handle (a CUDA
+        event on the peer-memory reducer, a ``Work`` on NCCL / Gloo) as ``_md_grad_event``;
         :class:`minidist.optim.FusedAdamW` updates every other parameter first and waits on
-        the events only for those, so the all-reduce of the gradients produced last in
-        backward (the token embedding) overlaps the optimizer.  Other consumers of the
-        gradients call :meth:`wait_gradients` first."""
+        the handles only for those, so the all-reduce of the gradients produced last in
+        backward (the token embedding) overlaps the optimizer.
+
+        Nothing else can see an un-reduced gradient: any other optimizer's ``step`` (a
+        global step pre-hook), :meth:`DistributedGradScaler.unscale_
+        <minidist.amp.DistributedGradScaler.unscale_>`, the next forward and ``no_sync``
+        all wait first.  Code that reads ``.grad`` directly between backward and the
+        optimizer step (e.g. ``clip_grad_norm_``) calls :meth:`wait_gradients` or
+        :func:`wait_all_deferred` before it."""
         super().__init__()
         self.defer_last_buckets = int(defer_last_buckets)
         self._deferred: list = []
+        if self.defer_last_buckets > 0:
+            _install_step_guard()
         comm.check_same_layout(list(module.parameters()), process_group, "DistributedDataParallel")
         self.module = module
         self.process_group = process_group
@@ -227,33 +236,43 @@ class DistributedDataParallel(nn.Module):
             self._next_to_launch += 1
         tail = {id(b) for b in self._buckets[len(self._buckets) - self.defer_last_buckets:]} \
             if self.defer_last_buckets > 0 else set()
-        self._deferred = []
+        self.wait_gradients()  # a previous step's deferred buckets, if nobody consumed them
         for b in self._buckets:
             if b.launched:
-                if id(b) in tail and isinstance(b.work, torch.cuda.Event):
+                if id(b) in tail and b.work is not None:
                     for p in b.params:
                         p._md_grad_event = b.work
                     self._deferred.extend(b.params)
                 else:
                     self._reducer.wait(b)
             b.reset()
+        if self._deferred:
+            _PENDING.add(self)
         self._next_to_launch = 0
         self._ready.clear()
 
     # -- public API --------------------------------------------------------------
 
     def wait_gradients(self) -> None:
-        """Make the current stream wait for the deferred buckets (see ``defer_last_buckets``)."""
+        """Order the current stream (or the host, for a ``Work``) after the deferred buckets'
+        all-reduce (see ``defer_last_buckets``); a no-op when nothing is pending."""
+        if not self._deferred:
+            return
+        seen: set[int] = set()
         for p in self._deferred:
-            ev = getattr(p, "_md_grad_event", None)
-            if ev is not None:
-                torch.cuda.current_stream().wait_event(ev)
+            h = getattr(p, "_md_grad_event", None)
+            if h is not None:
+                if id(h) not in seen:
+                    seen.add(id(h))
+                    wait_handle(h)
                 p._md_grad_event = None
         self._deferred = []
+        _PENDING.discard(self)
 
     @contextmanager
     def no_sync(self) -> Iterator[None]:
         """Accumulate gradients locally; the next synchronised backward reduces the sum."""
+        self.wait_gradients()
         prev = self.require_backward_grad_sync
         self.require_backward_grad_sync = False
         try:
@@ -262,6 +281,7 @@ class DistributedDataParallel(nn.Module):
             self.require_backward_grad_sync = prev
 
     def forward(self, *args, **kwargs):
+        self.wait_gradients()
         return self.module(*args, **kwargs)
 
     def bucket_summary(self) -> list[tuple[int, int, float]]:
@@ -281,6 +301,45 @@ class DistributedDataParallel(nn.Module):
 
 
 DDP = DistributedDataParallel
+
+
+# ---------------------------------------------------------------------------
+# Deferred gradients: nobody but an optimizer that asks for them sees them early
+# ---------------------------------------------------------------------------
+
+# DDP instances whose last backward left deferred buckets in flight.
+_PENDING: weakref.WeakSet = weakref.WeakSet()
+_GUARD = None
+
+
+def wait_handle(h) -> None:
+    """Wait for one gradient-reduction handle: a CUDA event (the current stream waits) or a
+    ``torch.distributed`` ``Work``."""
+    if isinstance(h, torch.cuda.Event):
+        torch.cuda.current_stream().wait_event(h)
+    else:
+        h.wait()
+
+
+def wait_all_deferred() -> None:
+    """Wait for every DDP module's deferred gradient buckets (see ``defer_last_buckets``)."""
+    for ddp in list(_PENDING):
+        ddp.wait_gradients()
+
+
+def _step_guard(optimizer, args, kwargs) -> None:
+    # An optimizer that orders itself after each parameter's handle (FusedAdamW) declares it;
+    # every other optimizer sees fully reduced gradients.
+    if _PENDING and not getattr(optimizer, "honours_grad_events", False):
+        wait_all_deferred()
+
+
+def _install_step_guard() -> None:
+    global _GUARD
+    if _GUARD is None:
+        from torch.optim.optimizer import register_optimizer_step_pre_hook
+
+        _GUARD = register_optimizer_step_pre_hook(_step_guard)
 
 
 # ---------------------------------------------------------------------------

@@ -20,6 +20,7 @@ import math
 
 import torch
 
+from .ddp import wait_handle
 from .ops import _native as nat
 from .ops import grads as gradsink
 
@@ -27,6 +28,11 @@ __all__ = ["FusedAdamW"]
 
 
 class FusedAdamW(torch.optim.Optimizer):
+    # Parameters whose DDP all-reduce is still in flight (``_md_grad_event``) are
+    # updated last, after waiting on exactly their handle (DistributedDataParallel's
+    # ``defer_last_buckets``); the global step guard in minidist.ddp leaves them to us.
+    honours_grad_events = True
+
     def __init__(self, params, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 1e-2, capturable: bool = False):
         if lr < 0 or eps < 0 or not (0 <= betas[0] < 1 and 0 <= betas[1] < 1):
@@ -112,14 +118,17 @@ class FusedAdamW(torch.optim.Optimizer):
                     if early:
                         self._fused_update((gi, 0), early, lr, b1, b2, eps, wd, bc1, bc2_sqrt, hp)
                     for ev in {id(p._md_grad_event): p._md_grad_event for p in late}.values():
-                        torch.cuda.current_stream().wait_event(ev)
+                        wait_handle(ev)
                     for p in late:
                         p._md_grad_event = None
                     self._fused_update((gi, 1), late, lr, b1, b2, eps, wd, bc1, bc2_sqrt, hp)
                 else:
                     self._fused_update(gi, fused, lr, b1, b2, eps, wd, bc1, bc2_sqrt, hp)
                 self._ensure_grad_buffers()
+            for ev in {id(h): h for h in (getattr(p, "_md_grad_event", None) for p in rest) if h is not None}.values():
+                wait_handle(ev)
             for p in rest:
+                p._md_grad_event = None
                 st = self.state[p]
                 g = p.grad.to(p.dtype)
                 p.mul_(1 - lr * wd)

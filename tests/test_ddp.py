@@ -82,6 +82,46 @@ def _layout(rank, world):
     assert model._buckets[0].params[0] is params[-1], "bucket 0 must start at the last parameter"
 
 
+def _deferred_with_torch_adamw(rank, world):
+    """Deferred tail buckets are invisible to an optimizer that does not ask for them:
+    torch AdamW over DDP(defer_last_buckets=2) takes exactly the steps it takes over a DDP
+    that waits for every bucket in backward."""
+    from minidist import ddp as ddp_mod
+
+    solo = solo_group(rank, world)
+    ids, tgt = _data()
+    runs = []
+    for defer in (0, 2):
+        model = DistributedDataParallel(GPT(CFG, tp_group=solo), bucket_cap_mb=0.01, defer_last_buckets=defer)
+        opt = torch.optim.AdamW(model.parameters(), lr=1e-2)
+        for it in range(3):
+            x, y = ids.roll(it, 0).chunk(world)[rank], tgt.roll(it, 0).chunk(world)[rank]
+            opt.zero_grad()
+            model(x, y)[1].backward()
+            if defer:
+                assert model._deferred, "the tail buckets should still be in flight after backward"
+            opt.step()  # the global step pre-hook waits for them
+            assert not model._deferred and model not in ddp_mod._PENDING
+        runs.append(model)
+    for (name, p), (_, q) in zip(runs[1].module.named_parameters(), runs[0].module.named_parameters()):
+        assert torch.equal(p, q), f"[rank {rank}] deferred + torch AdamW differs at {name}"
+    # Direct gradient readers wait explicitly.
+    model = runs[1]
+    model.zero_grad()
+    model(ids.chunk(world)[rank], tgt.chunk(world)[rank])[1].backward()
+    ddp_mod.wait_all_deferred()
+    norm = torch.nn.utils.clip_grad_norm_(model.parameters(), 1e9)
+    ref = runs[0]
+    ref.zero_grad()
+    ref(ids.chunk(world)[rank], tgt.chunk(world)[rank])[1].backward()
+    want = torch.nn.utils.clip_grad_norm_(ref.parameters(), 1e9)
+    assert torch.equal(norm, want), (norm, want)
+
+
+def test_ddp_deferred_buckets_with_a_plain_optimizer():
+    run_distributed(_deferred_with_torch_adamw, 2)
+
+
 @pytest.mark.parametrize("world", [2, 4])
 def test_ddp_matches_full_batch_gradient(world):
     run_distributed(_default, world)
