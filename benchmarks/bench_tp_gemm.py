@@ -11,8 +11,12 @@ it times, on the device (CUDA events, max over ranks, after warm-up):
   publishes bf16 partial tiles in symmetric memory and comm warps of the same
   kernel reduce this rank's tiles over NVLink (bias + residual added once) and
   copy the rest from their owners;
-* ``nccl``   — the reference structure (tensor_parallel.py:354-368): GEMM,
-  NCCL all-reduce of the bf16 output, then bias and residual.
+* ``nccl``   — our tcgen05 GEMM, then NCCL all-reduce of the bf16 output,
+  then bias and residual;
+* ``ref``    — the reference's row-parallel linear itself
+  (tensor_parallel.py:351-358, under bf16 autocast): ``F.linear`` (cuBLAS),
+  ``all_reduce`` over NCCL, bias added after the reduce, then the residual add
+  of its block (models/gpt.py:163-166).
 
 The roofline column is max(GEMM FLOPs / measured bf16 peak, NVLink bytes per
 rank / 770 GB/s), with NVLink bytes = 2 (W-1)/W * M * N * 2 (the all-reduce
@@ -76,6 +80,7 @@ def main() -> None:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--json", metavar="PATH", default=None, help="rank 0 appends one JSON line per shape")
     p.add_argument("--sweep", default="gpt", choices=["gpt", "baseline"],
                    help="gpt: GPT-2 small / 6.7B layer shapes (K per rank as at tp=8); "
                         "baseline: M in {2048, 8192, 32768}, K = N = 4096 (K split over the ranks)")
@@ -83,8 +88,8 @@ def main() -> None:
     rank, world, device = init_distributed(backend="nccl")
     peak = _peak_tflops() * 1e12
     print_rank0(f"\n  row-parallel GEMM + all-reduce, W={world}  (times: max over ranks)")
-    print_rank0(f"  {'M':>6}{'K':>6}{'N':>6}{'fused us':>10}{'nccl us':>10}{'speedup':>9}{'roofline us':>13}{'frac':>7}"
-                f"{'host us (fused/nccl)':>22}")
+    print_rank0(f"  {'M':>6}{'K':>6}{'N':>6}{'fused us':>10}{'nccl us':>10}{'ref us':>10}{'vs ref':>8}"
+                f"{'roofline us':>13}{'frac':>7}{'host us (fused/nccl)':>22}")
     if args.sweep == "baseline":
         shapes = [(M, 4096 // world, 4096) for M in (2048, 8192, 32768)]
     else:
@@ -100,11 +105,24 @@ def main() -> None:
         os.environ["MINIDIST_TP_FUSED"] = "0"
         tn, hn = timed(lambda: collectives.gemm_all_reduce(x, w, bias, resid, None), args.iters, args.warmup)
         os.environ["MINIDIST_TP_FUSED"] = "1"
+
+        def reference_row_parallel():
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                y = torch.nn.functional.linear(x, w)
+                dist.all_reduce(y)
+                y = y + bias
+                return resid + y
+
+        tr, _ = timed(reference_row_parallel, args.iters, args.warmup)
         flops = 2.0 * M * N * K
         nv = 2.0 * (world - 1) / world * M * N * 2
         roof = max(flops / peak, nv / 770e9)
-        print_rank0(f"  {M:>6}{K:>6}{N:>6}{tf * 1e6:>10.1f}{tn * 1e6:>10.1f}{tn / tf:>8.2f}x{roof * 1e6:>13.1f}"
-                    f"{roof / tf:>7.2f}{hf * 1e6:>12.1f}/{hn * 1e6:.1f}")
+        print_rank0(f"  {M:>6}{K:>6}{N:>6}{tf * 1e6:>10.1f}{tn * 1e6:>10.1f}{tr * 1e6:>10.1f}{tr / tf:>7.2f}x"
+                    f"{roof * 1e6:>13.1f}{roof / tf:>7.2f}{hf * 1e6:>12.1f}/{hn * 1e6:.1f}")
+        if args.json and rank == 0:
+            with open(args.json, "a") as f:
+                f.write(json.dumps(dict(world=world, M=M, K=K, N=N, fused_us=tf * 1e6, nccl_us=tn * 1e6,
+                                        ref_us=tr * 1e6, roofline_us=roof * 1e6, frac=roof / tf)) + "\n")
     shutdown_distributed()
 
 

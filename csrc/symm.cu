@@ -127,6 +127,33 @@ struct MdCeTpParams {
   float* loss;  // [M] out (lse - target logit)
 };
 
+// Vocab-parallel embedding forward (md_embed_tp): every rank's bf16 shard of
+// the token table sits in symmetric memory, so the token row for id lives on
+// exactly one rank (the owner of its vocabulary range).  Each rank reads every
+// row of its batch straight from the owner's shard over NVLink and adds the
+// position row -- the reference's masked local lookup followed by an
+// all-reduce of the [tokens, C] activations (tensor_parallel.py:409-416,
+// gpt.py:183-185) as one gather that moves (W-1)/W of the rows once instead
+// of 2(W-1)/W of them through a reduction.  An arrive barrier orders the
+// reads after every owner's last shard update (its optimizer step is stream-
+// ordered before this launch); a depart barrier keeps an owner from updating
+// its shard while a peer may still be reading it.
+struct MdEmbTpParams {
+  const __nv_bfloat16* wte[md::symm::kMaxWorld];  // every rank's [vocab_rows, ldw] bf16 shard
+  uint32_t* flags[md::symm::kMaxWorld];
+  int world, rank, channel;
+  unsigned long long timeout_ns;
+  md::Status* status;
+  const long long* ids;       // [M] token ids (global vocabulary)
+  const __nv_bfloat16* wpe;   // [>= S, ldp] position rows (local)
+  long long ldp;
+  __nv_bfloat16* out;         // [M, ldo]
+  long long ldo;
+  long long ldw;
+  long long vocab_rows;       // rows per shard (vocab / world)
+  int M, S, C;                // C a multiple of 8
+};
+
 namespace md {
 namespace symm {
 
@@ -441,10 +468,71 @@ __global__ void __launch_bounds__(256) md_ce_tp_kernel(const __grid_constant__ M
   vcta_release(p, vct.epoch);
 }
 
+// One warp per token row, each lane moving 16 bytes per vector with up to 8
+// peer loads in flight before any arithmetic (NVLink latency is ~1 us).
+__global__ void __launch_bounds__(256) md_embed_tp_kernel(const __grid_constant__ MdEmbTpParams p) {
+  const VCta vct = vcta_claim(p);
+  const int vc = vct.v;
+  const uint32_t arrive = 2u * vct.epoch + 1u, depart = 2u * vct.epoch + 2u;
+  if (vc >= 0 && cta_barrier(p, vc, arrive, 140)) {
+    const int warps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int per = (p.M + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+    const int lo = vc * per, hi = min(p.M, lo + per);
+    const int nvec = p.C / 8;
+    constexpr int U = 8;
+    for (int m = lo + warp; m < hi; m += warps) {
+      const long long id = p.ids[m];
+      long long owner = id / p.vocab_rows;
+      if (owner >= p.world) owner = p.world - 1;
+      const long long row = id - owner * p.vocab_rows;
+      const bool valid = id >= 0 && row < p.vocab_rows;
+      const uint4* src = reinterpret_cast<const uint4*>(p.wte[valid ? owner : 0] + (valid ? row : 0) * p.ldw);
+      const uint4* pos = reinterpret_cast<const uint4*>(p.wpe + static_cast<long long>(m % p.S) * p.ldp);
+      uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<long long>(m) * p.ldo);
+      for (int j0 = lane; j0 < nvec; j0 += 32 * U) {
+        uint4 w[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+          const int j = j0 + 32 * k;
+          w[k] = (valid && j < nvec) ? __ldcg(src + j) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+          const int j = j0 + 32 * k;
+          if (j >= nvec) break;
+          const uint4 q = pos[j];
+          const uint32_t a[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+          const uint32_t b[4] = {q.x, q.y, q.z, q.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 x = unpack_bf16x2(a[e]), y = unpack_bf16x2(b[e]);
+            o[e] = pack_bf16x2(x.x + y.x, x.y + y.y);
+          }
+          dst[j] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+    }
+    cta_barrier(p, vc, depart, 141);
+  }
+  vcta_release(p, vct.epoch);
+}
+
 }  // namespace symm
 }  // namespace md
 
 extern "C" {
+
+// Launch md_embed_tp_kernel with `ctas` CTAs (<= 160; the same count on every rank).
+int md_embed_tp(const MdEmbTpParams* prm, int ctas, cudaStream_t s) {
+  if (prm == nullptr || prm->world < 1 || prm->world > md::symm::kMaxWorld || prm->M <= 0 || prm->S <= 0 ||
+      prm->C <= 0 || (prm->C % 8) || (prm->ldw % 8) || (prm->ldp % 8) || (prm->ldo % 8) || prm->vocab_rows <= 0 ||
+      prm->out == nullptr || prm->ids == nullptr || prm->wpe == nullptr)
+    return -1;
+  if (ctas < 1 || ctas > md::symm::kMaxCtas || prm->channel < 0 || prm->channel >= md::symm::kChannels) return -2;
+  md::symm::md_embed_tp_kernel<<<ctas, 256, 0, s>>>(*prm);
+  return static_cast<int>(cudaGetLastError());
+}
 
 // Launch md_ce_tp_kernel with `ctas` CTAs (<= 160).
 int md_ce_tp(const MdCeTpParams* prm, int ctas, cudaStream_t s) {

@@ -20,10 +20,19 @@ are column sums fused into the LayerNorm backward, and nothing goes through
 autograd's AccumulateGrad; wrappers learn that a gradient is ready through
 :mod:`minidist.ops.grads`.
 
-With tensor parallelism the partial outputs of the row-parallel GEMMs and the
-input gradients of the column-parallel GEMMs are all-reduced over the TP group
-(the reference's ``g`` and ``f``, tensor_parallel.py:134-172) through
-:mod:`minidist.parallel.tp_fused`.
+With tensor parallelism every reduction over the TP group (the reference's
+``g`` and ``f``, tensor_parallel.py:134-172) runs in a peer-memory kernel of
+:mod:`minidist.parallel.collectives` when the group shares a node:
+
+* row-parallel forward (attention and MLP projections): ``md_gemm_ar``, the
+  GEMM with its all-reduce, bias and residual in one persistent kernel;
+* column-parallel backward (QKV, fc and the LM head's data gradient): the same
+  kernel on the data-gradient GEMM;
+* vocab-parallel embedding forward: ``md_embed_tp``, which reads each token
+  row from the rank that owns it instead of reducing masked lookups;
+* vocab-parallel cross-entropy statistics: ``md_ce_tp``.
+
+NCCL (``collectives.all_reduce_``) is the fallback off-node.
 """
 
 from __future__ import annotations
@@ -134,11 +143,11 @@ def _dgrad_all_reduce(dy: torch.Tensor, w: torch.Tensor, group) -> torch.Tensor:
 
 
 def _all_reduce_(t: torch.Tensor, group) -> torch.Tensor:
-    """Sum ``t`` over the TP group in place (fused NVLink kernel when available, else NCCL)."""
+    """Sum ``t`` over the TP group in place with NCCL (fallback of the peer-memory kernels)."""
     if _tp_world(group) > 1:
-        from ..parallel import tp_fused
+        from ..parallel import collectives
 
-        tp_fused.all_reduce_(t, group)
+        collectives.all_reduce_(t, group)
     return t
 
 
@@ -154,11 +163,18 @@ class _EmbeddingFn(torch.autograd.Function):
         emb = mod.wte
         group = emb.group
         tp = _tp_world(group)
-        add_pos = tp == 1 or emb.rank == 0  # positions summed once across the TP reduction
-        x = K.embedding_fwd(ids, bf16_weight(wte), bf16_weight(wpe)[:S] if add_pos else None, S,
-                            vocab_start=emb.vocab_start if tp > 1 else 0)
+        x = None
         if tp > 1:
-            _all_reduce_(x, group)
+            from ..parallel import collectives
+
+            # Each row read from the rank that owns its vocabulary range (no reduction).
+            x = collectives.embedding_tp(ids, wte, bf16_weight(wpe)[:S], group)
+        if x is None:
+            add_pos = tp == 1 or emb.rank == 0  # positions summed once across the TP reduction
+            x = K.embedding_fwd(ids, bf16_weight(wte), bf16_weight(wpe)[:S] if add_pos else None, S,
+                                vocab_start=emb.vocab_start if tp > 1 else 0)
+            if tp > 1:
+                _all_reduce_(x, group)
         ctx.mod, ctx.ids, ctx.shape = mod, ids, (B, S)
         return x.view(B, S, -1)
 
@@ -229,17 +245,17 @@ class _BlockFn(torch.autograd.Function):
         if tp == 1:
             x1 = G.linear_fwd(y, w_proj, proj_b, resid=xin)
         else:
-            from ..parallel import tp_fused
+            from ..parallel import collectives
 
-            x1 = tp_fused.row_parallel_fwd(y, w_proj, proj_b, xin, group)
+            x1 = collectives.gemm_all_reduce(y, w_proj, proj_b, xin, group)
         h2, mu2, r2 = K.layernorm_fwd(x1, ln2g, ln2b, blk.ln2.eps)
         a, hpre = G.linear_fwd(h2, w_fc, fc_b, gelu=True)
         if tp == 1:
             x2 = G.linear_fwd(a, w_mproj, mproj_b, resid=x1)
         else:
-            from ..parallel import tp_fused
+            from ..parallel import collectives
 
-            x2 = tp_fused.row_parallel_fwd(a, w_mproj, mproj_b, x1, group)
+            x2 = collectives.gemm_all_reduce(a, w_mproj, mproj_b, x1, group)
 
         ctx.blk = blk
         ctx.dims = (B, S, C, H, D, tp)
@@ -425,8 +441,7 @@ class _HeadFn(torch.autograd.Function):
         if t_w is not None:
             G.linear_wgrad(dlogits, h, t_w.dst, accumulate=t_w.accumulate)
             t_w.commit()
-        dh = G.linear_dgrad(dlogits, wb)
-        _all_reduce_(dh, group)
+        dh = _dgrad_all_reduce(dlogits, wb, group)  # f backward of the column-parallel head
         t_g, t_b = _targets(head.ln_f.weight, head.ln_f.bias)
         dx = K.layernorm_bwd(dh, xin, mu, r, lnw,
                              dgamma=t_g.dst if t_g else None, acc_gamma=bool(t_g and t_g.accumulate),

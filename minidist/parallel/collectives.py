@@ -146,13 +146,98 @@ def make_bucket_reducer(ddp, required: bool = False):
 
 
 # ---------------------------------------------------------------------------
-# Tensor parallel (NCCL)
+# Tensor parallel
 # ---------------------------------------------------------------------------
 
 
 def all_reduce_(t: torch.Tensor, group) -> torch.Tensor:
+    """NCCL all-reduce (sum) of ``t`` in place: the fallback for the tensor-parallel sites whose
+    peer-memory kernel is unavailable (no shared node, ``MINIDIST_TP_FUSED=0``, unsupported shape)."""
     comm.all_reduce(t, group=group)
     return t
+
+
+_EMB_CHANNEL = 7
+
+
+class EmbTpParams(ctypes.Structure):
+    """Mirror of ``struct MdEmbTpParams`` (csrc/symm.cu)."""
+
+    _fields_ = [
+        ("wte", ctypes.c_void_p * _MAXW),
+        ("flags", ctypes.c_void_p * _MAXW),
+        ("world", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("channel", ctypes.c_int),
+        ("timeout_ns", ctypes.c_ulonglong),
+        ("status", ctypes.c_void_p),
+        ("ids", ctypes.c_void_p),
+        ("wpe", ctypes.c_void_p),
+        ("ldp", ctypes.c_longlong),
+        ("out", ctypes.c_void_p),
+        ("ldo", ctypes.c_longlong),
+        ("ldw", ctypes.c_longlong),
+        ("vocab_rows", ctypes.c_longlong),
+        ("M", ctypes.c_int),
+        ("S", ctypes.c_int),
+        ("C", ctypes.c_int),
+    ]
+
+
+nat.declare("md_embed_tp", "i:pip")
+
+
+def symmetric_bf16_shadow(c: symm.Communicator, p: torch.Tensor):
+    """Give fp32 parameter ``p`` a bf16 shadow that lives in symmetric memory (peers can read
+    it); returns ``(shadow, buffer)``.  The shadow is refreshed like any other (a cast when
+    ``p`` changed, or in place by :class:`~minidist.optim.FusedAdamW`).  The first call is
+    collective over ``c``'s group: every rank registers its tables in the same order."""
+    from ..models import fused_gpt as F
+
+    buf = getattr(p, "_md_symm_shadow_buf", None)
+    if buf is None:
+        tables = c.__dict__.setdefault("_shadow_tables", [])
+        buf = c.buffer(f"tp_table_{len(tables)}", p.numel() * 2)
+        tables.append(buf)
+        setattr(p, F._SHADOW, buf.view(torch.bfloat16, 0, p.numel()).view(p.shape))
+        setattr(p, F._SHADOW_VER, None)  # force the first refresh
+        p._md_symm_shadow_buf = buf
+    return F.bf16_weight(p), buf
+
+
+def embedding_tp(ids: torch.Tensor, wte: torch.Tensor, wpe_bf16: torch.Tensor, group) -> torch.Tensor | None:
+    """Vocab-parallel embedding forward ``wte[ids] + wpe[s]`` (bf16 ``[B*S, C]``) read straight from
+    the owning rank's table shard over NVLink (``md_embed_tp``); ``None`` when peer memory is
+    unavailable for ``group`` (the caller does the masked lookup + NCCL all-reduce)."""
+    if not _tp_fused_enabled() or wte.dtype != torch.float32:
+        return None
+    c = _group_comm(group)
+    if c is None or wte.shape[1] % 8:
+        return None
+    shadow, buf = symmetric_bf16_shadow(c, wte)
+    B, S = ids.shape
+    M, C = B * S, shadow.shape[1]
+    ids_c = ids.reshape(-1)
+    if ids_c.dtype != torch.int64 or not ids_c.is_contiguous():
+        ids_c = ids_c.to(torch.int64).contiguous()
+    out = torch.empty(M, C, dtype=torch.bfloat16, device=ids.device)
+    prm = EmbTpParams()
+    for r in range(c.world):
+        prm.wte[r], prm.flags[r] = buf.ptrs[r], buf.flag_ptrs[r]
+    prm.world, prm.rank, prm.channel = c.world, c.rank, _EMB_CHANNEL
+    prm.timeout_ns, prm.status = _timeout_ns(), nat.status_ptr(ids.device)
+    prm.ids, prm.wpe, prm.ldp = ids_c.data_ptr(), wpe_bf16.data_ptr(), wpe_bf16.stride(0)
+    prm.out, prm.ldo = out.data_ptr(), out.stride(0)
+    prm.ldw, prm.vocab_rows = shadow.stride(0), shadow.shape[0]
+    prm.M, prm.S, prm.C = M, S, C
+    ctas = min(148, max(1, -(-M // 32)))
+    with _Range("md_embed_tp"):
+        rc = nat.lib().md_embed_tp(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr(None)))
+    nat.check(rc, "md_embed_tp")
+    # Bytes as the all-reduce it replaces would count them (so CommStats stays comparable).
+    n = M * C * 2
+    comm.comm_stats.add("all_reduce", n, comm.bus_bytes("all_reduce", n, c.world))
+    return out
 
 
 

@@ -18,9 +18,11 @@ tensor_parallel.py:82-99, 232-243).  That makes "TP reproduces the single-GPU
 model" a testable statement and keeps checkpoints interchangeable.
 
 This module is the portable path (Gloo/CPU and any CUDA model that is not
-routed through the fused kernels).  On B200 the GPT model runs its
-tensor-parallel blocks through :mod:`minidist.parallel.tp_fused`, which fuses
-the ``g`` reduction into the row-parallel GEMM over NVLink peer memory.
+routed through the fused kernels).  On B200 the GPT model's tensor-parallel
+reductions run in peer-memory kernels of :mod:`minidist.parallel.collectives`
+(the ``g`` reduction fused into the row-parallel GEMM, the ``f`` reduction into
+the data-gradient GEMM, the embedding's ``g`` replaced by a gather from the
+owning rank's shard).
 """
 
 from __future__ import annotations

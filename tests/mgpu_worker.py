@@ -247,6 +247,202 @@ def check_graphs(rank, world):
     _graph_vs_eager(rank, world, lambda m, mesh: m, tp_size=world)
 
 
+def _rel(a, b) -> float:
+    return ((a.float() - b.float()).abs().max() / b.float().abs().max().clamp(min=1e-8)).item()
+
+
+def _report(name: str, err: float, tol: float, rank: int) -> None:
+    """One line per check for the summary table (rank 0), then the assertion."""
+    if rank == 0:
+        print(f"CHECK {name} max_rel_err={err:.3e} tol={tol:.0e} {'PASS' if err < tol else 'FAIL'}", flush=True)
+    assert err < tol, f"rank {rank} {name}: {err} >= {tol}"
+
+
+def _stage_model(cfg, mesh):
+    """This pipeline stage's slice of the GPT layers, with the fused LM-head loss on the last stage."""
+    import minidist as md
+    from torch import nn
+
+    from minidist.models import build_pipeline_layers
+
+    layers = build_pipeline_layers(cfg, tp_group=mesh.tp_group, device="cuda")
+    mine = md.partition_layers(layers, mesh.pp_size, mesh.pp_rank)
+    loss_fn = None
+    if mesh.is_last_stage:
+        head = mine[-1]
+        head.loss_only = True
+
+        def loss_fn(hidden, targets):
+            return head.loss(hidden, targets)
+    return nn.Sequential(*mine), loss_fn, len(layers)
+
+
+def _stage_param_names(mesh, n_layers):
+    """Names in the unwrapped GPT of this stage's parameters, in the order of ``nn.Sequential``."""
+    from minidist.pipeline import partition_layers
+
+    idx = partition_layers(list(range(n_layers)), mesh.pp_size, mesh.pp_rank)
+    names = []
+    for i in idx:
+        prefix = "embedding" if i == 0 else ("lm_head" if i == n_layers - 1 else f"blocks.{i - 1}")
+        names.append(prefix)
+    return idx, names
+
+
+def check_pipeline(rank, world):
+    """GPipe and 1F1B over ``world`` stages (NCCL send / recv, fused blocks) reproduce the single-stage
+    loss and every stage's parameter gradients (reference tests/test_pipeline.py:53-97)."""
+    import minidist as md
+    from minidist.models import GPT, GPTConfig
+
+    cfg = GPTConfig(vocab_size=1024, block_size=128, n_layer=2 * world, n_head=4, n_embd=256, seed=5)
+    g = torch.Generator().manual_seed(17)
+    ids = torch.randint(0, cfg.vocab_size, (8, 128), generator=g).cuda()
+    tgt = torch.randint(0, cfg.vocab_size, (8, 128), generator=g).cuda()
+    solo = md.ParallelMesh(tp_size=1, pp_size=1, dp_size=world)
+    ref = GPT(cfg, tp_group=solo.tp_group, device="cuda")
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        l_ref = ref(ids, tgt)[1]
+    l_ref.backward()
+    refp = dict(ref.named_parameters())
+    mesh = md.ParallelMesh(tp_size=1, pp_size=world)
+    for sched in ("gpipe", "1f1b"):
+        core, loss_fn, n_layers = _stage_model(cfg, mesh)
+        stage = md.PipelineStage(core, mesh, loss_fn=loss_fn)
+        schedule = md.build_schedule(sched, stage, mesh, 4)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = schedule.step(inputs=ids, targets=tgt)
+        torch.cuda.synchronize()
+        v = torch.zeros(1, device="cuda")
+        if loss is not None:
+            v[0] = loss
+        dist.broadcast(v, src=mesh.pp_ranks[-1], group=mesh.pp_group)
+        _report(f"pipeline_{sched}_w{world}_loss", abs(v.item() - l_ref.item()) / abs(l_ref.item()), 2e-2, rank)
+        worst = 0.0
+        _, prefixes = _stage_param_names(mesh, n_layers)
+        for mod, prefix in zip(core, prefixes):
+            for n, p in mod.named_parameters():
+                worst = max(worst, _rel(p.grad, refp[f"{prefix}.{n}"].grad))
+        _report(f"pipeline_{sched}_w{world}_grads", worst, 6e-2, rank)
+        if sched == "1f1b" and world > 1:
+            assert schedule.max_activations_in_flight <= world - mesh.pp_rank
+    nat.check_status()
+
+
+def check_composition(rank, world):
+    """tp2 x pp2 x dp(world/4): 1F1B with 4 microbatches per replica and DDP over the data-parallel
+    group vs the single-process full batch (reference tests/test_composition.py:62-157)."""
+    import minidist as md
+    from minidist.models import GPT, GPTConfig
+
+    if world % 4:
+        return
+    cfg = GPTConfig(vocab_size=1024, block_size=128, n_layer=4, n_head=8, n_embd=256, seed=6)
+    dp = world // 4
+    g = torch.Generator().manual_seed(23)
+    ids = torch.randint(0, cfg.vocab_size, (4 * dp, 128), generator=g).cuda()
+    tgt = torch.randint(0, cfg.vocab_size, (4 * dp, 128), generator=g).cuda()
+    solo = md.ParallelMesh(tp_size=1, pp_size=1, dp_size=world)
+    ref = GPT(cfg, tp_group=solo.tp_group, device="cuda")
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        l_ref = ref(ids, tgt)[1]
+    l_ref.backward()
+    refp = dict(ref.named_parameters())
+    mesh = md.ParallelMesh(tp_size=2, pp_size=2)
+    core, loss_fn, n_layers = _stage_model(cfg, mesh)
+    model = md.DistributedDataParallel(core, process_group=mesh.dp_group, bucket_cap_mb=1.0) if dp > 1 else core
+    stage = md.PipelineStage(model, mesh, loss_fn=loss_fn)
+    schedule = md.build_schedule("1f1b", stage, mesh, 4)
+    mine = slice(mesh.dp_rank * 4, (mesh.dp_rank + 1) * 4)
+    ctx = model.no_sync() if dp > 1 else torch.enable_grad()
+    with ctx, torch.autocast("cuda", dtype=torch.bfloat16):
+        loss = schedule.step(inputs=ids[mine], targets=tgt[mine])
+    if dp > 1:
+        model.finish_gradient_sync()
+    torch.cuda.synchronize()
+    v = torch.zeros(1, device="cuda")
+    if loss is not None:
+        v[0] = loss
+    dist.all_reduce(v, group=mesh.pp_group)  # only the last stage holds it
+    dist.all_reduce(v, group=mesh.dp_group)
+    v /= mesh.dp_size
+    _report(f"composition_tp2pp2dp{dp}_loss", abs(v.item() - l_ref.item()) / abs(l_ref.item()), 2e-2, rank)
+    # Every parameter's gradient is this rank's tensor-parallel slice of the reference gradient.
+    worst = 0.0
+    _, prefixes = _stage_param_names(mesh, n_layers)
+    for mod, prefix in zip(core, prefixes):
+        for n, p in mod.named_parameters():
+            full = refp[f"{prefix}.{n}"].grad
+            if p.shape != full.shape:
+                dim = next(d for d in range(p.dim()) if p.shape[d] != full.shape[d])
+                full = full.chunk(mesh.tp_size, dim=dim)[mesh.tp_rank]
+            worst = max(worst, _rel(p.grad, full))
+    _report(f"composition_tp2pp2dp{dp}_grads", worst, 6e-2, rank)
+    nat.check_status()
+
+
+def check_fsdp_training(rank, world):
+    """Four AdamW steps of FSDP with bf16 parameter gathers track DDP's weights
+    (reference tests/test_fsdp.py:92-127, 189-211)."""
+    import minidist as md
+    from minidist.models import GPT, Block, GPTConfig
+    from minidist.optim import FusedAdamW
+
+    cfg = GPTConfig(vocab_size=1024, block_size=128, n_layer=2, n_head=4, n_embd=256, seed=8)
+    mesh = md.ParallelMesh(tp_size=1)
+    ddp = md.DistributedDataParallel(GPT(cfg, tp_group=mesh.tp_group, device="cuda"), process_group=mesh.dp_group)
+    fsdp = md.FullyShardedDataParallel(GPT(cfg, tp_group=mesh.tp_group, device="cuda"), unit_types=(Block,),
+                                       process_group=mesh.dp_group,
+                                       mixed_precision=md.MixedPrecisionPolicy(param_dtype=torch.bfloat16))
+    o1 = FusedAdamW(ddp.parameters(), lr=1e-3)
+    o2 = FusedAdamW(fsdp.parameters(), lr=1e-3)
+    g = torch.Generator().manual_seed(31)
+    losses = []
+    for it in range(4):
+        ids = torch.randint(0, cfg.vocab_size, (2, 128), generator=g).cuda()
+        tgt = torch.randint(0, cfg.vocab_size, (2, 128), generator=g).cuda()
+        pair = []
+        for model, opt in ((ddp, o1), (fsdp, o2)):
+            opt.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = model(ids, tgt)[1]
+            loss.backward()
+            opt.step()
+            pair.append(loss.item())
+        losses.append(pair)
+    torch.cuda.synchronize()
+    _report(f"fsdp_vs_ddp_w{world}_losses", max(abs(a - b) / abs(a) for a, b in losses), 2e-2, rank)
+    worst = 0.0
+    with fsdp.summon_full_params():
+        for (n, p), (_, q) in zip(fsdp.module.named_parameters(), ddp.module.named_parameters()):
+            worst = max(worst, (p.float() - q.float()).abs().max().item())
+    _report(f"fsdp_vs_ddp_w{world}_weights_abs", worst, 2e-2, rank)
+    nat.check_status()
+
+
+def check_tp_embedding(rank, world):
+    """md_embed_tp: each row read from its owner's bf16 shard equals the masked-lookup + all-reduce."""
+    import minidist as md
+    from minidist.models import GPT, GPTConfig
+
+    cfg = GPTConfig(vocab_size=1024 * world, block_size=128, n_layer=1, n_head=8, n_embd=512, seed=4)
+    mesh = md.ParallelMesh(tp_size=world)
+    model = GPT(cfg, tp_group=mesh.tp_group, device="cuda")
+    g = torch.Generator().manual_seed(3)
+    ids = torch.randint(0, cfg.vocab_size, (4, 128), generator=g).cuda()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        x = model.embedding(ids)
+    emb = model.embedding
+    full = torch.empty(cfg.vocab_size, cfg.n_embd, device="cuda")
+    dist.all_gather_into_tensor(full, emb.wte.weight.detach(), group=mesh.tp_group)
+    want = (full.bfloat16().float()[ids] + emb.wpe.detach().bfloat16().float()[:128]).bfloat16()
+    _report(f"tp_embedding_w{world}", _rel(x, want), 1e-2, rank)
+    allx = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(allx, x.contiguous())
+    assert all(torch.equal(allx[0], a) for a in allx), "embedding differs across TP ranks"
+    nat.check_status()
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
@@ -257,7 +453,11 @@ def main():
         check_ddp(rank, world)
         check_fsdp(rank, world)
         check_tp_gpt(rank, world)
+        check_tp_embedding(rank, world)
         check_graphs(rank, world)
+        check_pipeline(rank, world)
+        check_composition(rank, world)
+        check_fsdp_training(rank, world)
     finally:
         symm.release_all()
         dist.barrier()

@@ -1,5 +1,6 @@
-"""Multi-GPU tier: peer-memory collectives, the fused GEMM + all-reduce, DDP and tensor-parallel
-GPT on 2+ GPUs (skipped with fewer GPUs).
+"""Multi-GPU tier on 2, 4 and 8 GPUs (skipped with fewer): peer-memory collectives, the fused GEMM +
+all-reduce, DDP, FSDP (gradients and four training steps against DDP), tensor-parallel GPT and its
+embedding gather, CUDA-graph replay, GPipe / 1F1B pipelines and tp2 x pp2 x dp composition.
 
 Each test launches ``torchrun`` with one process per GPU (NCCL, 127.0.0.1) on a
 worker script in this directory and checks its exit code; the workers assert
@@ -41,3 +42,8 @@ def test_peer_allreduce_and_ddp_2gpu():
 @pytest.mark.skipif(_ngpus() < 4, reason="needs 4 GPUs")
 def test_peer_allreduce_and_ddp_4gpu():
     _torchrun("mgpu_worker.py", 4)
+
+
+@pytest.mark.skipif(_ngpus() < 8, reason="needs 8 GPUs")
+def test_peer_allreduce_and_ddp_8gpu():
+    _torchrun("mgpu_worker.py", 8, timeout=600)
