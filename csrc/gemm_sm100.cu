@@ -650,6 +650,12 @@ __device__ __forceinline__ void epilogue_row(const MdGemmParams& p, const CUtens
   }
 }
 
+// Peer-wait counters of the fused all-reduce (analysis; off unless
+// md_gemm_ar_wait_enable(1)): {CTA run ns, comm-warp ns spent waiting on peer
+// flags, launches}.
+__device__ int g_gar_pw_on;
+__device__ unsigned long long g_gar_pw[3];
+
 // Analysis trace of the fused all-reduce: CTA 0 stamps %globaltimer at its
 // hand-offs (no-op unless a trace buffer is passed).
 #define MD_AR_TRACE(ar, idx, slot)                                                          \
@@ -763,8 +769,10 @@ __device__ __forceinline__ void ar_reduce_rows(const MdGemmParams& p, const MdTp
 __device__ __forceinline__ bool ar_reduce_chunk(const MdGemmParams& p, const MdTpArParams& ar, unsigned epoch, int chunk,
                                                 int row0, int col0, int lane, volatile int* abort_flag) {
   bool ok = true;
+  const uint64_t tw = g_gar_pw_on ? globaltimer_ns() : 0ull;
   if (lane < ar.world) ok = flag_wait_ge(ar.flags[lane] + chunk, epoch, ar, p.status, 60, abort_flag);
   if (__any_sync(0xFFFFFFFFu, !ok)) return false;
+  if (tw != 0ull && lane == 0) atomicAdd(&g_gar_pw[1], globaltimer_ns() - tw);
   acquire_fence();  // every lane's loads below follow the lanes' observations (ordered by the vote)
   const int col = col0 + lane * 8;
   if (col < p.N) {
@@ -793,8 +801,13 @@ __device__ __forceinline__ int ar_pull_chunk(const MdGemmParams& p, const MdTpAr
   const unsigned* f = ar.flags[owner] + ar.max_chunks + chunk;
   int ready = 0;
   if (lane == 0) {
-    if (blocking) ready = flag_wait_ge(f, epoch, ar, p.status, 61, abort_flag) ? 1 : -1;
-    else ready = flag_acquire_sys(f) >= epoch ? 1 : 0;
+    if (blocking) {
+      const uint64_t tw = g_gar_pw_on ? globaltimer_ns() : 0ull;
+      ready = flag_wait_ge(f, epoch, ar, p.status, 61, abort_flag) ? 1 : -1;
+      if (tw != 0ull) atomicAdd(&g_gar_pw[1], globaltimer_ns() - tw);
+    } else {
+      ready = flag_acquire_sys(f) >= epoch ? 1 : 0;
+    }
   }
   ready = __shfl_sync(0xFFFFFFFFu, ready, 0);
   if (ready == 1) acquire_fence();  // every lane's loads below follow the observation
@@ -852,6 +865,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
   const MdGemmParams& p = kp.p;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint64_t t_entry = (AR && threadIdx.x == 0 && g_gar_pw_on) ? globaltimer_ns() : 0ull;
   const uint32_t crank = CG == 2 ? cluster_ctarank() : 0u;
   const bool leader = crank == 0;
   int cluster_id = CG == 2 ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
@@ -1180,12 +1194,14 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap& tmA, const CUtensor
     else tmem_dealloc(tmem_base, kTmemCols);
   }
   if constexpr (AR) {
+    if (t_entry != 0ull) atomicAdd(&g_gar_pw[0], globaltimer_ns() - t_entry);
     // The launch's last cluster resets the counters for the next launch.
     if (kp.ar.claim != nullptr && leader && threadIdx.x == 0 &&
         atomicAdd(kp.ar.claim + 1, 1u) == static_cast<unsigned>(nclusters - 1)) {
       atomicExch(kp.ar.claim + 2, ar_epoch);
       atomicExch(kp.ar.claim, 0u);
       atomicExch(kp.ar.claim + 1, 0u);
+      if (t_entry != 0ull) atomicAdd(&g_gar_pw[2], 1ull);
     }
   }
 }
@@ -1541,6 +1557,21 @@ extern "C" int md_gemm_ar(const MdGemmParams* prm, const MdTpArParams* arp, cuda
     e = cg == 2 ? launch<2, 4, false, false, kEpiBF16, true>(ta, tb, td, td, kp, grid, stream)
                 : launch<1, 4, false, false, kEpiBF16, true>(ta, tb, td, td, kp, grid, stream);
   return static_cast<int>(e);
+}
+
+// Peer-wait counters of md_gemm_ar: on != 0 turns counting on for the current
+// device; reset != 0 zeroes them first.  md_gemm_ar_wait_read copies
+// {run_ns, wait_ns, launches} to host memory.  Host-synchronous (analysis only).
+extern "C" int md_gemm_ar_wait_enable(int on, int reset) {
+  if (reset) {
+    unsigned long long zero[3] = {0ull, 0ull, 0ull};
+    cudaError_t e = cudaMemcpyToSymbol(md::gemm::g_gar_pw, zero, sizeof(zero));
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  return static_cast<int>(cudaMemcpyToSymbol(md::gemm::g_gar_pw_on, &on, sizeof(int)));
+}
+extern "C" int md_gemm_ar_wait_read(unsigned long long* out) {
+  return static_cast<int>(cudaMemcpyFromSymbol(out, md::gemm::g_gar_pw, sizeof(md::gemm::g_gar_pw)));
 }
 
 // Analysis: allocate (enable=1) / free (enable=0) the md_gemm_ar trace buffer;

@@ -44,6 +44,11 @@ constexpr int kMaxCtas = 160;     // flag slots per channel (one CTA per SM for 
 constexpr int kArMaxCtas = 64;    // bucket all-reduce: leaves SMs to the backward it overlaps
 constexpr int kChannels = 8;
 
+// Peer-wait counters (analysis; off unless md_peer_wait_enable(1)): per
+// channel, {CTA run ns, CTA ns spent in cross-rank barriers, launches}.
+__device__ int g_pw_on;
+__device__ unsigned long long g_pw[kChannels][3];
+
 }  // namespace symm
 }  // namespace md
 
@@ -185,12 +190,15 @@ __device__ __forceinline__ uint32_t* vcta_counter(const P& p) {
 struct VCta {
   int v;
   uint32_t epoch;
+  uint64_t t0;  // %globaltimer at entry when the peer-wait counters are on, else 0
 };
 template <typename P>
 __device__ VCta vcta_claim(const P& p) {
   __shared__ int v_sh;
   __shared__ uint32_t e_sh;
+  __shared__ uint64_t t_sh;
   if (threadIdx.x == 0) {
+    t_sh = g_pw_on ? globaltimer_ns() : 0ull;
     uint32_t* c = vcta_counter(p);
     const uint32_t v = atomicAdd(c, 1u);
     v_sh = v < gridDim.x ? static_cast<int>(v) : -1;
@@ -198,21 +206,24 @@ __device__ VCta vcta_claim(const P& p) {
     e_sh = *reinterpret_cast<volatile uint32_t*>(c + 2) + 1u;
   }
   __syncthreads();
-  return VCta{v_sh, e_sh};
+  return VCta{v_sh, e_sh, t_sh};
 }
 
 // Every CTA calls this once on every exit path; the launch's last CTA records
 // the epoch and resets the claim counters for the next launch on this channel
 // (stream-ordered after it).
 template <typename P>
-__device__ void vcta_release(const P& p, uint32_t epoch) {
+__device__ void vcta_release(const P& p, const VCta& vct) {
   __syncthreads();
   if (threadIdx.x == 0) {
+    const bool counting = vct.t0 != 0ull;
+    if (counting) atomicAdd(&g_pw[p.channel][0], globaltimer_ns() - vct.t0);
     uint32_t* c = vcta_counter(p);
     if (atomicAdd(c + 1, 1u) == gridDim.x - 1) {
-      atomicExch(c + 2, epoch);
+      atomicExch(c + 2, vct.epoch);
       atomicExch(c, 0u);
       atomicExch(c + 1, 0u);
+      if (counting) atomicAdd(&g_pw[p.channel][2], 1ull);
     }
   }
 }
@@ -222,7 +233,11 @@ __device__ void vcta_release(const P& p, uint32_t epoch) {
 template <typename P>
 __device__ bool cta_barrier(const P& p, int v, uint32_t value, uint32_t where) {
   __shared__ int ok_sh;
-  if (threadIdx.x == 0) ok_sh = 1;
+  __shared__ uint64_t tw_sh;
+  if (threadIdx.x == 0) {
+    ok_sh = 1;
+    tw_sh = g_pw_on ? globaltimer_ns() : 0ull;
+  }
   __syncthreads();
   const int peer = threadIdx.x;
   if (peer < p.world) {
@@ -241,6 +256,7 @@ __device__ bool cta_barrier(const P& p, int v, uint32_t value, uint32_t where) {
     }
   }
   __syncthreads();
+  if (threadIdx.x == 0 && tw_sh != 0ull) atomicAdd(&g_pw[p.channel][1], globaltimer_ns() - tw_sh);
   return ok_sh != 0;
 }
 
@@ -302,7 +318,7 @@ __global__ void __launch_bounds__(512) md_ar_bucket_kernel(const __grid_constant
   }
   cta_barrier(p, vc, depart, 101);
   }
-  vcta_release(p, vct.epoch);
+  vcta_release(p, vct);
 }
 
 __global__ void __launch_bounds__(512) md_rs_shard_kernel(const __grid_constant__ MdRsParams p) {
@@ -381,7 +397,7 @@ __global__ void __launch_bounds__(512) md_rs_shard_kernel(const __grid_constant_
   // No rank rewrites its gradient buffer before every peer has read it.
   cta_barrier(p, vc, depart, 111);
   }
-  vcta_release(p, vct.epoch);
+  vcta_release(p, vct);
 }
 
 __global__ void __launch_bounds__(512) md_ag_shards_kernel(const __grid_constant__ MdAgParams p) {
@@ -417,7 +433,7 @@ __global__ void __launch_bounds__(512) md_ag_shards_kernel(const __grid_constant
   }
   cta_barrier(p, vc, depart, 121);
   }
-  vcta_release(p, vct.epoch);
+  vcta_release(p, vct);
 }
 
 __global__ void __launch_bounds__(256) md_ce_tp_kernel(const __grid_constant__ MdCeTpParams p) {
@@ -465,7 +481,7 @@ __global__ void __launch_bounds__(256) md_ce_tp_kernel(const __grid_constant__ M
       cta_barrier(p, vc, depart, 131);
     }
   }
-  vcta_release(p, vct.epoch);
+  vcta_release(p, vct);
 }
 
 // One warp per token row, each lane moving 16 bytes per vector with up to 8
@@ -515,7 +531,7 @@ __global__ void __launch_bounds__(256) md_embed_tp_kernel(const __grid_constant_
     }
     cta_barrier(p, vc, depart, 141);
   }
-  vcta_release(p, vct.epoch);
+  vcta_release(p, vct);
 }
 
 }  // namespace symm
@@ -564,6 +580,22 @@ int md_rs_shard(const MdRsParams* prm, int ctas, cudaStream_t s) {
   return static_cast<int>(cudaGetLastError());
 }
 
+
+// Peer-wait counters: on != 0 turns counting on (off otherwise) for the current
+// device; reset != 0 zeroes the counters first.  Host-synchronous (analysis only).
+int md_peer_wait_enable(int on, int reset) {
+  if (reset) {
+    unsigned long long zero[md::symm::kChannels][3] = {};
+    cudaError_t e = cudaMemcpyToSymbol(md::symm::g_pw, zero, sizeof(zero));
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  return static_cast<int>(cudaMemcpyToSymbol(md::symm::g_pw_on, &on, sizeof(int)));
+}
+
+// Copy the counters ([channel][run_ns, wait_ns, launches], 8 x 3) to host memory.
+int md_peer_wait_read(unsigned long long* out) {
+  return static_cast<int>(cudaMemcpyFromSymbol(out, md::symm::g_pw, sizeof(md::symm::g_pw)));
+}
 
 int md_symm_max_world() { return md::symm::kMaxWorld; }
 long long md_symm_flag_bytes() {

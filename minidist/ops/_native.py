@@ -214,3 +214,40 @@ def env_flag(name: str, default: bool = False) -> bool:
     if v is None:
         return default
     return v not in ("0", "", "false", "False", "no")
+
+
+declare("md_peer_wait_enable", "i:ii")
+declare("md_peer_wait_read", "i:p")
+declare("md_gemm_ar_wait_enable", "i:ii")
+declare("md_gemm_ar_wait_read", "i:p")
+
+# Channel of each peer-memory kernel family (minidist.parallel.collectives).
+_PEER_WAIT_FAMILIES = {0: "md_ar_bucket", 1: "md_ar_bucket", 2: "md_ar_bucket", 3: "md_ar_bucket",
+                       4: "md_rs_shard", 5: "md_ag_shards", 6: "md_ce_tp", 7: "md_embed_tp"}
+
+
+def peer_wait_counters(enable: bool, reset: bool = False) -> dict[str, dict[str, float]]:
+    """Turn the fused kernels' device-side wait counters on or off for the current device and
+    return what they hold: ``{family: {"run_ms", "wait_ms", "wait_frac", "launches"}}`` with
+    times summed over CTAs (``wait`` = time in cross-rank barriers / peer-flag polls).  Host-
+    synchronous; for analysis runs (``minidist.profiling.PeerWaitCounters``), not inside a
+    CUDA-graph capture."""
+    h = lib()
+    raw = (ctypes.c_ulonglong * 24)()
+    check(h.md_peer_wait_read(ctypes.cast(raw, ctypes.c_void_p)), "md_peer_wait_read")
+    gar = (ctypes.c_ulonglong * 3)()
+    check(h.md_gemm_ar_wait_read(ctypes.cast(gar, ctypes.c_void_p)), "md_gemm_ar_wait_read")
+    check(h.md_peer_wait_enable(int(enable), int(reset)), "md_peer_wait_enable")
+    check(h.md_gemm_ar_wait_enable(int(enable), int(reset)), "md_gemm_ar_wait_enable")
+    acc: dict[str, list[float]] = {}
+    for ch, fam in _PEER_WAIT_FAMILIES.items():
+        run, wait, n = raw[3 * ch], raw[3 * ch + 1], raw[3 * ch + 2]
+        if run or n:
+            a = acc.setdefault(fam, [0.0, 0.0, 0.0])
+            a[0] += run
+            a[1] += wait
+            a[2] += n
+    if gar[0] or gar[2]:
+        acc["md_gemm_ar"] = [float(gar[0]), float(gar[1]), float(gar[2])]
+    return {fam: {"run_ms": a[0] / 1e6, "wait_ms": a[1] / 1e6, "wait_frac": a[1] / a[0] if a[0] else 0.0,
+                  "launches": a[2]} for fam, a in acc.items()}
