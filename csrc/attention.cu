@@ -660,7 +660,7 @@ int md_attn_bwd_tc(const void* qkv, long long ldq, const void* out, long long ld
   if (B <= 0 || H <= 0 || S <= 0 || !al16(qkv) || !al16(out) || !al16(dout) || !al16(dqkv) || (ldq % 8) ||
       (ldo % 8) || (lddo % 8) || (lddq % 8))
     return -1;
-  if (D != 64) return -2;
+  if (D != 64 && D != 80 && D != 128) return -2;
   const long long rows = static_cast<long long>(B) * S;
   cudaError_t e = cudaMemsetAsync(dqacc, 0, rows * H * D * sizeof(float), st);
   if (e != cudaSuccess) return static_cast<int>(e);
@@ -668,18 +668,27 @@ int md_attn_bwd_tc(const void* qkv, long long ldq, const void* out, long long ld
   int g1 = static_cast<int>((nd + 255) / 256);
   if (g1 > 148 * 32) g1 = 148 * 32;
   // out == null: delta was produced upstream (the epilogue of the GEMM that made dout).
-  if (out != nullptr)
-    md::launch_pdl(md::attn::delta_kernel<64>, dim3(g1), dim3(256), 0, st, reinterpret_cast<const __nv_bfloat16*>(out), ldo,
-        reinterpret_cast<const __nv_bfloat16*>(dout), lddo, delta, B, H, S);
+  if (out != nullptr) {
+    const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(out);
+    const __nv_bfloat16* d = reinterpret_cast<const __nv_bfloat16*>(dout);
+    if (D == 64) md::launch_pdl(md::attn::delta_kernel<64>, dim3(g1), dim3(256), 0, st, o, ldo, d, lddo, delta, B, H, S);
+    if (D == 80) md::launch_pdl(md::attn::delta_kernel<80>, dim3(g1), dim3(256), 0, st, o, ldo, d, lddo, delta, B, H, S);
+    if (D == 128) md::launch_pdl(md::attn::delta_kernel<128>, dim3(g1), dim3(256), 0, st, o, ldo, d, lddo, delta, B, H, S);
+  }
   int rc = md_attn_bwd_tc_main(qkv, ldq, dout, lddo, lse, delta, dqacc, static_cast<long long>(H) * D, dqkv, lddq, B,
                                H, S, D, scale, status, st);
   if (rc != 0) return rc;
-  const long long nq = rows * H * (64 / 2);
+  const long long nq = rows * H * (D / 8);
   int g2 = static_cast<int>((nq + 255) / 256);
   if (g2 > 148 * 32) g2 = 148 * 32;
-  md::launch_pdl(md::attn::dq_convert_kernel<64>, dim3(g2), dim3(256), 0, st, dqacc, static_cast<long long>(H) * 64,
-      reinterpret_cast<__nv_bfloat16*>(dqkv), lddq,
-      static_cast<int>(rows), H, scale);
+  __nv_bfloat16* dq = reinterpret_cast<__nv_bfloat16*>(dqkv);
+  const long long lda = static_cast<long long>(H) * D;
+  if (D == 64)
+    md::launch_pdl(md::attn::dq_convert_kernel<64>, dim3(g2), dim3(256), 0, st, dqacc, lda, dq, lddq, static_cast<int>(rows), H, scale);
+  if (D == 80)
+    md::launch_pdl(md::attn::dq_convert_kernel<80>, dim3(g2), dim3(256), 0, st, dqacc, lda, dq, lddq, static_cast<int>(rows), H, scale);
+  if (D == 128)
+    md::launch_pdl(md::attn::dq_convert_kernel<128>, dim3(g2), dim3(256), 0, st, dqacc, lda, dq, lddq, static_cast<int>(rows), H, scale);
   return static_cast<int>(cudaGetLastError());
 }
 

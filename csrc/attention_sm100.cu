@@ -958,6 +958,477 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
 
+
+// ===========================================================================
+// Backward, head_dim 128 (and 80 on zero-padded boxes)
+//
+// The head_dim 64 layout needs S^T, dP^T (128 queries each), dK, dV and dQ
+// accumulators = 256 + 3 D TMEM columns, 640 at D = 128 (512 exist).  This
+// kernel walks each 128-key tile's queries in blocks of 64 and computes dQ
+// transposed, dQ^T = K^T dS^T (M = D = 128 rows, N = 64 queries), so
+//   S^T 64 | dP^T 64 | dQ^T 64 | (64 spare) | dK 128 | dV 128  = 512 columns.
+// Per 64-query block i of key tile kt:
+//   S^T  = K Q_i^T,  dP^T = V dO_i^T                 (M 128 keys, N 64)
+//   P^T  = exp(S^T scale - lse_i),  dS^T = P^T (dP^T - delta_i)   [compute warps, bf16 to smem]
+//   dK  += dS^T Q_i,  dV += P^T dO_i                 (M 128 keys, N D, K 64)
+//   dQ_i^T = K^T dS^T                                (M D, N 64, K 128 keys; both operands MN-major)
+// Roles as in the head_dim 64 kernel: warp 0 TMA, warp 1 MMA, warps 2..9
+// compute (thread = key row; warps 2..5 take query columns 0..31 of the
+// block, 6..9 columns 32..63), warps 10..13 drain dQ^T (thread = head-dim
+// row) into a dedicated fp32 staging tile [64 queries][128] (four 128B-
+// swizzled boxes of 32 columns) and one bulk tensor reduce-add per box into
+// the fp32 accumulator.  Two Q/dO stages (the smem budget), P^T double-
+// buffered, dS^T single-buffered; the next block's score products are queued
+// as soon as the compute warps hold the current scores in registers.
+// Real head_dim dr <= 128: every tensor map is 4-D [B, S, slots, dr], so
+// boxes read zeros past dr and the dQ reduce-add clips there; only dr
+// columns of dK / dV are stored.
+// ===========================================================================
+struct Bwd128Cfg {
+  static constexpr int D = 128;
+  static constexpr int kBQ = 64;                              // queries per block
+  static constexpr int kKTile = 128 * D * 2;                  // K or V tile: 2 chunks [128][64]
+  static constexpr int kQTile = kBQ * D * 2;                  // Q or dO tile: 2 chunks [64][64]
+  static constexpr int kQChunk = kBQ * 128;                   // 8 KB
+  static constexpr int kQStages = 2;
+  static constexpr int kPBytes = 128 * kBQ * 2;               // P^T / dS^T [128 keys][64 queries]
+  static constexpr int kStgBytes = kBQ * D * 4;               // dQ staging, 4 boxes [64][32] fp32
+  static constexpr int kSmemData = 2 * kKTile + 2 * kQStages * kQTile + 3 * kPBytes + kStgBytes + 2 * 2 * kBQ * 4;
+  static constexpr int kSmemBytes = kSmemData + 256;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kColS = 0, kColDP = 64, kColDQ = 128, kColDK = 256, kColDV = 384;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+struct Bwd128Params {
+  const float* lse;    // [B, H, S] natural log
+  const float* delta;  // [B, H, S]
+  void* dqkv;          // [B*S, lddq] bf16 interleaved [H, 3, dr]
+  long long lddq;
+  int B, H, S;
+  int n_kt;            // 128-key tiles per sequence
+  int n_qb;            // 64-query blocks per sequence
+  int items;
+  int dr;              // real head dim (128 or 80)
+  float scale, scale_log2;
+  Status* status;
+};
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    bwd128_kernel(const __grid_constant__ CUtensorMap tmKV, const __grid_constant__ CUtensorMap tmQ,
+                  const __grid_constant__ CUtensorMap tmDO, const __grid_constant__ CUtensorMap tmDQ,
+                  const __grid_constant__ Bwd128Params p) {
+  using C = Bwd128Cfg;
+  constexpr int D = C::D;
+  constexpr int QS = C::kQStages;
+  constexpr int BQ = C::kBQ;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if ((smem_u32(smem_raw) & 1023u) != 0u) {  // uniform across the CTA
+    if (threadIdx.x == 0) report(p.status, kBadArgument, 159, smem_u32(smem_raw));
+    return;
+  }
+  uint8_t* sK = smem_raw;
+  uint8_t* sV = sK + C::kKTile;
+  uint8_t* sQ = sV + C::kKTile;                  // [QS]
+  uint8_t* sdO = sQ + QS * C::kQTile;            // [QS]
+  uint8_t* sPt = sdO + QS * C::kQTile;           // [2] P^T
+  uint8_t* sdSt = sPt + 2 * C::kPBytes;          // dS^T
+  uint8_t* sStg = sdSt + C::kPBytes;             // dQ staging (fp32)
+  float* sL = reinterpret_cast<float*>(sStg + C::kStgBytes);  // [2][64] lse (log2 units)
+  float* sDel = sL + 2 * BQ;                                    // [2][64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 2 * BQ);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* kv_empty = bars + 1;
+  uint64_t* qd_full = bars + 2;    // [2]
+  uint64_t* qd_empty = bars + 4;   // [2]
+  uint64_t* sd_full = bars + 6;
+  uint64_t* sd_free = bars + 7;
+  uint64_t* pds_full = bars + 8;
+  uint64_t* p_free = bars + 9;     // [2] dV done reading P^T buffer
+  uint64_t* ds_free = bars + 11;   // dK and dQ^T done reading dS^T
+  uint64_t* dq_full = bars + 12;
+  uint64_t* dq_free = bars + 13;
+  uint64_t* dkv_free = bars + 14;
+  uint64_t* drain = bars + 15;
+  uint64_t* stage_bar = bars + 16;  // [2]
+  uint64_t* stg_free = bars + 18;   // staging tile read by the bulk reduce-adds
+  uint64_t* dq_staged = bars + 19;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 21);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int bhc = p.B * p.H;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
+    for (int i = 0; i < QS; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
+    mbar_init(sd_full, 1);
+    mbar_init(sd_free, kBwdCompute);
+    mbar_init(pds_full, kBwdCompute);
+    mbar_init(&p_free[0], 1);
+    mbar_init(&p_free[1], 1);
+    mbar_init(ds_free, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(dkv_free, kBwdCompute);
+    mbar_init(drain, 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&stage_bar[i], kBwdCompute);
+    mbar_init(stg_free, 1);
+    mbar_init(dq_staged, 4);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmKV);
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmDO);
+    tma_prefetch_desc(&tmDQ);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA producer
+    int kv_armed = -1;
+    int q_armed[QS];
+    for (int i = 0; i < QS; ++i) q_armed[i] = -1;
+    int g = 0, t = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
+      const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
+      const uint32_t tph = static_cast<uint32_t>(t) & 1u;
+      if (!mbar_wait(kv_empty, tph ^ 1u, p.status, 160, abort_flag)) break;
+      mbar_arrive_expect_tx(kv_full, 2 * C::kKTile);
+      kv_armed = static_cast<int>(tph);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        tma_load_4d(&tmKV, kv_full, sK + c * 16384, c * 64, 3 * h + 1, kt * 128, b);
+        tma_load_4d(&tmKV, kv_full, sV + c * 16384, c * 64, 3 * h + 2, kt * 128, b);
+      }
+      for (int i = 2 * kt; i < p.n_qb; ++i, ++g) {
+        const int st = g % QS;
+        const uint32_t ph = static_cast<uint32_t>(g / QS) & 1u;
+        if (!mbar_wait(&qd_empty[st], ph ^ 1u, p.status, 161, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&qd_full[st], 2 * C::kQTile);
+        q_armed[st] = static_cast<int>(ph);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tma_load_4d(&tmQ, &qd_full[st], sQ + st * C::kQTile + c * C::kQChunk, c * 64, 3 * h, i * BQ, b);
+          tma_load_4d(&tmDO, &qd_full[st], sdO + st * C::kQTile + c * C::kQChunk, c * 64, h, i * BQ, b);
+        }
+      }
+    }
+    if (kv_armed >= 0) mbar_wait(kv_full, static_cast<uint32_t>(kv_armed), p.status, 162, nullptr);
+    for (int i = 0; i < QS; ++i)
+      if (q_armed[i] >= 0) mbar_wait(&qd_full[i], static_cast<uint32_t>(q_armed[i]), p.status, 163, nullptr);
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (whole warp, elected lane issues)
+    constexpr uint32_t idS = idesc_bf16_f32(128, BQ, false, false);  // S^T, dP^T
+    constexpr uint32_t idKV = idesc_bf16_f32(128, D, false, true);   // dK, dV: B (Q, dO) MN-major
+    constexpr uint32_t idQT = idesc_bf16_f32(D, BQ, true, true);     // dQ^T: A (K^T), B (dS^T) MN-major
+    const uint64_t dK_k = sdesc_sw128(smem_u32(sK), 16, 1024);
+    const uint64_t dK_mn = sdesc_sw128(smem_u32(sK), 16384, 1024);
+    const uint64_t dV_k = sdesc_sw128(smem_u32(sV), 16, 1024);
+    const uint64_t dQ_k = sdesc_sw128(smem_u32(sQ), 16, 1024);
+    const uint64_t dQ_mn = sdesc_sw128(smem_u32(sQ), C::kQChunk, 1024);
+    const uint64_t ddO_k = sdesc_sw128(smem_u32(sdO), 16, 1024);
+    const uint64_t ddO_mn = sdesc_sw128(smem_u32(sdO), C::kQChunk, 1024);
+    const uint64_t dP_k = sdesc_sw128(smem_u32(sPt), 16, 1024);
+    const uint64_t ddS_k = sdesc_sw128(smem_u32(sdSt), 16, 1024);
+    const uint64_t ddS_mn = sdesc_sw128(smem_u32(sdSt), 16384, 1024);
+    constexpr uint32_t kQT16 = C::kQTile >> 4;
+    constexpr uint32_t kP16 = C::kPBytes >> 4;
+    int g = 0, t = 0;
+    bool ok = true;
+    auto issue_scores = [&](int gg) -> bool {
+      const int st = gg % QS;
+      if (!mbar_wait(&qd_full[st], static_cast<uint32_t>(gg / QS) & 1u, p.status, 170, abort_flag) ||
+          !mbar_wait(sd_free, (static_cast<uint32_t>(gg) & 1u) ^ 1u, p.status, 171, abort_flag))
+        return false;
+      tc_fence_after();
+      const uint64_t q0 = dQ_k + st * kQT16, o0 = ddO_k + st * kQT16;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t offk = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+        const uint32_t offq = ((kk >> 2) * C::kQChunk + (kk & 3) * 32) >> 4;
+        umma_bf16_ss_elect(tmem + C::kColS, dK_k + offk, q0 + offq, idS, kk > 0 ? 1u : 0u);
+        umma_bf16_ss_elect(tmem + C::kColDP, dV_k + offk, o0 + offq, idS, kk > 0 ? 1u : 0u);
+      }
+      umma_commit_elect(sd_full);
+      return true;
+    };
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
+      const int kt = w / bhc;
+      const int n = p.n_qb - 2 * kt;
+      if (!mbar_wait(kv_full, static_cast<uint32_t>(t) & 1u, p.status, 172, abort_flag)) break;
+      if (!issue_scores(g)) break;
+      for (int u = 0; u < n; ++u, ++g) {
+        const int st = g % QS;
+        const int pb = g & 1;
+        if (u + 1 < n && !issue_scores(g + 1)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(pds_full, static_cast<uint32_t>(g) & 1u, p.status, 173, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (u == 0 && !mbar_wait(dkv_free, (static_cast<uint32_t>(t) & 1u) ^ 1u, p.status, 174, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t qmn = dQ_mn + st * kQT16, omn = ddO_mn + st * kQT16;
+        const uint64_t pk = dP_k + pb * kP16;
+        const uint32_t acc0 = u > 0 ? 1u : 0u;
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)
+          umma_bf16_ss_elect(tmem + C::kColDK, ddS_k + ((kk * 32) >> 4), qmn + kk * 128, idKV, (acc0 | kk) ? 1u : 0u);
+        if (!mbar_wait(dq_free, (static_cast<uint32_t>(g) & 1u) ^ 1u, p.status, 175, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 128 / 16; ++kk)
+          umma_bf16_ss_elect(tmem + C::kColDQ, dK_mn + kk * 128, ddS_mn + kk * 128, idQT, kk > 0 ? 1u : 0u);
+        umma_commit_elect(ds_free);
+        umma_commit_elect(dq_full);
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)
+          umma_bf16_ss_elect(tmem + C::kColDV, pk + ((kk * 32) >> 4), omn + kk * 128, idKV, (acc0 | kk) ? 1u : 0u);
+        umma_commit_elect(&qd_empty[st]);
+        umma_commit_elect(&p_free[pb]);
+      }
+      if (!ok) break;
+      umma_commit_elect(kv_empty);
+    }
+    umma_commit_elect(drain);
+    mbar_wait(drain, 0, p.status, 176, nullptr);
+  } else if (warp >= 2 && warp < 2 + kBwdCompute) {
+    // ------------------------------------------------------------ compute (thread = key row)
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;  // query columns [32*half, 32*half + 32) of the block
+    const int krow = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int ct = threadIdx.x - 64;  // 0..255: 0..63 stage lse, 64..127 delta
+    auto load_raw = [&](int w_, int i_) -> float {
+      const int q = min(i_ * BQ + (ct & 63), p.S - 1);
+      const long long idx = static_cast<long long>(w_ % bhc) * p.S + q;
+      return ct < 64 ? p.lse[idx] : (ct < 128 ? p.delta[idx] : 0.f);
+    };
+    auto stage = [&](int gg, int i_, float raw) {
+      if (ct < 128) {
+        const int q = i_ * BQ + (ct & 63);
+        const float v = ct < 64 ? (q < p.S ? raw * 1.4426950408889634f : INFINITY) : (q < p.S ? raw : 0.f);
+        (ct < 64 ? sL : sDel)[(gg & 1) * BQ + (ct & 63)] = v;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&stage_bar[gg & 1]);
+    };
+    auto next_block = [&](int w_, int i_, int& wn, int& in) {
+      if (i_ + 1 < p.n_qb) {
+        wn = w_;
+        in = i_ + 1;
+      } else if (w_ + static_cast<int>(gridDim.x) < p.items) {
+        wn = w_ + static_cast<int>(gridDim.x);
+        in = 2 * (wn / bhc);
+      } else {
+        wn = -1;
+      }
+    };
+    float pre = 0.f;
+    int pre_w = -1, pre_i = 0;
+    if (static_cast<int>(blockIdx.x) < p.items) {
+      const int i0 = 2 * (static_cast<int>(blockIdx.x) / bhc);
+      stage(0, i0, load_raw(blockIdx.x, i0));
+      next_block(blockIdx.x, i0, pre_w, pre_i);
+      if (pre_w >= 0) pre = load_raw(pre_w, pre_i);
+    }
+    int g = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x) {
+      const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
+      const int n = p.n_qb - 2 * kt;
+      for (int u = 0; u < n; ++u, ++g) {
+        if (!mbar_wait(&stage_bar[g & 1], static_cast<uint32_t>(g >> 1) & 1u, p.status, 179, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const float* L = sL + (g & 1) * BQ + half * 32;
+        const float* Dl = sDel + (g & 1) * BQ + half * 32;
+        if (!mbar_wait(sd_full, static_cast<uint32_t>(g) & 1u, p.status, 180, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sv[32], dv[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + C::kColS + static_cast<uint32_t>(half * 32), sv);
+        tmem_ld_32x32b_x32(tmem + lane_base + C::kColDP + static_cast<uint32_t>(half * 32), dv);
+        tmem_ld_wait();
+        // S^T and dP^T in registers: the next block's score products may overwrite them.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sd_free);
+        // Diagonal: query q_abs < key k_abs is masked; only the first two blocks can hold such pairs.
+        const int qoff = (2 * kt + u) * BQ + half * 32 - (kt * 128 + krow);  // q_abs - k_abs at column 0
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float p0 = ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -L[e]));
+          float p1 = ex2(fmaf(__uint_as_float(sv[e + 1]), p.scale_log2, -L[e + 1]));
+          if (u < 2) {
+            if (qoff + e < 0) p0 = 0.f;
+            if (qoff + e + 1 < 0) p1 = 0.f;
+          }
+          const float g0 = p0 * (__uint_as_float(dv[e]) - Dl[e]);
+          const float g1 = p1 * (__uint_as_float(dv[e + 1]) - Dl[e + 1]);
+          pp[e >> 1] = pack_bf16x2(p0, p1);
+          dd[e >> 1] = pack_bf16x2(g0, g1);
+        }
+        // dV of block g-2 is done with this P^T buffer; dK / dQ^T of block g-1 with dS^T.
+        if ((g >= 2 && !mbar_wait(&p_free[g & 1], (static_cast<uint32_t>(g >> 1) & 1u) ^ 1u, p.status, 181,
+                                  abort_flag)) ||
+            (g >= 1 && !mbar_wait(ds_free, static_cast<uint32_t>(g - 1) & 1u, p.status, 182, abort_flag))) {
+          ok = false;
+          break;
+        }
+        if (pre_w >= 0) {
+          stage(g + 1, pre_i, pre);
+          int w2, i2;
+          next_block(pre_w, pre_i, w2, i2);
+          pre_w = w2;
+          pre_i = i2;
+          if (w2 >= 0) pre = load_raw(w2, i2);
+        }
+        uint8_t* sP = sPt + (g & 1) * C::kPBytes;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t off = sw128_off(krow, half * 4 + k);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(sP + off)), "r"(pp[4 * k]),
+                       "r"(pp[4 * k + 1]), "r"(pp[4 * k + 2]), "r"(pp[4 * k + 3])
+                       : "memory");
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(sdSt + off)), "r"(dd[4 * k]),
+                       "r"(dd[4 * k + 1]), "r"(dd[4 * k + 2]), "r"(dd[4 * k + 3])
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pds_full);
+      }
+      if (!ok) break;
+      // dV of the last block done: dK and dV of this key tile are final.
+      if (!mbar_wait(&p_free[(g - 1) & 1], static_cast<uint32_t>((g - 1) >> 1) & 1u, p.status, 183, abort_flag)) break;
+      tc_fence_after();
+      const int key = kt * 128 + krow;
+      const float sc = half == 0 ? p.scale : 1.f;
+      const uint32_t colx = half == 0 ? C::kColDK : C::kColDV;
+      uint8_t* row = reinterpret_cast<uint8_t*>(p.dqkv) +
+                     ((static_cast<long long>(b) * p.S + key) * p.lddq + static_cast<long long>(h) * 3 * p.dr +
+                      (half + 1) * p.dr) * 2;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        if (c * 32 >= p.dr) break;  // uniform
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + colx + c * 32, o);
+        tmem_ld_wait();
+        if (key < p.S) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (c * 32 + k * 8 >= p.dr) break;
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[8 * k + 0]) * sc, __uint_as_float(o[8 * k + 1]) * sc);
+            v.y = pack_bf16x2(__uint_as_float(o[8 * k + 2]) * sc, __uint_as_float(o[8 * k + 3]) * sc);
+            v.z = pack_bf16x2(__uint_as_float(o[8 * k + 4]) * sc, __uint_as_float(o[8 * k + 5]) * sc);
+            v.w = pack_bf16x2(__uint_as_float(o[8 * k + 6]) * sc, __uint_as_float(o[8 * k + 7]) * sc);
+            *reinterpret_cast<uint4*>(row + c * 64 + k * 16) = v;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dkv_free);
+    }
+  } else if (warp >= 2 + kBwdCompute) {
+    // ------------------------------------------------------------ dQ drain (thread = head-dim row)
+    const int quarter = warp & 3;  // head-dim rows [32*quarter, +32) = staging box `quarter`
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const bool issuer = warp == 2 + kBwdCompute && lane == 0;
+    uint8_t* box = sStg + quarter * (BQ * 128);
+    int g = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x) {
+      const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
+      for (int i = 2 * kt; i < p.n_qb; ++i, ++g) {
+        if (!mbar_wait(dq_full, static_cast<uint32_t>(g) & 1u, p.status, 185, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t o[2][32];
+        tmem_ld_32x32b_x32(tmem + lane_base + C::kColDQ, o[0]);
+        tmem_ld_32x32b_x32(tmem + lane_base + C::kColDQ + 32, o[1]);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_free);
+        // The previous block's reduce-adds have read the staging tile.
+        if (g >= 1 && !mbar_wait(stg_free, static_cast<uint32_t>(g - 1) & 1u, p.status, 186, abort_flag)) {
+          ok = false;
+          break;
+        }
+        // Element (query q, head-dim row quarter*32 + lane) of box `quarter`: row q, 4-byte word
+        // `lane` of the 128-byte row, 16-byte chunk swizzled by q % 8.
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int q = c * 32 + e;
+            const uint32_t off = static_cast<uint32_t>(q * 128 + ((((lane >> 2) ^ (q & 7))) << 4) + (lane & 3) * 4);
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(smem_u32(box + off)), "r"(o[c][e]) : "memory");
+          }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_staged);
+        if (issuer) {
+          if (!mbar_wait(dq_staged, static_cast<uint32_t>(g) & 1u, p.status, 187, abort_flag)) {
+            ok = false;
+          } else {
+#pragma unroll
+            for (int bx = 0; bx < 4; ++bx)
+              if (bx * 32 < p.dr) tma_reduce_add_4d(&tmDQ, sStg + bx * (BQ * 128), bx * 32, h, i * BQ, b);
+            bulk_commit_group();
+            bulk_wait_read_all();
+            mbar_arrive(stg_free);
+          }
+        }
+        ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
+      }
+    }
+    if (issuer) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
+}
+
 }  // namespace attn_tc
 }  // namespace md
 
@@ -991,14 +1462,14 @@ bool make_map_bsc(CUtensorMap* map, const void* ptr, int B, int S, long long col
 }
 
 // [B, S, slots, dr] view of a [B*S, ld] bf16 matrix whose rows hold `slots`
-// consecutive dr-wide head vectors; box {64, 1, 128 rows, 1}, 128B swizzle.
+// consecutive dr-wide head vectors; box {64, 1, rows, 1}, 128B swizzle.
 // Columns dr..63 of the last box read as zero.
-bool make_map_bshd(CUtensorMap* map, const void* ptr, int B, int S, int slots, int dr, long long ld) {
+bool make_map_bshd(CUtensorMap* map, const void* ptr, int B, int S, int slots, int dr, long long ld, int rows = 128) {
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(dr), static_cast<cuuint64_t>(slots), static_cast<cuuint64_t>(S),
                         static_cast<cuuint64_t>(B)};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(dr) * 2, static_cast<cuuint64_t>(ld) * 2,
                            static_cast<cuuint64_t>(ld) * 2 * S};
-  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(rows), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   return g_encode_attn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1012,6 +1483,20 @@ bool make_map_f32_bsc(CUtensorMap* map, const void* ptr, int B, int S, long long
   cuuint32_t box[3] = {32, 128, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return g_encode_attn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// [B, S, H, dr] view of a [B*S, ld] fp32 matrix (head h at columns h*dr); box {32, 1, rows, 1},
+// 128B swizzle.  Reduce-adds clip columns past dr and rows past S.
+bool make_map_f32_bshd(CUtensorMap* map, const void* ptr, int B, int S, int H, int dr, long long ld, int rows) {
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(dr), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(S),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(dr) * 4, static_cast<cuuint64_t>(ld) * 4,
+                           static_cast<cuuint64_t>(ld) * 4 * S};
+  cuuint32_t box[4] = {32, 1, static_cast<cuuint32_t>(rows), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return g_encode_attn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(ptr), dims, strides, box, estr,
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -1101,19 +1586,61 @@ int bwd_tc_launch(const void* qkv, long long ldq, const void* dout, long long ld
   return static_cast<int>(cudaGetLastError());
 }
 
+// head_dim 128 (dr = 128) or 80 (dr = 80, zero-padded boxes): bwd128_kernel.
+int bwd128_tc_launch(const void* qkv, long long ldq, const void* dout, long long lddo, const float* lse,
+                     const float* delta, float* dqacc, long long ldacc, void* dqkv, long long lddq, int B, int H,
+                     int S, int dr, float scale, void* status, cudaStream_t st) {
+  using C = md::attn_tc::Bwd128Cfg;
+  if (!get_encoder()) return -3;
+  if (dr % 8 || dr > 128 || dr < 72 || ldacc != static_cast<long long>(H) * dr) return -2;
+  CUtensorMap tkv, tq, tdo, tdq;
+  if (!make_map_bshd(&tkv, qkv, B, S, 3 * H, dr, ldq, 128) || !make_map_bshd(&tq, qkv, B, S, 3 * H, dr, ldq, 64) ||
+      !make_map_bshd(&tdo, dout, B, S, H, dr, lddo, 64) || !make_map_f32_bshd(&tdq, dqacc, B, S, H, dr, ldacc, 64))
+    return -4;
+  if (g_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  md::attn_tc::Bwd128Params p;
+  p.lse = lse;
+  p.delta = delta;
+  p.dqkv = dqkv;
+  p.lddq = lddq;
+  p.B = B;
+  p.H = H;
+  p.S = S;
+  p.n_kt = (S + 127) / 128;
+  p.n_qb = (S + 63) / 64;
+  p.items = p.n_kt * B * H;
+  p.dr = dr;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.status = reinterpret_cast<md::Status*>(status);
+  auto k = md::attn_tc::bwd128_kernel;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const int grid = p.items < g_sms ? p.items : g_sms;
+  md::launch_pdl(k, grid, dim3(md::attn_tc::kBwdThreads), C::kSmemBytes, st, tkv, tq, tdo, tdq, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
 }  // namespace
 
 extern "C" {
 
-// Main pass of the tcgen05 attention backward (head_dim 64): dK, dV into dqkv
+// Main pass of the tcgen05 attention backward (head_dim 64, 80 or 128): dK, dV into dqkv
 // and dQ (unscaled) added into the zeroed fp32 accumulator dqacc [B*S, ldacc].
 // delta [B, H, S] = rowsum(dO * O) must be ready.  attention.cu's
 // md_attn_bwd_tc wraps this with the delta and dQ conversion steps.
 int md_attn_bwd_tc_main(const void* qkv, long long ldq, const void* dout, long long lddo, const float* lse,
                         const float* delta, float* dqacc, long long ldacc, void* dqkv, long long lddq, int B, int H,
                         int S, int D, float scale, void* status, cudaStream_t st) {
-  if (D != 64) return -2;
-  return bwd_tc_launch<64>(qkv, ldq, dout, lddo, lse, delta, dqacc, ldacc, dqkv, lddq, B, H, S, scale, status, st);
+  if (D == 64)
+    return bwd_tc_launch<64>(qkv, ldq, dout, lddo, lse, delta, dqacc, ldacc, dqkv, lddq, B, H, S, scale, status, st);
+  if (D == 80 || D == 128)
+    return bwd128_tc_launch(qkv, ldq, dout, lddo, lse, delta, dqacc, ldacc, dqkv, lddq, B, H, S, D, scale, status, st);
+  return -2;
 }
 
 // Performance analysis: record clock64() hand-off timestamps of CTA 0 of the

@@ -119,10 +119,36 @@ __global__ void __launch_bounds__(256) adamw_kernel(const MdAdamEntry* __restric
   }
 }
 
+// Loss-scaler overflow test over the same (tensor, chunk) table: *flag = 1
+// when any gradient element is inf or NaN (read-only; the unscale itself is
+// folded into adamw_kernel through inv_scale, and the update is skipped
+// there through `skip` = this flag after the cross-rank MAX).
+__global__ void __launch_bounds__(256) nonfinite_kernel(const MdAdamEntry* __restrict__ table,
+                                                        const int2* __restrict__ chunks, float* __restrict__ flag) {
+  pdl_trigger();
+  pdl_wait();
+  const int2 c = chunks[blockIdx.x];
+  const MdAdamEntry e = table[c.x];
+  const long long lo = static_cast<long long>(c.y) * kChunk;
+  const long long hi = lo + kChunk < e.n ? lo + kChunk : e.n;
+  bool bad = false;
+  for (long long k = lo + threadIdx.x; k < hi; k += blockDim.x) bad |= !isfinite(e.g[k]);
+  if (__syncthreads_or(bad) && threadIdx.x == 0) *flag = 1.f;
+}
+
 }  // namespace optim
 }  // namespace md
 
 extern "C" {
+
+// *flag = 1 if any gradient of the table is non-finite (flag is not cleared here).
+int md_nonfinite(const void* table, const void* chunks, int num_chunks, float* flag, cudaStream_t s) {
+  if (num_chunks <= 0) return 0;
+  if (flag == nullptr) return -1;
+  md::launch_pdl(md::optim::nonfinite_kernel, dim3(num_chunks), dim3(256), 0, s,
+                 reinterpret_cast<const MdAdamEntry*>(table), reinterpret_cast<const int2*>(chunks), flag);
+  return static_cast<int>(cudaGetLastError());
+}
 
 int md_adamw_chunk() { return md::optim::kChunk; }
 int md_adamw_entry_bytes() { return static_cast<int>(sizeof(MdAdamEntry)); }

@@ -161,11 +161,32 @@ class DistributedGradScaler:
         return self._step_found_inf
 
     def step(self, optimizer: torch.optim.Optimizer) -> bool:
-        """Apply ``optimizer.step()`` unless the group found an overflow; return whether it stepped."""
+        """Apply ``optimizer.step()`` unless the group found an overflow; return whether it stepped.
+
+        With :class:`minidist.optim.FusedAdamW` on CUDA (and ``unscale_`` not called this step)
+        the decision stays on the device: a read-only overflow check of the gradients, the
+        group-wide MAX of the flag, then the AdamW kernel, which unscales each gradient as it
+        reads it and skips the whole update when the flag is set -- no separate unscale pass
+        and no host synchronisation here.  The outcome is read in :meth:`update`; this call
+        returns ``True`` (the update was issued, conditionally)."""
         self.num_steps += 1
         if not self.enabled:
             optimizer.step()
             return True
+        if self._step_found_inf is None and getattr(optimizer, "check_nonfinite", None) is not None:
+            grads = self._grads(optimizer)
+            if grads and grads[0].is_cuda:
+                from .ddp import wait_all_deferred
+
+                wait_all_deferred()  # the check reads every gradient
+                flag = torch.zeros(1, dtype=torch.float32, device=grads[0].device)
+                optimizer.check_nonfinite(flag)
+                if comm.is_distributed() and comm.get_world_size(self.process_group) > 1:
+                    dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.process_group)
+                inv = torch.full((1,), 1.0 / self._scale, dtype=torch.float32, device=flag.device)
+                optimizer.step(inv_scale=inv, skip=flag)
+                self._device_found_inf = flag
+                return True
         if self.unscale_(optimizer):
             self.num_skipped += 1
             return False
@@ -176,6 +197,12 @@ class DistributedGradScaler:
         """Adapt the scale from this step's (group-agreed) outcome and reset per-step state."""
         if not self.enabled:
             return
+        flag = getattr(self, "_device_found_inf", None)
+        if flag is not None:
+            self._device_found_inf = None
+            self._step_found_inf = bool(flag.item() > 0)
+            if self._step_found_inf:
+                self.num_skipped += 1
         if self._step_found_inf:
             self._scale = max(self._min_scale, self._scale * self._backoff_factor)
             self._good_steps = 0

@@ -36,6 +36,7 @@ _SIGS = {
     "md_ce_backward": "i:plpplpfpliip",
     "md_adamw": "i:ppifffffffppipp",
     "md_adamw_chunk": "i:",
+    "md_nonfinite": "i:ppipp",
     "md_adamw_entry_bytes": "i:",
 }
 for _n, _s in _SIGS.items():
@@ -126,7 +127,7 @@ def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int, D: int, impl: str |
 
 
 def attention_bwd_impl() -> str:
-    """The attention backward in use: ``"tc"`` (tcgen05, d = 64) or ``"mma"``."""
+    """The attention backward in use: ``"tc"`` (tcgen05, d = 64 / 80 / 128) or ``"mma"``."""
     return _ATTN_BWD
 
 
@@ -143,7 +144,7 @@ def attention_bwd(qkv, out, dout, lse, B: int, S: int, H: int, D: int, dqkv: tor
         delta = torch.empty(B * H * S, dtype=torch.float32, device=qkv.device)
     dqacc = torch.empty(B * S, H * D, dtype=torch.float32, device=qkv.device)
     impl = impl or _ATTN_BWD
-    if impl == "tc" and D == 64:
+    if impl == "tc" and D in (64, 80, 128):  # d = 80 runs the d = 128 kernel on zero-padded boxes
         rc = nat.lib().md_attn_bwd_tc(qkv.data_ptr(), _ld(qkv), None if have_delta else out.data_ptr(), _ld(out),
                                       dout.data_ptr(), _ld(dout),
                                       lse.data_ptr(), delta.data_ptr(), dqacc.data_ptr(), dqkv.data_ptr(), _ld(dqkv),

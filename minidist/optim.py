@@ -75,11 +75,42 @@ class FusedAdamW(torch.optim.Optimizer):
     # -- step -----------------------------------------------------------------------
 
     @torch.no_grad()
-    def step(self, closure=None):
+    def check_nonfinite(self, flag: torch.Tensor) -> None:
+        """Set device ``flag`` (float32 ``[1]``) to 1 if any gradient is inf / NaN, without a host
+        synchronisation (one read-only multi-tensor pass per parameter group; CPU parameters are
+        checked with torch ops)."""
+        for gi, group in enumerate(self.param_groups):
+            params = [p for p in group["params"] if p.grad is not None]
+            fused = [p for p in params if p.is_cuda and p.dtype == torch.float32 and p.grad.dtype == torch.float32]
+            for p in params:
+                if p not in fused:
+                    flag.add_((~torch.isfinite(p.grad)).any().to(flag.dtype).to(flag.device))
+            if fused:
+                for key, part in self._partitions(gi, fused):
+                    table, chunk_t, n = self._table(key, part)
+                    nat.check(nat.lib().md_nonfinite(table.data_ptr(), chunk_t.data_ptr(), n, flag.data_ptr(),
+                                                     nat.stream_ptr()), "md_nonfinite")
+
+    def _partitions(self, gi, fused):
+        late = [p for p in fused if getattr(p, "_md_grad_event", None) is not None]
+        if not late:
+            return [(gi, fused)]
+        early = [p for p in fused if getattr(p, "_md_grad_event", None) is None]
+        return [((gi, 0), early), ((gi, 1), late)] if early else [((gi, 1), late)]
+
+    @torch.no_grad()
+    def step(self, closure=None, *, inv_scale: torch.Tensor | None = None, skip: torch.Tensor | None = None):
+        """One AdamW step.  ``inv_scale`` / ``skip`` (device float32 ``[1]``, from
+        :class:`minidist.amp.DistributedGradScaler`): gradients are multiplied by ``inv_scale``
+        inside the update kernel, and the whole update is skipped on the device when ``skip``
+        is nonzero -- the loss scaler's unscale and overflow skip with no extra pass over the
+        gradients and no host synchronisation."""
         loss = None
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        self._scaler_ptrs = (None if inv_scale is None else inv_scale.data_ptr(),
+                             None if skip is None else skip.data_ptr())
         for gi, group in enumerate(self.param_groups):
             params = [p for p in group["params"] if p.grad is not None]
             if not params:
@@ -127,10 +158,14 @@ class FusedAdamW(torch.optim.Optimizer):
                 self._ensure_grad_buffers()
             for ev in {id(h): h for h in (getattr(p, "_md_grad_event", None) for p in rest) if h is not None}.values():
                 wait_handle(ev)
+            if rest and skip is not None and bool(skip.item()):
+                rest = []
             for p in rest:
                 p._md_grad_event = None
                 st = self.state[p]
                 g = p.grad.to(p.dtype)
+                if inv_scale is not None:
+                    g = g * inv_scale.to(g.device)
                 p.mul_(1 - lr * wd)
                 st["exp_avg"].mul_(b1).add_(g, alpha=1 - b1)
                 st["exp_avg_sq"].mul_(b2).addcmul_(g, g, value=1 - b2)
@@ -167,6 +202,20 @@ class FusedAdamW(torch.optim.Optimizer):
         self._grad_flat = flat
 
     def _fused_update(self, gi, params, lr, b1, b2, eps, wd, bc1, bc2_sqrt, hp=None) -> None:
+        from .models.fused_gpt import _SHADOW
+
+        table, chunk_t, n = self._table(gi, params)
+        inv_ptr, skip_ptr = getattr(self, "_scaler_ptrs", (None, None))
+        rc = nat.lib().md_adamw(table.data_ptr(), chunk_t.data_ptr(), n, lr, b1, b2, eps, wd, bc1, bc2_sqrt,
+                                inv_ptr, skip_ptr, 0, nat.stream_ptr(), None if hp is None else hp.data_ptr())
+        nat.check(rc, "md_adamw")
+        for p in params:
+            if getattr(p, _SHADOW, None) is not None:
+                setattr(p, "_md_bf16_ver", p._version)
+
+    def _table(self, gi, params):
+        """Device (tensor, chunk) table of ``params`` for the multi-tensor kernels, cached per key
+        while the pointers stay the same."""
         from .models.fused_gpt import _SHADOW, _SHADOW_VER
 
         lib = nat.lib()
@@ -194,10 +243,4 @@ class FusedAdamW(torch.optim.Optimizer):
             chunk_t = chunk_h.to(dev, non_blocking=True)
             cached = (key, table, chunk_t, len(chunks), table_h, chunk_h)
             self._tables[gi] = cached
-        table, chunk_t, n = cached[1], cached[2], cached[3]
-        rc = lib.md_adamw(table.data_ptr(), chunk_t.data_ptr(), n, lr, b1, b2, eps, wd, bc1, bc2_sqrt,
-                          None, None, 0, nat.stream_ptr(), None if hp is None else hp.data_ptr())
-        nat.check(rc, "md_adamw")
-        for p in params:
-            if getattr(p, _SHADOW, None) is not None:
-                setattr(p, _SHADOW_VER, p._version)
+        return cached[1], cached[2], cached[3]

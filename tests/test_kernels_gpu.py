@@ -101,6 +101,25 @@ def test_attention_fwd_tc_many_tiles():
     assert _rel(g1, g2) < 2e-2
 
 
+@pytest.mark.parametrize("D", [80, 128])
+def test_attention_bwd_tc_wide_heads_many_tiles(D):
+    """The head_dim 80 / 128 tcgen05 backward (64-query blocks, dQ^T in TMEM) with several work
+    items per CTA and a padded row stride, against the mma.sync backward and fp32 autograd."""
+    torch.manual_seed(4)
+    B, S, H = 2, 1280, 16  # 10 key tiles x 32 heads = 320 items over 148 CTAs
+    buf = torch.randn(B * S, 3 * H * D + 64, device="cuda").bfloat16()
+    qkv = buf[:, : 3 * H * D]
+    y, lse = K.attention_fwd(qkv, B, S, H, D, impl="tc")
+    dy = torch.randn(B * S, H * D, device="cuda").bfloat16()
+    g1 = K.attention_bwd(qkv, y, dy, lse, B, S, H, D, impl="tc")
+    g2 = K.attention_bwd(qkv, y, dy, lse, B, S, H, D, impl="mma")
+    nat.check_status()
+    assert _rel(g1, g2) < 2e-2
+    qf = qkv.float().requires_grad_(True)
+    _attn_ref(qf, B, S, H, D).backward(dy.float())
+    assert _rel(g1, qf.grad) < 3e-2
+
+
 def test_embedding_and_colsum():
     torch.manual_seed(2)
     V, C, B, S = 1000, 768, 4, 64
