@@ -9,6 +9,8 @@
 // Reads the bf16 shadow of the tables; gradients land in fp32.
 // Replaces VocabParallelEmbedding.forward (reference tensor_parallel.py:409-416)
 // and Embedding.forward (models/gpt.py:183-185).
+#include <atomic>
+
 #include "md_noalloc.h"
 #include "md_sm100.cuh"
 
@@ -304,12 +306,21 @@ static __device__ __align__(256) float md_colsum_scratch[MD_NOALLOC_SCRATCH_FLOA
 
 namespace {
 constexpr int kMaxDevices = 64;
-void* g_colsum_scratch[kMaxDevices] = {};
+// Per-device device address of md_colsum_scratch, looked up on the first call
+// on that device.  Atomic, so two host threads making their first call at the
+// same time do not race (both store the same address).  A cudaDeviceReset
+// ends the context the address belongs to; call md_colsum_noalloc_reset()
+// after one so the next call looks the address up again.
+std::atomic<void*> g_colsum_scratch[kMaxDevices];
 }  // namespace
 
-extern "C" int md_colsum_scratch_floats(int M, int N) {
+extern "C" long long md_colsum_scratch_floats(int M, int N) {
   if (M <= 0 || N <= 0) return 0;
-  return md_colsum_chunks(M, N) * N;
+  return static_cast<long long>(md_colsum_chunks(M, N)) * N;
+}
+
+extern "C" void md_colsum_noalloc_reset() {
+  for (auto& a : g_colsum_scratch) a.store(nullptr, std::memory_order_release);
 }
 
 extern "C" int md_colsum_noalloc(const void* x, long long ldx, int M, int N, float* out, int accumulate,
@@ -321,13 +332,13 @@ extern "C" int md_colsum_noalloc(const void* x, long long ldx, int M, int N, flo
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return static_cast<int>(e);
   if (dev < 0 || dev >= kMaxDevices) return -2;
-  if (g_colsum_scratch[dev] == nullptr) {
+  void* scratch = g_colsum_scratch[dev].load(std::memory_order_acquire);
+  if (scratch == nullptr) {
     // Device address of the static array for the current device; the host
     // symbol itself is only a stand-in and must never reach a kernel.
-    void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, md_colsum_scratch);
+    e = cudaGetSymbolAddress(&scratch, md_colsum_scratch);
     if (e != cudaSuccess) return static_cast<int>(e);
-    g_colsum_scratch[dev] = ptr;
+    g_colsum_scratch[dev].store(scratch, std::memory_order_release);
   }
-  return md_colsum(x, ldx, M, N, static_cast<float*>(g_colsum_scratch[dev]), out, accumulate, s);
+  return md_colsum(x, ldx, M, N, static_cast<float*>(scratch), out, accumulate, s);
 }

@@ -20,9 +20,11 @@
 //
 // The first call on each device looks up that device's address of the static
 // array (cudaGetSymbolAddress, with the device current) and caches it; make
-// that first call before any stream capture.  All calls on a device share the
-// one array, so calls that may overlap on the GPU (different streams without
-// ordering between them) race on it; serialise them.
+// that first call before any stream capture.  After a cudaDeviceReset, call
+// md_colsum_noalloc_reset() so the next call looks the address up again.
+// All calls on a device share the one array, so calls that may overlap on the
+// GPU (different streams without ordering between them) race on it; serialise
+// them.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -37,8 +39,12 @@ extern "C" {
 
 int md_colsum_noalloc(const void* x, long long ldx, int M, int N, float* out, int accumulate, cudaStream_t stream);
 
-// Scratch floats md_colsum / md_colsum_noalloc need for an [M, N] input.
-int md_colsum_scratch_floats(int M, int N);
+// Scratch floats md_colsum / md_colsum_noalloc need for an [M, N] input
+// (64-bit: the product exceeds INT_MAX for N beyond about 14.5 million).
+long long md_colsum_scratch_floats(int M, int N);
+
+// Forget the cached device addresses of the scratch array (after cudaDeviceReset).
+void md_colsum_noalloc_reset(void);
 
 #ifdef __cplusplus
 }

@@ -42,9 +42,13 @@ def test_noalloc_colsum_matches_allocating_entry_point():
     fn = _entry()
     torch.manual_seed(0)
     stream = torch.cuda.current_stream().cuda_stream
-    shapes = [(16384, 3072, False), (1000, 768, True)]
-    for M, N, accumulate in shapes:  # two calls in a row, different sizes
-        x = torch.randn(M, N, device="cuda").bfloat16()
+    # Two contiguous shapes (the 8-column vector path), then ragged ones that take the scalar
+    # path: N % 8 != 0, and a strided view whose row stride is not a multiple of 8.
+    wide = torch.randn(333, 778, device="cuda").bfloat16()  # row stride 778: even, not a multiple of 8
+    shapes = [(16384, 3072, False, None), (1000, 768, True, None), (999, 770, False, None),
+              (333, 771, True, wide[:, :771])]
+    for M, N, accumulate, view in shapes:  # calls in a row, different sizes
+        x = torch.randn(M, N, device="cuda").bfloat16() if view is None else view
         base = torch.randn(N, device="cuda")
         want = base.clone()
         K.colsum(x, want, accumulate=accumulate)
@@ -54,6 +58,14 @@ def test_noalloc_colsum_matches_allocating_entry_point():
         torch.cuda.synchronize()
         assert _rel(got, want) < 1e-5
         assert _rel(got, (base if accumulate else 0) + x.float().sum(0)) < 1e-4
+
+
+def test_noalloc_scratch_size_query_is_64_bit():
+    lib = ctypes.CDLL(str(nat.library_path()))
+    q = lib.md_colsum_scratch_floats
+    q.argtypes, q.restype = [ctypes.c_int, ctypes.c_int], ctypes.c_longlong
+    assert q(16384, 20_000_000) > 2**31  # no int overflow for very wide inputs
+    assert q(0, 5) == 0
 
 
 def test_noalloc_colsum_rejects_oversized_jobs():
