@@ -99,6 +99,7 @@ def bench_attention(B, H, S, D, iters):
     y, lse = K.attention_fwd(qkv, B, S, H, D)
     dy = torch.randn_like(y)
     tb = timed(lambda: K.attention_bwd(qkv, y, dy, lse, B, S, H, D), iters)
+    tmb = timed(lambda: K.attention_bwd(qkv, y, dy, lse, B, S, H, D, impl="mma"), iters)
     q, k, v = (z.transpose(1, 2) for z in qkv.view(B, S, H, 3, D).unbind(3))
     q, k, v = (z.contiguous().requires_grad_(True) for z in (q, k, v))
     tr = timed(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True), iters)
@@ -109,7 +110,7 @@ def bench_attention(B, H, S, D, iters):
     print(f"attention fwd B={B} H={H} S={S} D={D}: {t * 1e6:8.1f} us {fl_f / t / 1e12:6.1f} TFLOP/s | "
           f"torch SDPA {tr * 1e6:8.1f} us {fl_f / tr / 1e12:6.1f} TFLOP/s | mma.sync {tm * 1e6:8.1f} us")
     print(f"attention bwd B={B} H={H} S={S} D={D}: {tb * 1e6:8.1f} us {2.5 * fl_f / tb / 1e12:6.1f} TFLOP/s | "
-          f"torch SDPA {trb * 1e6:8.1f} us {2.5 * fl_f / trb / 1e12:6.1f} TFLOP/s")
+          f"torch SDPA {trb * 1e6:8.1f} us {2.5 * fl_f / trb / 1e12:6.1f} TFLOP/s | mma.sync {tmb * 1e6:8.1f} us")
 
 
 def bench_layernorm(M, C, iters):
@@ -142,7 +143,8 @@ def main():
                    (16384, 50257, 768), (8192, 8192, 8192)]):
             bench_gemm(*s, iters=a.iters, cta_group=a.cta_group, which=a.which)
     if a.op in ("all", "attention"):
-        for s in ([shp] if shp and a.op == "attention" else [(16, 12, 1024, 64), (4, 16, 2048, 128)]):
+        for s in ([shp] if shp and a.op == "attention" else [(16, 12, 1024, 64), (8, 25, 1024, 64), (4, 16, 2048, 80), (4, 16, 2048, 128),
+                                                               (4, 4, 2048, 128)]):
             bench_attention(*s, iters=a.iters)
     if a.op in ("all", "layernorm"):
         for s in ([shp] if shp and a.op == "layernorm" else [(16384, 768), (8192, 4096)]):

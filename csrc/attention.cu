@@ -624,6 +624,7 @@ int md_attn_fwd(const void* qkv, long long ldq, void* out, long long ldo, float*
                 float scale, cudaStream_t st) {
   if (B <= 0 || H <= 0 || S <= 0 || !al16(qkv) || !al16(out) || (ldq % 8) || (ldo % 8)) return -1;
   switch (D) {
+    case 32: return fwd_launch<32>(qkv, ldq, out, ldo, lse, B, H, S, scale, st);
     case 64: return fwd_launch<64>(qkv, ldq, out, ldo, lse, B, H, S, scale, st);
     case 80: return fwd_launch<80>(qkv, ldq, out, ldo, lse, B, H, S, scale, st);
     case 128: return fwd_launch<128>(qkv, ldq, out, ldo, lse, B, H, S, scale, st);
@@ -640,6 +641,7 @@ int md_attn_bwd(const void* qkv, long long ldq, const void* out, long long ldo, 
       (ldo % 8) || (lddo % 8) || (lddq % 8))
     return -1;
   switch (D) {
+    case 32: return bwd_launch<32>(qkv, ldq, out, ldo, dout, lddo, lse, delta, dqacc, dqkv, lddq, B, H, S, scale, st);
     case 64: return bwd_launch<64>(qkv, ldq, out, ldo, dout, lddo, lse, delta, dqacc, dqkv, lddq, B, H, S, scale, st);
     case 80: return bwd_launch<80>(qkv, ldq, out, ldo, dout, lddo, lse, delta, dqacc, dqkv, lddq, B, H, S, scale, st);
     case 128:

@@ -337,7 +337,7 @@ def check_composition(rank, world):
 
     if world % 4:
         return
-    cfg = GPTConfig(vocab_size=1024, block_size=128, n_layer=4, n_head=8, n_embd=256, seed=6)
+    cfg = GPTConfig(vocab_size=1024, block_size=128, n_layer=4, n_head=8, n_embd=512, seed=6)
     dp = world // 4
     g = torch.Generator().manual_seed(23)
     ids = torch.randint(0, cfg.vocab_size, (4 * dp, 128), generator=g).cuda()

@@ -60,7 +60,7 @@ def _attn_ref(qkv, B, S, H, D):
 
 @pytest.mark.parametrize("impl", ["tc", "mma"])
 @pytest.mark.parametrize("B,S,H,D", [(2, 256, 3, 64), (1, 200, 2, 64), (1, 192, 2, 80), (2, 128, 2, 128),
-                                     (1, 1024, 4, 64), (2, 333, 2, 128), (2, 333, 3, 80)])
+                                     (1, 1024, 4, 64), (2, 333, 2, 128), (2, 333, 3, 80), (2, 160, 4, 32)])
 def test_attention(B, S, H, D, impl):
     torch.manual_seed(1)
     qkv = torch.randn(B * S, 3 * H * D, device="cuda").bfloat16()
