@@ -38,6 +38,7 @@ from __future__ import annotations
 
 from collections.abc import Iterator, Sequence
 from contextlib import contextmanager
+from contextlib import nullcontext as _nullctx
 
 import torch
 import torch.distributed as dist
@@ -125,6 +126,9 @@ class _FSDPUnit:
         comm.all_gather_into_tensor(self._full, src.contiguous(), group=self.group)
 
     def unshard(self) -> None:
+        if not self._unsharded and self._owner_state is not None:
+            # Peer-memory path: every gather runs on the communication stream (see _reduce_scatter_peer).
+            self.prefetch(self._owner_state["stream"])
         if self._unsharded:
             if self._gather_event is not None:
                 torch.cuda.current_stream().wait_event(self._gather_event)
@@ -144,8 +148,6 @@ class _FSDPUnit:
             ev.record(stream)
         self._full.record_stream(torch.cuda.current_stream())
         self._gather_event = ev
-        if self._owner_state is not None:
-            self._owner_state["last_gather"] = ev
         self._unsharded = True
 
     def reshard(self) -> None:
@@ -204,18 +206,14 @@ class _FSDPUnit:
 
         comm_, buf, off = self._peer
         full = self._full_grad_buffer()
-        st = self._owner_state
-        if st is not None and st.get("last_gather") is not None:
-            # A prefetch gather (another cross-rank kernel) may still be running on the side
-            # stream: start the reduce-scatter only after it, on every rank.
-            torch.cuda.current_stream().wait_event(st["last_gather"])
-            st["last_gather"] = None
         o = 0
         with torch.no_grad():
             for p, n in zip(self.params, self.numels, strict=True):
                 slot = full[o : o + n]
                 g = p.grad
-                if g is not None and g.data_ptr() == slot.data_ptr():
+                if g is None and getattr(p, "_md_grad_written", False):
+                    pass  # a fused kernel wrote the fp32 gradient of a low-precision view in place
+                elif g is not None and g.data_ptr() == slot.data_ptr():
                     pass  # written in place (fused kernels' main gradient, or autograd accumulating into it)
                 elif g is not None:
                     slot.copy_(g.detach().reshape(-1))
@@ -223,18 +221,32 @@ class _FSDPUnit:
                     slot.zero_()  # no gradient this step
                 o += n
         shard = self.flat_shard
-        if self._adam is not None:
-            a = self._adam
-            a["step"] += 1
-            b1, b2 = a["betas"]
-            collectives.reduce_scatter_shard(buf, comm_, off, self.shard_numel, None, False, 1.0 / self.world,
-                                             adam=(shard.data, a["m"], a["v"], a["lr"], b1, b2, a["eps"],
-                                                   a["weight_decay"], a["step"]))
-        else:
-            acc = shard.grad is not None
-            if not acc:
-                shard.grad = torch.empty(self.shard_numel, dtype=torch.float32, device=shard.device)
-            collectives.reduce_scatter_shard(buf, comm_, off, self.shard_numel, shard.grad, acc, 1.0 / self.world)
+        acc = shard.grad is not None
+        if self._adam is None and not acc:
+            shard.grad = torch.empty(self.shard_numel, dtype=torch.float32, device=shard.device)
+        # The reduce-scatter runs on the module's communication stream, after this unit's
+        # gradients on the compute stream; the backward's end makes the compute stream wait
+        # for it (FullyShardedDataParallel._end_of_backward).  Gathers and reduce-scatters share
+        # that one stream, so the cross-rank kernels of a rank run one at a time, in the same
+        # order on every rank.
+        stream = self._owner_state["stream"] if self._owner_state is not None else None
+        if stream is not None:
+            stream.wait_stream(torch.cuda.current_stream())
+            if shard.grad is not None:
+                shard.grad.record_stream(stream)
+        with torch.cuda.stream(stream) if stream is not None else _nullctx():
+            if self._adam is not None:
+                a = self._adam
+                a["step"] += 1
+                b1, b2 = a["betas"]
+                collectives.reduce_scatter_shard(buf, comm_, off, self.shard_numel, None, False, 1.0 / self.world,
+                                                 adam=(shard.data, a["m"], a["v"], a["lr"], b1, b2, a["eps"],
+                                                       a["weight_decay"], a["step"]))
+            else:
+                collectives.reduce_scatter_shard(buf, comm_, off, self.shard_numel, shard.grad, acc,
+                                                 1.0 / self.world)
+        if stream is not None:
+            self._owner_state["pending"] = True
         for p in self.params:
             p.grad = None
             p._md_grad_written = False
@@ -323,7 +335,8 @@ class FullyShardedDataParallel(nn.Module):
                 u._peer = (self._peer_comm, self._grad_buf, off)
                 u._full_grad_buffer()  # fused kernels write gradients straight into the symmetric buffer
                 off += u.padded_numel
-            self._gather_state: dict = {"last_gather": None}
+            # One communication stream for every peer-memory gather and reduce-scatter.
+            self._gather_state: dict = {"stream": torch.cuda.Stream(device=device), "pending": False}
             if all(u.flat_shard.dtype == torch.float32 and u.policy.param_dtype in (torch.float32, torch.bfloat16)
                    for u in self._units) and collectives.fsdp_gather_enabled():
                 # fp32 shards move into a symmetric buffer so peers can read them.
@@ -351,7 +364,9 @@ class FullyShardedDataParallel(nn.Module):
         self._shards = nn.ParameterList([u.flat_shard for u in self._units])
         self._prefetch_stream = None
         if prefetch and device.type == "cuda" and self.world_size > 1:
-            self._prefetch_stream = torch.cuda.Stream(device=device)
+            st = getattr(self, "_gather_state", None)
+            self._prefetch_stream = st["stream"] if st is not None else torch.cuda.Stream(device=device)
+        self._callback_queued = False
         self._register_hooks()
 
     def _build_units(self, root, unit_types, reshard_after_forward, reshard_root, device) -> list[_FSDPUnit]:
@@ -417,8 +432,25 @@ class FullyShardedDataParallel(nn.Module):
 
     def _grad_ready(self, unit):
         def hook(param):
+            if not self._callback_queued and getattr(self, "_gather_state", None) is not None:
+                self._callback_queued = True
+                try:
+                    torch.autograd.Variable._execution_engine.queue_callback(self._end_of_backward)
+                except Exception:  # pragma: no cover - only legal inside backward
+                    self._callback_queued = False
             unit.on_param_grad_ready(param, sync=self.require_backward_grad_sync)
         return hook
+
+    def _end_of_backward(self) -> None:
+        """The compute stream waits for the reduce-scatters still running on the communication stream."""
+        self._callback_queued = False
+        self._wait_comm()
+
+    def _wait_comm(self) -> None:
+        st = getattr(self, "_gather_state", None)
+        if st is not None and st["pending"]:
+            torch.cuda.current_stream().wait_stream(st["stream"])
+            st["pending"] = False
 
     # -- public API ----------------------------------------------------------------
 
@@ -458,7 +490,8 @@ class FullyShardedDataParallel(nn.Module):
                     u.reshard()
 
     def finish_gradient_sync(self) -> None:
-        """Reduce-scatter units whose gradients were accumulated under ``no_sync``."""
+        """Reduce-scatter units whose gradients were accumulated under ``no_sync``, and order the
+        current stream after every reduce-scatter in flight."""
         if self.world_size == 1:
             return
         for u in self._units:
@@ -466,6 +499,7 @@ class FullyShardedDataParallel(nn.Module):
                 u.reduce_scatter_grads()
                 if u.reshard_after_forward:
                     u.reshard()
+        self._wait_comm()
 
     def memory_summary(self) -> dict[str, float]:
         total = sum(u.total_numel for u in self._units)

@@ -92,8 +92,10 @@ def bf16_weight(p: torch.Tensor) -> torch.Tensor:
 def fp32_param(p: torch.Tensor) -> torch.Tensor:
     """fp32, contiguous, 16-byte-aligned copy or view of a (small) parameter such as a bias or LN weight."""
     t = p.detach()
-    if t.dtype != torch.float32 or not t.is_contiguous() or (t.data_ptr() % 16):
-        t = t.float().contiguous().clone()
+    if t.dtype != torch.float32:
+        return t.float()  # a fresh (aligned, contiguous) fp32 tensor
+    if not t.is_contiguous() or (t.data_ptr() % 16):
+        t = t.contiguous().clone()
     return t
 
 
@@ -105,6 +107,15 @@ class _GradTarget:
     def __init__(self, p: torch.Tensor):
         self.p = p
         self._tmp = None
+        mg = gradsink.main_grad(p)
+        if (p.dtype != torch.float32 and p.grad is None and mg is not None and mg.dtype == torch.float32
+                and mg.is_contiguous() and mg.data_ptr() % 16 == 0):
+            # A low-precision parameter (an FSDP view gathered in bf16) whose wrapper keeps an fp32
+            # gradient buffer: the kernel writes there directly (no bf16 round trip); the first
+            # write of a backward overwrites, later ones accumulate.
+            self.dst, self.accumulate = mg, bool(getattr(p, "_md_grad_written", False))
+            p._md_grad_written = True
+            return
         if p.dtype == torch.float32 and (p.grad is None or p.grad.is_contiguous()):
             self.dst, self.accumulate = gradsink.grad_destination(p)
             if not self.dst.is_contiguous() or self.dst.data_ptr() % 16:

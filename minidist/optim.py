@@ -82,9 +82,12 @@ class FusedAdamW(torch.optim.Optimizer):
         for gi, group in enumerate(self.param_groups):
             params = [p for p in group["params"] if p.grad is not None]
             fused = [p for p in params if p.is_cuda and p.dtype == torch.float32 and p.grad.dtype == torch.float32]
+            fused_ids = {id(p) for p in fused}
             for p in params:
-                if p not in fused:
+                if id(p) not in fused_ids:
                     flag.add_((~torch.isfinite(p.grad)).any().to(flag.dtype).to(flag.device))
+            for p in fused:
+                self._state(p)  # the kernel table points at the moments too
             if fused:
                 for key, part in self._partitions(gi, fused):
                     table, chunk_t, n = self._table(key, part)
