@@ -119,6 +119,9 @@ class _FSDPUnit:
 
             comm_, buf, off = self._peer_shard
             collectives.all_gather_shards(buf, comm_, off, self.shard_numel, self._full)
+            # The kernel writes through a raw pointer: advance the version the parameter views
+            # share, so cached casts of them (the fused path's bf16 shadows) are refreshed.
+            torch.autograd.graph.increment_version(self._full)
             return
         src = self.flat_shard.detach()
         if src.dtype != self.policy.param_dtype:

@@ -89,6 +89,48 @@ def bf16_weight(p: torch.Tensor) -> torch.Tensor:
     return sh
 
 
+_SHADOW_LIST = "_md_shadow_params"
+
+
+def refresh_shadows(module: torch.nn.Module) -> None:
+    """Bring every stale bf16 weight shadow of ``module`` up to date in ONE multi-tensor launch
+    (the AdamW kernel in shadow-only mode) instead of one cast per weight: on the first
+    forward, and after any optimizer that does not refresh the shadows itself (FusedAdamW
+    does, inside its update) has changed the fp32 weights."""
+    params = getattr(module, _SHADOW_LIST, None)
+    if params is None:
+        params = [p for p in module.parameters() if p.dim() == 2 and p.dtype == torch.float32 and p.is_cuda
+                  and p.is_contiguous()]
+        setattr(module, _SHADOW_LIST, params)
+    # (Parameters whose storage is released -- FSDP units between their gathers -- are skipped;
+    # bf16_weight refreshes them when their unit runs.)
+    stale = [p for p in params if (getattr(p, _SHADOW_VER, None) != p._version
+                                   or getattr(p, _SHADOW, None) is None or getattr(p, _SHADOW).shape != p.shape)
+             and p.untyped_storage().nbytes() >= (p.storage_offset() + p.numel()) * 4]
+    if len(stale) < 2:
+        return  # nothing to batch; bf16_weight handles a single one
+    rows, chunks = [], []
+    chunk = nat.lib().md_adamw_chunk()
+    for i, p in enumerate(stale):
+        sh = getattr(p, _SHADOW, None)
+        if sh is None or sh.shape != p.shape:
+            sh = torch.empty(p.shape, dtype=torch.bfloat16, device=p.device)
+            setattr(p, _SHADOW, sh)
+        ptr = p.data_ptr()
+        rows.append((ptr, ptr, ptr, ptr, sh.data_ptr(), p.numel()))
+        chunks += [(i, c) for c in range(-(-p.numel() // chunk))]
+    dev = stale[0].device
+    table = torch.tensor(rows, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+    chunk_t = torch.tensor(chunks, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+    rc = nat.lib().md_adamw(table.data_ptr(), chunk_t.data_ptr(), len(chunks), 0.0, 0.0, 0.0, 0.0, 0.0, 1.0, 1.0,
+                            None, None, 1, nat.stream_ptr(), None)
+    nat.check(rc, "md_adamw(shadows)")
+    # (The pinned host tables are released through torch's caching host allocator, which keeps a
+    # block until the copy that reads it has run.)
+    for p in stale:
+        setattr(p, _SHADOW_VER, p._version)
+
+
 def fp32_param(p: torch.Tensor) -> torch.Tensor:
     """fp32, contiguous, 16-byte-aligned copy or view of a (small) parameter such as a bias or LN weight."""
     t = p.detach()

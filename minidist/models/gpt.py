@@ -213,6 +213,8 @@ class GPT(nn.Module):
     def forward(self, input_ids, targets=None):
         from . import fused_gpt
 
+        if fused_gpt.should_fuse(input_ids):
+            fused_gpt.refresh_shadows(self)
         x = self.embedding(input_ids)
         for block in self.blocks:
             x = block(x)

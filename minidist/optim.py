@@ -72,6 +72,22 @@ class FusedAdamW(torch.optim.Optimizer):
             st["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.contiguous_format)
         return st
 
+    def _init_states(self, params) -> None:
+        """First step of CUDA fp32 parameters: their moments as views of two flat zeroed buffers
+        (two fills for the whole group instead of two per parameter; 16-byte-aligned slices)."""
+        todo = [p for p in params if not self.state[p] and p.is_cuda and p.dtype == torch.float32]
+        if not todo:
+            return
+        sizes = [(p.numel() + 3) // 4 * 4 for p in todo]
+        flat = torch.zeros(2, sum(sizes), dtype=torch.float32, device=todo[0].device)
+        off = 0
+        for p, n in zip(todo, sizes):
+            st = self.state[p]
+            st["step"] = torch.zeros((), dtype=torch.float32)
+            st["exp_avg"] = flat[0, off: off + p.numel()].view_as(p)
+            st["exp_avg_sq"] = flat[1, off: off + p.numel()].view_as(p)
+            off += n
+
     # -- step -----------------------------------------------------------------------
 
     @torch.no_grad()
@@ -86,8 +102,7 @@ class FusedAdamW(torch.optim.Optimizer):
             for p in params:
                 if id(p) not in fused_ids:
                     flag.add_((~torch.isfinite(p.grad)).any().to(flag.dtype).to(flag.device))
-            for p in fused:
-                self._state(p)  # the kernel table points at the moments too
+            self._init_states(fused)  # the kernel table points at the moments too
             if fused:
                 for key, part in self._partitions(gi, fused):
                     table, chunk_t, n = self._table(key, part)
@@ -118,6 +133,7 @@ class FusedAdamW(torch.optim.Optimizer):
             params = [p for p in group["params"] if p.grad is not None]
             if not params:
                 continue
+            self._init_states(params)
             states = [self._state(p) for p in params]
             # One multi-tensor op for every parameter's step count (a per-tensor
             # loop of CPU adds cost ~0.6 ms of host time per step at GPT-2 size).

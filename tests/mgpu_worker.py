@@ -382,18 +382,24 @@ def check_composition(rank, world):
 
 
 def check_fsdp_training(rank, world):
-    """Four AdamW steps of FSDP with bf16 parameter gathers track DDP's weights
+    """Four AdamW steps of FSDP, with bf16 and with fp32 parameter gathers, track DDP's weights
     (reference tests/test_fsdp.py:92-127, 189-211)."""
+    for pdt in (torch.bfloat16, torch.float32):
+        _fsdp_training(rank, world, pdt)
+
+
+def _fsdp_training(rank, world, param_dtype):
     import minidist as md
     from minidist.models import GPT, Block, GPTConfig
     from minidist.optim import FusedAdamW
 
+    tag = "bf16" if param_dtype == torch.bfloat16 else "fp32"
     cfg = GPTConfig(vocab_size=1024, block_size=128, n_layer=2, n_head=4, n_embd=256, seed=8)
     mesh = md.ParallelMesh(tp_size=1)
     ddp = md.DistributedDataParallel(GPT(cfg, tp_group=mesh.tp_group, device="cuda"), process_group=mesh.dp_group)
     fsdp = md.FullyShardedDataParallel(GPT(cfg, tp_group=mesh.tp_group, device="cuda"), unit_types=(Block,),
                                        process_group=mesh.dp_group,
-                                       mixed_precision=md.MixedPrecisionPolicy(param_dtype=torch.bfloat16))
+                                       mixed_precision=md.MixedPrecisionPolicy(param_dtype=param_dtype))
     o1 = FusedAdamW(ddp.parameters(), lr=1e-3)
     o2 = FusedAdamW(fsdp.parameters(), lr=1e-3)
     g = torch.Generator().manual_seed(31)
@@ -411,12 +417,12 @@ def check_fsdp_training(rank, world):
             pair.append(loss.item())
         losses.append(pair)
     torch.cuda.synchronize()
-    _report(f"fsdp_vs_ddp_w{world}_losses", max(abs(a - b) / abs(a) for a, b in losses), 2e-2, rank)
+    _report(f"fsdp_{tag}_vs_ddp_w{world}_losses", max(abs(a - b) / abs(a) for a, b in losses), 2e-2, rank)
     worst = 0.0
     with fsdp.summon_full_params():
         for (n, p), (_, q) in zip(fsdp.module.named_parameters(), ddp.module.named_parameters()):
             worst = max(worst, (p.float() - q.float()).abs().max().item())
-    _report(f"fsdp_vs_ddp_w{world}_weights_abs", worst, 2e-2, rank)
+    _report(f"fsdp_{tag}_vs_ddp_w{world}_weights_abs", worst, 2e-2 if tag == "bf16" else 2e-3, rank)
     nat.check_status()
 
 
