@@ -1,10 +1,11 @@
-.PHONY: help build test test-gpu smoke bench bench-cpu clean
+.PHONY: help build test ci test-gpu smoke bench bench-cpu clean
 
 NPROC ?= 4
 
 help:
 	@echo "make build      compile the sm_100a kernels into minidist/_lib/libminidist_cuda.so"
 	@echo "make test       CPU correctness suite (Gloo, no GPU needed)"
+	@echo "make ci         what CI runs: lint, CPU suite, trainer smoke (tests/run_tests.sh)"
 	@echo "make test-gpu   GPU tier (kernel numerics, fused model, multi-GPU)"
 	@echo "make smoke      3-D parallel trainer smoke test on Gloo"
 	@echo "make bench      headline benchmark (bench.py) on 1 GPU"
@@ -15,6 +16,9 @@ build:
 
 test:
 	python -m pytest tests -q -m "not gpu"
+
+ci:
+	tests/run_tests.sh
 
 test-gpu: build
 	python -m pytest tests -q -m gpu
