@@ -73,6 +73,7 @@ __global__ void backward_kernel(const __nv_bfloat16* __restrict__ logits, long l
   const int nthr = static_cast<int>(blockDim.x);
   for (int m = blockIdx.x; m < M; m += gridDim.x) {
     const float l = lse[m];
+    MD_CHECK(target[m] >= 0, MD_CHECK_STATUS, 310, target[m]);  // (a negative target matches no column)
     const long long t = target[m] - col_offset;
     const uint4* zr = reinterpret_cast<const uint4*>(logits + m * ldl);
     uint4* dr = reinterpret_cast<uint4*>(dlogits + m * ldd);
@@ -121,3 +122,5 @@ int md_ce_backward(const void* logits, long long ldl, const float* lse, const lo
 }
 
 }  // extern "C"
+
+MD_DEFINE_CHECK_READER(md_check_status_cross_entropy)

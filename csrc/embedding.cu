@@ -28,6 +28,7 @@ __global__ void embed_fwd_kernel(const long long* __restrict__ ids, const __nv_b
   const int lane = threadIdx.x & 31;
   const int nvec = C / 8;
   for (int m = blockIdx.x * warps + (threadIdx.x >> 5); m < M; m += gridDim.x * warps) {
+    if (!MD_CHECK(ids[m] >= 0, MD_CHECK_STATUS, 300, ids[m])) continue;  // (rows of other shards are zero)
     const long long id = ids[m] - vocab_start;
     const bool own = id >= 0 && id < vocab_rows;
     const int s = m % S;
@@ -75,6 +76,7 @@ __global__ void embed_bwd_wte_kernel(const long long* __restrict__ ids, const __
   const int lane = threadIdx.x & 31;
   const int nvec = C / 8;
   for (int m = blockIdx.x * warps + (threadIdx.x >> 5); m < M; m += gridDim.x * warps) {
+    if (!MD_CHECK(ids[m] >= 0, MD_CHECK_STATUS, 301, ids[m])) continue;
     const long long id = ids[m] - vocab_start;
     if (id < 0 || id >= vocab_rows) continue;
     for (int j = lane; j < nvec; j += 32) {
@@ -290,6 +292,8 @@ int md_colsum_final(const float* partial, int chunks, int N, float* out, int acc
 }
 
 }  // extern "C"
+
+MD_DEFINE_CHECK_READER(md_check_status_embedding)
 
 // ---------------------------------------------------------------------------
 // Allocation-free variant of md_colsum (declared in md_noalloc.h).

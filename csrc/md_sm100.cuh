@@ -46,6 +46,39 @@ __device__ __forceinline__ void report(Status* st, uint32_t code, uint32_t where
   }
 }
 
+// Index checks of the bounds-checking build (-DMD_BOUNDS_CHECK; nothing in the
+// normal build): MD_CHECK(cond, where, detail) evaluates to `cond`, and when it
+// is false records kBadArgument at site `where` with `detail` (the offending
+// value, truncated) in the status word.  Callers skip the access on false; no
+// kernel traps.
+// Kernels without a status argument report into a per-file device word,
+// g_md_check_status, read by that file's md_check_status_<file>() entry
+// (MD_DEFINE_CHECK_READER).
+#ifdef MD_BOUNDS_CHECK
+#define MD_CHECK(cond, st, where, detail) \
+  ((cond) ? true : (::md::report((st), ::md::kBadArgument, (where), static_cast<uint32_t>(detail)), false))
+static __device__ ::md::Status g_md_check_status;
+#define MD_CHECK_STATUS (&::md::g_md_check_status)
+#define MD_DEFINE_CHECK_READER(name)                                                             \
+  extern "C" int name(void* out, int reset) {                                                    \
+    cudaError_t e = cudaMemcpyFromSymbol(out, ::md::g_md_check_status, sizeof(::md::Status));          \
+    if (e == cudaSuccess && reset) {                                                             \
+      ::md::Status z{};                                                                          \
+      e = cudaMemcpyToSymbol(::md::g_md_check_status, &z, sizeof(z));                                  \
+    }                                                                                            \
+    return static_cast<int>(e);                                                                  \
+  }
+#else
+#define MD_CHECK(cond, st, where, detail) true
+#define MD_CHECK_STATUS nullptr
+#define MD_DEFINE_CHECK_READER(name)                                                             \
+  extern "C" int name(void* out, int reset) {                                                    \
+    (void)reset;                                                                                 \
+    memset(out, 0, sizeof(::md::Status));                                                        \
+    return 0;                                                                                    \
+  }
+#endif
+
 // Programmatic dependent launch.  A kernel launched with launch_pdl() may
 // start while the previous kernel on its stream is still finishing: its CTAs
 // run their prologue (barrier init, TMEM allocation) on SMs the predecessor

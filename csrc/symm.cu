@@ -502,6 +502,7 @@ __global__ void __launch_bounds__(256) md_embed_tp_kernel(const __grid_constant_
       if (owner >= p.world) owner = p.world - 1;
       const long long row = id - owner * p.vocab_rows;
       const bool valid = id >= 0 && row < p.vocab_rows;
+      MD_CHECK(valid, p.status, 142, id);  // an id outside the vocabulary reads as a zero row
       const uint4* src = reinterpret_cast<const uint4*>(p.wte[valid ? owner : 0] + (valid ? row : 0) * p.ldw);
       const uint4* pos = reinterpret_cast<const uint4*>(p.wpe + static_cast<long long>(m % p.S) * p.ldp);
       uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<long long>(m) * p.ldo);

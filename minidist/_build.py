@@ -59,9 +59,13 @@ def _headers_digest() -> str:
     return h.hexdigest()
 
 
-def _compile_one(src: Path, flags: list[str], hdr_digest: str, verbose: bool) -> tuple[Path, bool, str]:
-    obj = OBJDIR / (src.stem + ".o")
-    stamp = OBJDIR / (src.stem + ".hash")
+CHECKED_LIBNAME = "libminidist_cuda_checked.so"
+
+
+def _compile_one(src: Path, flags: list[str], hdr_digest: str, verbose: bool,
+                 objdir: Path = OBJDIR) -> tuple[Path, bool, str]:
+    obj = objdir / (src.stem + ".o")
+    stamp = objdir / (src.stem + ".hash")
     h = hashlib.sha256()
     h.update(src.read_bytes())
     h.update(hdr_digest.encode())
@@ -75,30 +79,39 @@ def _compile_one(src: Path, flags: list[str], hdr_digest: str, verbose: bool) ->
     if proc.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src.name}:\n{' '.join(cmd)}\n{log}")
     stamp.write_text(digest)
-    (OBJDIR / (src.stem + ".ptxas.txt")).write_text(log)
+    (objdir / (src.stem + ".ptxas.txt")).write_text(log)
     if verbose:
         print(f"  compiled {src.name}")
     return obj, True, log
 
 
-def build(verbose: bool = True, jobs: int | None = None) -> Path:
-    """Compile and link the native library; return its path."""
-    OBJDIR.mkdir(parents=True, exist_ok=True)
+def build(verbose: bool = True, jobs: int | None = None, bounds_check: bool = False) -> Path:
+    """Compile and link the native library; return its path.
+
+    ``bounds_check=True`` builds the checking variant ``libminidist_cuda_checked.so``
+    (``-DMD_BOUNDS_CHECK``: kernels verify data-dependent indices -- token ids, targets,
+    table entries -- and on a violation record ``kBadArgument`` with the site and the bad
+    value in the status word and skip the access, never trapping).  It is loaded instead
+    of the normal library when ``MINIDIST_BOUNDS_CHECK=1``."""
+    objdir = OBJDIR / "checked" if bounds_check else OBJDIR
+    flags = NVCC_FLAGS + (["-DMD_BOUNDS_CHECK"] if bounds_check else [])
+    libname = CHECKED_LIBNAME if bounds_check else LIBNAME
+    objdir.mkdir(parents=True, exist_ok=True)
     sources = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
     if not sources:
         raise RuntimeError(f"no sources under {CSRC}")
     hdr = _headers_digest()
     jobs = jobs or min(len(sources), os.cpu_count() or 4)
     with cf.ThreadPoolExecutor(max_workers=jobs) as pool:
-        results = list(pool.map(lambda s: _compile_one(s, NVCC_FLAGS, hdr, verbose), sources))
+        results = list(pool.map(lambda s: _compile_one(s, flags, hdr, verbose, objdir), sources))
     objs = [r[0] for r in results]
-    lib = LIBDIR / LIBNAME
+    lib = LIBDIR / libname
     relink = any(r[1] for r in results) or not lib.exists()
     if not relink:
         newest = max(o.stat().st_mtime for o in objs)
         relink = newest > lib.stat().st_mtime
     if relink:
-        tmp = LIBDIR / (LIBNAME + ".tmp")
+        tmp = LIBDIR / (libname + ".tmp")
         cmd = [nvcc_path(), *ARCH_FLAGS, "-shared", "-cudart", "static", *map(str, objs), "-o", str(tmp), "-lcuda"]
         proc = subprocess.run(cmd, capture_output=True, text=True)
         if proc.returncode != 0:
@@ -110,5 +123,5 @@ def build(verbose: bool = True, jobs: int | None = None) -> Path:
 
 
 if __name__ == "__main__":
-    build(verbose=True)
+    build(verbose=True, bounds_check="--bounds-check" in sys.argv[1:])
     sys.exit(0)

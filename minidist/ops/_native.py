@@ -19,7 +19,10 @@ from pathlib import Path
 
 import torch
 
-_LIB_PATH = Path(__file__).resolve().parent.parent / "_lib" / "libminidist_cuda.so"
+# MINIDIST_BOUNDS_CHECK=1 loads the checking build (python -m minidist._build --bounds-check).
+_LIB_PATH = Path(__file__).resolve().parent.parent / "_lib" / (
+    "libminidist_cuda_checked.so" if os.environ.get("MINIDIST_BOUNDS_CHECK", "0") not in ("0", "", "false", "no")
+    else "libminidist_cuda.so")
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 
@@ -34,6 +37,11 @@ class CommTimeoutError(NativeError):
 
 def library_path() -> Path:
     return _LIB_PATH
+
+
+def bounds_checked() -> bool:
+    """True when the bounds-checking build is the one loaded (``MINIDIST_BOUNDS_CHECK=1``)."""
+    return _LIB_PATH.name == "libminidist_cuda_checked.so"
 
 
 def available() -> bool:
@@ -177,6 +185,14 @@ def check_status(device=None, reset: bool = True) -> None:
     buf = status_buffer(device)
     torch.cuda.synchronize(buf.device)
     code, where, block, detail = (int(v) for v in buf.tolist())
+    if code == 0 and bounds_checked():
+        # The checking build's kernels without a status argument report into per-file words.
+        for reader in ("md_check_status_embedding", "md_check_status_cross_entropy"):
+            word = (ctypes.c_uint32 * 4)()
+            check(getattr(lib(), reader)(ctypes.cast(word, ctypes.c_void_p), int(reset)), reader)
+            if word[0]:
+                code, where, block, detail = (int(v) for v in word)
+                break
     if code == 0:
         return
     if reset:
@@ -251,3 +267,7 @@ def peer_wait_counters(enable: bool, reset: bool = False) -> dict[str, dict[str,
         acc["md_gemm_ar"] = [float(gar[0]), float(gar[1]), float(gar[2])]
     return {fam: {"run_ms": a[0] / 1e6, "wait_ms": a[1] / 1e6, "wait_frac": a[1] / a[0] if a[0] else 0.0,
                   "launches": a[2]} for fam, a in acc.items()}
+
+
+declare("md_check_status_embedding", "i:pi")
+declare("md_check_status_cross_entropy", "i:pi")
