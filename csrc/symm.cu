@@ -87,6 +87,7 @@ struct MdRsParams {
   float* m;
   float* v;
   float lr, b1, b2, eps, wd, bc1, bc2_sqrt;
+  __nv_bfloat16* p_bf16; // fused AdamW: bf16 copy of the updated shard (the gather source), or null
 };
 
 // All-gather of FSDP parameter shards (md_ag_shards): every rank's fp32 shard
@@ -107,6 +108,7 @@ struct MdAgParams {
   md::Status* status;
   void* out;             // world * shard elements, fp32 or bf16
   int out_bf16;
+  int in_bf16;           // bufs hold bf16 shards (copied as they are; out must be bf16, shard % 8 == 0)
 };
 
 // Vocab-parallel cross-entropy statistics (md_ce_tp): each rank folds its
@@ -356,6 +358,8 @@ __global__ void __launch_bounds__(512) md_rs_shard_kernel(const __grid_constant_
       reinterpret_cast<float4*>(p.p)[u] = pp;
       reinterpret_cast<float4*>(p.m)[u] = mm;
       reinterpret_cast<float4*>(p.v)[u] = vv;
+      if (p.p_bf16 != nullptr)
+        reinterpret_cast<uint2*>(p.p_bf16)[u] = make_uint2(pack_bf16x2(pp.x, pp.y), pack_bf16x2(pp.z, pp.w));
     } else {
       float4* g = reinterpret_cast<float4*>(p.grad_out) + u;
       if (p.accumulate) {
@@ -411,6 +415,24 @@ __global__ void __launch_bounds__(512) md_ag_shards_kernel(const __grid_constant
   // ranks read from W different sources (no peer's links serve every reader);
   // four vectors per thread in flight (peer loads have ~us latency).
   constexpr int U = 4;
+  if (p.in_bf16) {
+    // bf16 shards (the optimizer keeps them next to the fp32 masters): 16-byte copies, no cast.
+    const long long n8 = p.shard / 8;
+    for (int step = 0; step < p.world; ++step) {
+      const int r = (p.rank + step) % p.world;
+      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.bufs[r]) + p.offset);
+      uint4* dst = reinterpret_cast<uint4*>(p.out) + static_cast<long long>(r) * n8;
+      for (long long j = static_cast<long long>(vc) * blockDim.x + threadIdx.x; j < n8; j += U * stride) {
+        uint4 a[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k)
+          if (j + k * stride < n8) a[k] = __ldcg(src + j + k * stride);
+#pragma unroll
+        for (int k = 0; k < U; ++k)
+          if (j + k * stride < n8) dst[j + k * stride] = a[k];
+      }
+    }
+  } else
   for (int step = 0; step < p.world; ++step) {
     const int r = (p.rank + step) % p.world;
     const float4* src = reinterpret_cast<const float4*>(p.bufs[r] + p.offset);
@@ -566,6 +588,7 @@ int md_ag_shards(const MdAgParams* prm, int ctas, cudaStream_t s) {
   if (prm == nullptr || prm->world < 1 || prm->world > md::symm::kMaxWorld || (prm->shard % 4) || (prm->offset % 4) ||
       prm->out == nullptr)
     return -1;
+  if (prm->in_bf16 && (!prm->out_bf16 || (prm->shard % 8) || (prm->offset % 8))) return -1;
   if (ctas < 1 || ctas > md::symm::kMaxCtas || prm->channel < 0 || prm->channel >= md::symm::kChannels) return -2;
   md::symm::md_ag_shards_kernel<<<ctas, 512, 0, s>>>(*prm);
   return static_cast<int>(cudaGetLastError());

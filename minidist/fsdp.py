@@ -103,6 +103,7 @@ class _FSDPUnit:
         self._peer: tuple | None = None
         # Peer-memory gather: (communicator, symmetric shard buffer, element offset) or None.
         self._peer_shard: tuple | None = None
+        self._peer_shard_bf16: tuple | None = None  # bf16 copies of the shards (bf16 gathers)
         self._owner_state: dict | None = None  # shared with the FSDP module: last gather event
         self._adam: dict | None = None  # fused AdamW: hyper-parameters, m, v, step
 
@@ -118,7 +119,20 @@ class _FSDPUnit:
             from .parallel import collectives
 
             comm_, buf, off = self._peer_shard
-            collectives.all_gather_shards(buf, comm_, off, self.shard_numel, self._full)
+            bf = getattr(self, "_peer_shard_bf16", None)
+            if bf is not None:
+                from .models import fused_gpt
+
+                shard = self.flat_shard
+                if getattr(shard, fused_gpt._SHADOW_VER, None) != shard._version:
+                    # The bf16 copy is stale (first gather, or the shard changed outside the
+                    # optimizer): refresh it locally before peers read it.
+                    getattr(shard, fused_gpt._SHADOW).copy_(shard.detach())
+                    setattr(shard, fused_gpt._SHADOW_VER, shard._version)
+                comm_, buf, off = bf
+                collectives.all_gather_shards(buf, comm_, off, self.shard_numel, self._full, src_bf16=True)
+            else:
+                collectives.all_gather_shards(buf, comm_, off, self.shard_numel, self._full)
             # The kernel writes through a raw pointer: advance the version the parameter views
             # share, so cached casts of them (the fused path's bf16 shadows) are refreshed.
             torch.autograd.graph.increment_version(self._full)
@@ -242,9 +256,18 @@ class _FSDPUnit:
                 a = self._adam
                 a["step"] += 1
                 b1, b2 = a["betas"]
+                sh = None
+                if self._peer_shard_bf16 is not None:
+                    from .models import fused_gpt
+
+                    sh = getattr(shard, fused_gpt._SHADOW, None)
                 collectives.reduce_scatter_shard(buf, comm_, off, self.shard_numel, None, False, 1.0 / self.world,
                                                  adam=(shard.data, a["m"], a["v"], a["lr"], b1, b2, a["eps"],
-                                                       a["weight_decay"], a["step"]))
+                                                       a["weight_decay"], a["step"]), p_bf16=sh)
+                if sh is not None:
+                    from .models import fused_gpt
+
+                    setattr(shard, fused_gpt._SHADOW_VER, shard._version)  # updated in the same pass
             else:
                 collectives.reduce_scatter_shard(buf, comm_, off, self.shard_numel, shard.grad, acc,
                                                  1.0 / self.world)
@@ -327,7 +350,7 @@ class FullyShardedDataParallel(nn.Module):
             from .parallel import collectives
 
             self._peer_comm = collectives.fsdp_communicator(process_group)
-        self._align = 4 if self._peer_comm is not None else 1
+        self._align = 8 if self._peer_comm is not None else 1
         self._units = self._build_units(module, tuple(unit_types), reshard_after_forward,
                                         reshard_root_after_forward, device)
         if self._peer_comm is not None:
@@ -353,6 +376,21 @@ class FullyShardedDataParallel(nn.Module):
                     u._peer_shard = (self._peer_comm, self._shard_buf, off)
                     u._owner_state = self._gather_state
                     off += u.shard_numel
+                if all(u.policy.param_dtype == torch.bfloat16 for u in self._units):
+                    # bf16 gathers read a bf16 copy of every fp32 shard, kept next to it in
+                    # symmetric memory: the optimizer writes it in the same pass as the update
+                    # (FusedAdamW's weight shadow, or the fused AdamW of the reduce-scatter), so
+                    # a gather moves half the bytes and casts nothing.
+                    from .models import fused_gpt
+
+                    self._shard_bf16_buf = self._peer_comm.buffer(f"fsdp_shards_bf16_{id(self)}", total_shard * 2)
+                    off = 0
+                    for u in self._units:
+                        view = self._shard_bf16_buf.view(torch.bfloat16, off * 2, u.shard_numel)
+                        setattr(u.flat_shard, fused_gpt._SHADOW, view)
+                        setattr(u.flat_shard, fused_gpt._SHADOW_VER, None)  # filled at the first gather
+                        u._peer_shard_bf16 = (self._peer_comm, self._shard_bf16_buf, off)
+                        off += u.shard_numel
                 torch.cuda.synchronize(device)
         if fused_adamw is not None:
             if self._peer_comm is None or any(u.flat_shard.dtype != torch.float32 for u in self._units):

@@ -405,6 +405,7 @@ class RsParams(ctypes.Structure):
         ("wd", ctypes.c_float),
         ("bc1", ctypes.c_float),
         ("bc2_sqrt", ctypes.c_float),
+        ("p_bf16", ctypes.c_void_p),
     ]
 
 
@@ -425,7 +426,7 @@ def fsdp_gather_enabled() -> bool:
 
 def reduce_scatter_shard(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offset: int, shard: int,
                          grad_out: torch.Tensor | None, accumulate: bool, scale: float,
-                         adam: tuple | None = None) -> None:
+                         adam: tuple | None = None, p_bf16: torch.Tensor | None = None) -> None:
     """Rank r's slice ``[elem_offset + r*shard, +shard)`` of ``buf`` summed over ranks, times ``scale``,
     into ``grad_out`` (or, with ``adam = (p, m, v, lr, b1, b2, eps, wd, step)``, an AdamW update of ``p``)."""
     prm = RsParams()
@@ -444,6 +445,7 @@ def reduce_scatter_shard(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_of
         prm.lr, prm.b1, prm.b2, prm.eps, prm.wd = lr, b1, b2, eps, wd
         prm.bc1 = 1.0 - b1 ** step
         prm.bc2_sqrt = (1.0 - b2 ** step) ** 0.5
+        prm.p_bf16 = None if p_bf16 is None else p_bf16.data_ptr()
     else:
         prm.grad_out = grad_out.data_ptr()
         prm.accumulate = int(accumulate)
@@ -476,6 +478,7 @@ class AgParams(ctypes.Structure):
         ("status", ctypes.c_void_p),
         ("out", ctypes.c_void_p),
         ("out_bf16", ctypes.c_int),
+        ("in_bf16", ctypes.c_int),
     ]
 
 
@@ -483,11 +486,14 @@ nat.declare("md_ag_shards", "i:pip")
 
 
 def all_gather_shards(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offset: int, shard: int,
-                      out: torch.Tensor) -> None:
-    """Every rank's fp32 shard ``buf[elem_offset : elem_offset + shard]`` into ``out`` (rank r's at
-    ``out[r*shard]``), cast to ``out.dtype`` (fp32 or bf16) on the way, on the current stream."""
+                      out: torch.Tensor, src_bf16: bool = False) -> None:
+    """Every rank's shard ``buf[elem_offset : elem_offset + shard]`` into ``out`` (rank r's at
+    ``out[r*shard]``), on the current stream: fp32 shards cast to ``out.dtype`` (fp32 or bf16)
+    on the way, or with ``src_bf16`` bf16 shards copied into a bf16 ``out``."""
     if out.dtype not in (torch.float32, torch.bfloat16) or out.numel() < shard * comm_.world:
         raise ValueError("all_gather_shards: out must be fp32 / bf16 with world * shard elements")
+    if src_bf16 and (out.dtype != torch.bfloat16 or shard % 8 or elem_offset % 8):
+        raise ValueError("all_gather_shards: bf16 shards need a bf16 out and 8-element alignment")
     prm = AgParams()
     for r in range(comm_.world):
         prm.bufs[r] = buf.ptrs[r]
@@ -499,6 +505,7 @@ def all_gather_shards(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offse
     prm.status = nat.status_ptr(buf.device)
     prm.out = out.data_ptr()
     prm.out_bf16 = int(out.dtype == torch.bfloat16)
+    prm.in_bf16 = int(src_bf16)
     # One CTA per 64 K output elements, at most 64: the gather overlaps the compute stream.
     ctas = min(64, max(1, shard * comm_.world // 65536))
     with _Range("md_ag_shards"):
@@ -506,6 +513,8 @@ def all_gather_shards(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offse
     nat.check(rc, "md_ag_shards")
     n = shard * comm_.world * out.element_size()
     comm.comm_stats.add("all_gather", n, int((comm_.world - 1) / comm_.world * n))
+    # (bf16 sources move half the bytes of fp32 ones; the count above is the gathered payload,
+    # the reference's accounting for a gather in param_dtype.)
 
 
 # ---------------------------------------------------------------------------
