@@ -141,6 +141,36 @@ def fp32_param(p: torch.Tensor) -> torch.Tensor:
     return t
 
 
+def _fp32_params(*params):
+    """``fp32_param`` of several small parameters (None passes through).  Low-precision ones (FSDP
+    views gathered in bf16) are converted together -- one concatenation and one cast -- and
+    returned as views of the result (each slice starts 16-byte aligned)."""
+    low = [p for p in params if p is not None and p.dtype != torch.float32]
+    if len(low) < 2:
+        return tuple(None if p is None else fp32_param(p) for p in params)
+    pads = []
+    for p in low:
+        n = p.numel()
+        pads.append(p.detach().reshape(-1))
+        if n % 4:
+            pads.append(p.new_zeros(4 - n % 4))
+    flat = torch.cat(pads).float()
+    out, off = [], 0
+    views = {}
+    for p in low:
+        n = p.numel()
+        views[id(p)] = flat[off: off + n].view(p.shape)
+        off += -(-n // 4) * 4
+    for p in params:
+        if p is None:
+            out.append(None)
+        elif id(p) in views:
+            out.append(views[id(p)])
+        else:
+            out.append(fp32_param(p))
+    return tuple(out)
+
+
 class _GradTarget:
     """Where a kernel writes ``p``'s fp32 gradient; :meth:`commit` publishes it."""
 
@@ -283,12 +313,9 @@ class _BlockFn(torch.autograd.Function):
         tp = _tp_world(group)
         H = attn.n_head_local
         D = attn.head_dim
-        ln1g, ln1b = fp32_param(blk.ln1.weight), fp32_param(blk.ln1.bias)
-        ln2g, ln2b = fp32_param(blk.ln2.weight), fp32_param(blk.ln2.bias)
-        qkv_b = fp32_param(attn.qkv.bias) if attn.qkv.bias is not None else None
-        proj_b = fp32_param(attn.proj.bias) if attn.proj.bias is not None else None
-        fc_b = fp32_param(mlp.fc.bias) if mlp.fc.bias is not None else None
-        mproj_b = fp32_param(mlp.proj.bias) if mlp.proj.bias is not None else None
+        ln1g, ln1b, ln2g, ln2b, qkv_b, proj_b, fc_b, mproj_b = _fp32_params(
+            blk.ln1.weight, blk.ln1.bias, blk.ln2.weight, blk.ln2.bias, attn.qkv.bias, attn.proj.bias,
+            mlp.fc.bias, mlp.proj.bias)
         w_qkv, w_proj = bf16_weight(attn.qkv.weight), bf16_weight(attn.proj.weight)
         w_fc, w_mproj = bf16_weight(mlp.fc.weight), bf16_weight(mlp.proj.weight)
 
