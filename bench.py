@@ -205,13 +205,15 @@ def setup(args):
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    # A short process-group timeout ends a collective that a failed rank never joins.
+    pg_timeout = timedelta(seconds=float(os.environ.get("MINIDIST_PG_TIMEOUT_S", "600")))
     if args.device == "cuda":
         torch.cuda.set_device(local)
         if world > 1:
-            dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=600),
+            dist.init_process_group("nccl", rank=rank, world_size=world, timeout=pg_timeout,
                                     device_id=torch.device("cuda", local))
     elif world > 1:
-        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=600))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=pg_timeout)
     return rank, world, local
 
 
