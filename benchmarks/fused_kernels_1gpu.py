@@ -17,6 +17,11 @@ benchmarks/bench_tp_gemm.py and benchmarks/bench_collectives.py.
 * ``ddp_ar``   -- md_ar_bucket_kernel on a 25 MB fp32 bucket (1/W scale).
 * ``fsdp_rs``  -- md_rs_shard_kernel with the in-kernel AdamW on a 40 M-element shard.
 * ``fsdp_ag``  -- md_ag_shards_kernel: a 40 M-element fp32 shard gathered as bf16.
+* ``fsdp_ag_bf16`` -- md_ag_shards_kernel on bf16 shard copies (the bf16-gather path).
+* ``ce_tp``    -- md_ce_tp_kernel: the vocab-parallel cross-entropy statistics of
+  8192 tokens over 50304 / 8 columns (50 slabs of 128).
+* ``embed_tp`` -- md_embed_tp_kernel: 8192 token rows of 4096 bf16 gathered from
+  the (here local) shard that owns them, positions added.
 """
 
 from __future__ import annotations
@@ -140,9 +145,80 @@ def run_fsdp_ag(iters: int) -> None:
           f"{6 * shard / t / 1e9:.0f} GB/s (read + write)")
 
 
+def run_fsdp_ag_bf16(iters: int) -> None:
+    shard = 40 * 1024 * 1024
+    src = torch.randn(shard, device="cuda").bfloat16()
+    out = torch.empty(shard, dtype=torch.bfloat16, device="cuda")
+    flags = torch.zeros(int(nat.lib().md_symm_flag_bytes()) // 4, dtype=torch.int32, device="cuda")
+    a = C.AgParams()
+    a.bufs[0], a.flags[0] = src.data_ptr(), flags.data_ptr()
+    a.offset, a.shard, a.world, a.rank, a.channel = 0, shard, 1, 0, 5
+    a.timeout_ns, a.status = 10**10, nat.status_ptr()
+    a.out, a.out_bf16, a.in_bf16 = out.data_ptr(), 1, 1
+    def call():
+        nat.check(nat.lib().md_ag_shards(ctypes.byref(a), 64, ctypes.c_void_p(nat.stream_ptr())), "md_ag_shards")
+
+    t = timed(call, iters)
+    nat.check_status()
+    assert torch.equal(out, src)
+    print(f"md_ag_shards world=1 {shard / 1e6:.0f} M elements bf16->bf16: {t * 1e6:.1f} us, "
+          f"{4 * shard / t / 1e9:.0f} GB/s (read + write)")
+
+
+def run_ce_tp(iters: int) -> None:
+    M, tiles = 8192, -(-50304 // 8 // 128)
+    tmax = torch.randn(tiles, M, device="cuda")
+    tsum = torch.rand(tiles, M, device="cuda") * 100
+    ttgt = torch.randn(M, device="cuda")
+    buf = torch.empty(3 * M, device="cuda")
+    flags = torch.zeros(int(nat.lib().md_symm_flag_bytes()) // 4, dtype=torch.int32, device="cuda")
+    lse, loss = torch.empty(M, device="cuda"), torch.empty(M, device="cuda")
+    prm = C.CeTpParams()
+    prm.bufs[0], prm.flags[0] = buf.data_ptr(), flags.data_ptr()
+    prm.world, prm.rank, prm.channel = 1, 0, 6
+    prm.timeout_ns, prm.status = 10**10, nat.status_ptr()
+    prm.tmax, prm.tsum, prm.tiles, prm.ttgt, prm.M = tmax.data_ptr(), tsum.data_ptr(), tiles, ttgt.data_ptr(), M
+    prm.lse, prm.loss = lse.data_ptr(), loss.data_ptr()
+    ctas = min(64, max(1, -(-M // 256)))
+    def call():
+        nat.check(nat.lib().md_ce_tp(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr())), "md_ce_tp")
+
+    t = timed(call, iters)
+    nat.check_status()
+    want = torch.logsumexp(tmax + torch.log(tsum), 0)
+    assert (lse - want).abs().max().item() < 1e-3
+    print(f"md_ce_tp world=1 M={M} tiles={tiles}: {t * 1e6:.1f} us, "
+          f"{(2 * tiles + 1 + 5) * M * 4 / t / 1e9:.0f} GB/s")
+
+
+def run_embed_tp(iters: int) -> None:
+    V, C_, M, S = 50304 // 8, 4096, 8192, 2048
+    wte = torch.randn(V, C_, device="cuda").bfloat16()
+    wpe = torch.randn(S, C_, device="cuda").bfloat16()
+    ids = torch.randint(0, V, (M,), device="cuda")
+    out = torch.empty(M, C_, dtype=torch.bfloat16, device="cuda")
+    flags = torch.zeros(int(nat.lib().md_symm_flag_bytes()) // 4, dtype=torch.int32, device="cuda")
+    prm = C.EmbTpParams()
+    prm.wte[0], prm.flags[0] = wte.data_ptr(), flags.data_ptr()
+    prm.world, prm.rank, prm.channel = 1, 0, 7
+    prm.timeout_ns, prm.status = 10**10, nat.status_ptr()
+    prm.ids, prm.wpe, prm.ldp, prm.out, prm.ldo = ids.data_ptr(), wpe.data_ptr(), C_, out.data_ptr(), C_
+    prm.ldw, prm.vocab_rows, prm.M, prm.S, prm.C = C_, V, M, S, C_
+    ctas = min(148, max(1, -(-M // 32)))
+    def call():
+        nat.check(nat.lib().md_embed_tp(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr())), "md_embed_tp")
+
+    t = timed(call, iters)
+    nat.check_status()
+    want = (wte.float()[ids] + wpe.float()[torch.arange(M, device="cuda") % S]).bfloat16()
+    assert torch.equal(out, want)
+    print(f"md_embed_tp world=1 {M} rows x {C_}: {t * 1e6:.1f} us, {3 * M * C_ * 2 / t / 1e9:.0f} GB/s")
+
+
 def main() -> None:
     a = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    a.add_argument("--kernel", default="all", choices=["all", "gemm_ar", "ddp_ar", "fsdp_rs", "fsdp_ag"])
+    a.add_argument("--kernel", default="all", choices=["all", "gemm_ar", "ddp_ar", "fsdp_rs", "fsdp_ag",
+                                                       "fsdp_ag_bf16", "ce_tp", "embed_tp"])
     a.add_argument("--iters", type=int, default=20)
     args = a.parse_args()
     if args.kernel in ("all", "gemm_ar"):
@@ -153,6 +229,12 @@ def main() -> None:
         run_fsdp_rs(args.iters)
     if args.kernel in ("all", "fsdp_ag"):
         run_fsdp_ag(args.iters)
+    if args.kernel in ("all", "fsdp_ag_bf16"):
+        run_fsdp_ag_bf16(args.iters)
+    if args.kernel in ("all", "ce_tp"):
+        run_ce_tp(args.iters)
+    if args.kernel in ("all", "embed_tp"):
+        run_embed_tp(args.iters)
 
 
 if __name__ == "__main__":
