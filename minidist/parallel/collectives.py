@@ -72,6 +72,9 @@ class _Range:
             torch.cuda.nvtx.range_pop()
 
 
+_AR_CTA_CAP = int(os.environ.get("MINIDIST_AR_CTAS", "0"))
+
+
 def _timeout_ns() -> int:
     return int(float(os.environ.get("MINIDIST_PEER_TIMEOUT_S", "60")) * 1e9)
 
@@ -91,6 +94,8 @@ def allreduce_fp32_(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_offset:
     p.timeout_ns = _timeout_ns()
     p.status = nat.status_ptr()
     ctas = lib.md_allreduce_ctas(n, buf.world)
+    if _AR_CTA_CAP > 0:  # MINIDIST_AR_CTAS: fewer CTAs leave more SMs to the backward it overlaps
+        ctas = max(1, min(ctas, _AR_CTA_CAP))
     with _Range("md_ar_bucket"):
         nat.check(lib.md_allreduce(ctypes.byref(p), ctas, ctypes.c_void_p(nat.stream_ptr(stream))), "md_allreduce")
 
