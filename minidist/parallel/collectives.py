@@ -454,7 +454,9 @@ def reduce_scatter_shard(buf: symm.SymmBuffer, comm_: symm.Communicator, elem_of
     else:
         prm.grad_out = grad_out.data_ptr()
         prm.accumulate = int(accumulate)
-    ctas = min(nat.num_sms(), 160, max(1, shard // (4 * 512 * 8)))
+    # At most 64 CTAs: the reduce-scatter runs beside the backward on the communication stream,
+    # and 64 x 512 threads with 2 x W vectors in flight each already saturate NVLink.
+    ctas = min(64, max(1, shard // (4 * 512 * 8)))
     with _Range("md_rs_shard"):
         rc = nat.lib().md_rs_shard(ctypes.byref(prm), ctas, ctypes.c_void_p(nat.stream_ptr(None)))
     nat.check(rc, "md_rs_shard")
