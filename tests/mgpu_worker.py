@@ -30,7 +30,7 @@ def check_allreduce(rank, world):
         torch.cuda.synchronize()
         want = torch.stack(parts).sum(0) / world
         err = (t - want).abs().max().item()
-        assert err < 1e-5, f"rank {rank} iter {it}: err {err}"
+        _report(f"peer_allreduce_fp32_w{world}_iter{it}_abs", err, 1e-5, rank)
         # every rank holds the identical result
         allv = [torch.empty_like(t) for _ in range(world)]
         dist.all_gather(allv, t)
@@ -57,9 +57,10 @@ def check_ddp(rank, world):
         model(ids.chunk(world)[rank], tgt.chunk(world)[rank])[1].backward()
     model.wait_gradients()  # the last bucket is deferred (defer_last_buckets=2)
     torch.cuda.synchronize()
+    worst = 0.0
     for (n, p), (_, q) in zip(model.module.named_parameters(), ref.named_parameters()):
-        err = ((p.grad - q.grad).abs().max() / q.grad.abs().max().clamp(min=1e-8)).item()
-        assert err < 5e-2, f"rank {rank} {n}: {err}"
+        worst = max(worst, ((p.grad - q.grad).abs().max() / q.grad.abs().max().clamp(min=1e-8)).item())
+    _report(f"ddp_grads_vs_full_batch_w{world}", worst, 5e-2, rank)
     opt = FusedAdamW(model.parameters(), lr=1e-3)
     for _ in range(3):
         opt.zero_grad(set_to_none=True)
@@ -115,7 +116,7 @@ def check_fsdp(rank, world):
         full = torch.cat([full, full.new_zeros(u.padded_numel - u.total_numel)])
         want = full[rank * u.shard_numel:(rank + 1) * u.shard_numel]
         err = ((u.flat_shard.grad - want).abs().max() / want.abs().max().clamp(min=1e-8)).item()
-        assert err < 5e-2, f"rank {rank} unit {u.name}: shard grad err {err}"
+        _report(f"fsdp_shard_grad_w{world}_unit_{u.name}", err, 5e-2, rank)
     # in-kernel AdamW vs FusedAdamW on the same FSDP shards
     hp = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
     fa = md.FullyShardedDataParallel(GPT(cfg, tp_group=mesh.tp_group, device="cuda"), unit_types=(Block,),
@@ -138,7 +139,7 @@ def check_fsdp(rank, world):
     for ua, ub in zip(fa._units, fb._units):
         assert ua.flat_shard.grad is None, "fused AdamW left a shard gradient behind"
         d = (ua.flat_shard.data - ub.flat_shard.data).abs().max().item()
-        assert d < 1e-4, f"rank {rank} unit {ua.name}: fused AdamW differs by {d}"
+        _report(f"fsdp_inkernel_adamw_w{world}_unit_{ua.name}_abs", d, 1e-4, rank)
     nat.check_status()
 
 
@@ -157,7 +158,7 @@ def check_gemm_ar(rank, world):
         if resid is not None:
             want = want + resid.float()
         err = ((out.float() - want).abs().max() / want.abs().max()).item()
-        assert err < 2e-2, f"rank {rank} case {it}: rel err {err}"
+        _report(f"gemm_allreduce_w{world}_case{it}_M{M}_K{K}_N{N}", err, 2e-2, rank)
         allo = [torch.empty(M, N, dtype=torch.bfloat16, device="cuda") for _ in range(world)]
         dist.all_gather(allo, out.contiguous())
         assert all(torch.equal(allo[0], a) for a in allo), f"case {it}: ranks differ"
@@ -183,18 +184,18 @@ def check_tp_gpt(rank, world):
     l_ref.backward()
     l_tp.backward()
     torch.cuda.synchronize()
-    assert abs(l_ref.item() - l_tp.item()) < 2e-2 * abs(l_ref.item()), (l_ref.item(), l_tp.item())
+    _report(f"tp_gpt_w{world}_loss", abs(l_ref.item() - l_tp.item()) / abs(l_ref.item()), 2e-2, rank)
     # the row-parallel weight gradient is this rank's column slice of the full gradient
     gfull = ref.blocks[0].mlp.proj.weight.grad
     gpart = model.blocks[0].mlp.proj.weight.grad
     cols = gpart.shape[1]
     want = gfull[:, rank * cols:(rank + 1) * cols]
     err = ((gpart - want).abs().max() / want.abs().max()).item()
-    assert err < 5e-2, f"rank {rank}: mlp.proj grad err {err}"
+    _report(f"tp_gpt_w{world}_mlp_proj_grad", err, 5e-2, rank)
     # position-embedding gradient: downstream of every fused data-gradient all-reduce
     gw, gr = model.embedding.wpe.grad, ref.embedding.wpe.grad
     err = ((gw - gr).abs().max() / gr.abs().max()).item()
-    assert err < 5e-2, f"rank {rank}: wpe grad err {err}"
+    _report(f"tp_gpt_w{world}_wpe_grad", err, 5e-2, rank)
     nat.check_status()
 
 
@@ -232,8 +233,8 @@ def _graph_vs_eager(rank, world, wrap, tp_size):
         if graph:
             run.release()
         out.append(losses)
-    for a, b in zip(*out, strict=True):
-        assert abs(a - b) <= 3e-3 * abs(a), (rank, out)
+    _report(f"cuda_graph_vs_eager_w{world}_tp{tp_size}_losses",
+            max(abs(a - b) / abs(a) for a, b in zip(*out, strict=True)), 3e-3, rank)
     nat.check_status()
 
 
