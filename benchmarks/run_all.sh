@@ -18,10 +18,12 @@ RUN="python -m torch.distributed.run --nnodes=1 --nproc-per-node=$NPROC --master
   python -c 'import torch; print("torch:", torch.__version__, "cuda:", torch.version.cuda)'
   python -c 'import torch; [print("gpu", i, torch.cuda.get_device_name(i)) for i in range(torch.cuda.device_count())]'
 } | tee "$OUT/environment.txt"
-$RUN benchmarks/bench_collectives.py --max-mb 256 --csv "$OUT/collectives.csv" $BACKEND_ARG 2>&1 | tee "$OUT/collectives.txt"
-$RUN benchmarks/bench_parallelism.py --profile-dir "$OUT/traces" $BACKEND_ARG 2>&1 | tee "$OUT/parallelism.txt"
+PREC=""
+[ -z "${BACKEND:-}" ] && python -c 'import torch, sys; sys.exit(0 if torch.cuda.is_available() else 1)' && PREC="--precision bf16"
+$RUN benchmarks/bench_collectives.py --max-mb 256 --json "$OUT/collectives.jsonl" $BACKEND_ARG 2>&1 | tee "$OUT/collectives.txt"
+$RUN benchmarks/bench_parallelism.py --trace-dir "$OUT/traces" --json "$OUT/parallelism.jsonl" $PREC $BACKEND_ARG 2>&1 | tee "$OUT/parallelism.txt"
 if [ "$NPROC" -ge 2 ]; then
-  $RUN benchmarks/bench_pipeline.py --microbatches 1,2,4,8,16 --gantt $BACKEND_ARG 2>&1 | tee "$OUT/pipeline.txt"
+  $RUN benchmarks/bench_pipeline.py --microbatches 1,2,4,8,16 --gantt --json "$OUT/pipeline.jsonl" $PREC $BACKEND_ARG 2>&1 | tee "$OUT/pipeline.txt"
 fi
-python benchmarks/analyze_trace.py "$OUT"/traces/*rank0.json --csv "$OUT/overlap.csv" 2>&1 | tee "$OUT/overlap.txt" || true
+python benchmarks/analyze_trace.py "$OUT"/traces/*_rank*.json --kernels 15 --csv "$OUT/overlap.csv" --json "$OUT/overlap.json" 2>&1 | tee "$OUT/overlap.txt" || true
 echo "done -> $OUT"
