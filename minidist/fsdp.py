@@ -118,6 +118,7 @@ class _FSDPUnit:
         if self._peer_shard is not None:
             from .parallel import collectives
 
+            self._invalidate_casts()
             comm_, buf, off = self._peer_shard
             bf = getattr(self, "_peer_shard_bf16", None)
             if bf is not None:
@@ -133,14 +134,23 @@ class _FSDPUnit:
                 collectives.all_gather_shards(buf, comm_, off, self.shard_numel, self._full, src_bf16=True)
             else:
                 collectives.all_gather_shards(buf, comm_, off, self.shard_numel, self._full)
-            # The kernel writes through a raw pointer: advance the version the parameter views
-            # share, so cached casts of them (the fused path's bf16 shadows) are refreshed.
-            torch.autograd.graph.increment_version(self._full)
             return
+        self._invalidate_casts()
         src = self.flat_shard.detach()
         if src.dtype != self.policy.param_dtype:
             src = src.to(self.policy.param_dtype)
         comm.all_gather_into_tensor(self._full, src.contiguous(), group=self.group)
+
+    def _invalidate_casts(self) -> None:
+        """Mark the fused path's cached bf16 casts of this unit's parameters stale.
+
+        A gather rewrites the parameters' bytes (``.data`` views of ``_full``) without touching
+        their version counters -- a ``.data`` view keeps its own counter, and bumping it would
+        trip autograd's saved-tensor check in the portable path -- so the cast cache is told
+        directly."""
+        for p in self.params:
+            if getattr(p, "_md_bf16_ver", None) is not None:
+                p._md_bf16_ver = None
 
     def unshard(self) -> None:
         if not self._unsharded and self._owner_state is not None:

@@ -418,12 +418,15 @@ def _fsdp_training(rank, world, param_dtype):
             pair.append(loss.item())
         losses.append(pair)
     torch.cuda.synchronize()
-    _report(f"fsdp_{tag}_vs_ddp_w{world}_losses", max(abs(a - b) / abs(a) for a, b in losses), 2e-2, rank)
+    # The losses see the forward weights directly: stale gathered weights (or stale casts of
+    # them) show up here at the 1e-2 level after four steps, reduction-order noise at 1e-4.
+    _report(f"fsdp_{tag}_vs_ddp_w{world}_losses", max(abs(a - b) / abs(a) for a, b in losses), 2e-3, rank)
     worst = 0.0
     with fsdp.summon_full_params():
         for (n, p), (_, q) in zip(fsdp.module.named_parameters(), ddp.module.named_parameters()):
             worst = max(worst, (p.float() - q.float()).abs().max().item())
-    _report(f"fsdp_{tag}_vs_ddp_w{world}_weights_abs", worst, 2e-2 if tag == "bf16" else 2e-3, rank)
+    # Adam turns reduction-order differences of tiny gradients into steps of up to ~lr each.
+    _report(f"fsdp_{tag}_vs_ddp_w{world}_weights_abs", worst, 2e-2, rank)
     nat.check_status()
 
 

@@ -155,6 +155,24 @@ def test_fsdp_actually_shards(world):
     run_distributed(_shards, world)
 
 
+def _casts_invalidated(rank, world):
+    """Every gather marks the cached low-precision casts of the unit's parameters stale (the
+    gathered bytes change without the parameters' version counters moving)."""
+    solo = solo_group(rank, world)
+    model = FullyShardedDataParallel(GPT(CFG, tp_group=solo), unit_types=(Block,))
+    for u in model._units:
+        for p in u.params:
+            p._md_bf16_ver = p._version  # as a cast made at this version would record
+        u.reshard()
+        u.unshard()
+        assert all(p._md_bf16_ver is None for p in u.params), u.name
+        u.reshard()
+
+
+def test_fsdp_gather_invalidates_cached_casts():
+    run_distributed(_casts_invalidated, 2)
+
+
 def test_fsdp_frees_gathered_parameters():
     run_distributed(_frees, 2)
 
