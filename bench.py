@@ -433,6 +433,21 @@ def main(argv=None) -> int:
         return 0
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
     c = resolve_config(args.config, world_env, args.tiny)
+    if args.impl == "reference" and args.device == "cuda" and c["pp"] > 1 and args.schedule == "1f1b":
+        # The reference's 1F1B (minidist/pipeline.py:205-231, 413-440 there) posts its
+        # activation isend and its blocking gradient recv on the same NCCL process group, so
+        # NCCL runs them in issue order on one stream: stage 0's send of microbatch m+1 waits
+        # for stage 1's recv, which is queued behind stage 1's gradient send, which waits for
+        # stage 0's recv, queued behind that first send.  Messages larger than NCCL's P2P
+        # buffer (a 4 x 2048 x 2560 microbatch is 42 MB) therefore deadlock; on a B200 box the
+        # 4-GPU run of this configuration made no progress for 4.5 minutes.  GPipe (all sends
+        # of a direction before any recv of the other) has no such cycle.
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": (
+                "the reference's 1F1B schedule deadlocks on NCCL for this configuration (unbatched "
+                "isend + blocking recv on one process group; 42 MB microbatch messages); "
+                "--schedule gpipe runs the reference")}))
+        return 0
     rank, world, local = setup(args)
     dev = args.device
     cuda = dev == "cuda"

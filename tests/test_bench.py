@@ -57,3 +57,17 @@ def test_layout_resolution():
     assert (c["tp"], c["dp"], c["batch"]) == (1, 8, 16)
     with pytest.raises(SystemExit):
         bench.resolve_config("gpt2.7b-3d", 2)
+
+
+@pytest.mark.skipif(not HAVE_REF, reason="baseline/_ref not installed")
+def test_reference_1f1b_on_gpus_reports_unavailable(monkeypatch, capsys):
+    """The reference's 1F1B deadlocks on NCCL at this configuration's message sizes, so on
+    GPUs its arm prints the one-line ``unavailable`` record (and builds nothing) instead."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    monkeypatch.setenv("WORLD_SIZE", "4")
+    monkeypatch.setenv("RANK", "0")
+    assert bench.main(["--impl", "reference", "--config", "gpt2.7b-3d", "--gpus", "4"]) == 0
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert out["impl"] == "reference" and "deadlocks" in out["unavailable"]
