@@ -91,10 +91,17 @@ def bench_gemm(M, N, K, iters, cta_group=0, which="fwd,dgrad,wgrad"):
               f"cuBLAS {tc * 1e6:8.1f} us {fl / tc / 1e12:7.1f} TFLOP/s | ratio {tc / t:5.2f}")
 
 
-def bench_attention(B, H, S, D, iters):
+def bench_attention(B, H, S, D, iters, fwd_only=False):
     qkv = torch.randn(B * S, 3 * H * D, device="cuda").bfloat16()
     fl_f = 4.0 * B * H * S * S * D / 2
     t = timed(lambda: K.attention_fwd(qkv, B, S, H, D), iters)
+    if fwd_only:
+        q, k, v = (z.transpose(1, 2).contiguous() for z in qkv.view(B, S, H, 3, D).unbind(3))
+        tr = timed(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True), iters)
+        nat.check_status()
+        print(f"attention fwd B={B} H={H} S={S} D={D}: {t * 1e6:8.1f} us {fl_f / t / 1e12:6.1f} TFLOP/s | "
+              f"torch SDPA {tr * 1e6:8.1f} us {fl_f / tr / 1e12:6.1f} TFLOP/s | ratio {tr / t:5.2f}")
+        return
     tm = timed(lambda: K.attention_fwd(qkv, B, S, H, D, impl="mma"), iters)
     y, lse = K.attention_fwd(qkv, B, S, H, D)
     dy = torch.randn_like(y)
@@ -135,6 +142,7 @@ def main():
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--cta-group", type=int, default=0)
     p.add_argument("--which", default="fwd,dgrad,wgrad")
+    p.add_argument("--fwd-only", action="store_true", help="attention: forward against SDPA only")
     a = p.parse_args()
     shp = [int(v) for v in a.shape.split(",")] if a.shape else None
     if a.op in ("all", "gemm") and a.which != "none":
@@ -145,7 +153,7 @@ def main():
     if a.op in ("all", "attention"):
         for s in ([shp] if shp and a.op == "attention" else [(16, 12, 1024, 64), (8, 25, 1024, 64), (4, 16, 2048, 80), (4, 16, 2048, 128),
                                                                (4, 4, 2048, 128)]):
-            bench_attention(*s, iters=a.iters)
+            bench_attention(*s, iters=a.iters, fwd_only=a.fwd_only)
     if a.op in ("all", "layernorm"):
         for s in ([shp] if shp and a.op == "layernorm" else [(16384, 768), (8192, 4096)]):
             bench_layernorm(*s, iters=a.iters)

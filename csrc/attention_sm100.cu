@@ -46,25 +46,32 @@ namespace attn_tc {
 constexpr int kBM = 128;   // queries per tile (TMEM lanes)
 constexpr int kBN = 128;   // keys per block
 constexpr float kRescaleLog2 = 8.0f;
-constexpr int kThreads = 192;
 
 // head_dim 64 runs two CTAs per SM (112 KB shared memory, 256 TMEM columns
 // each) so two independent softmax pipelines share every SM sub-partition and
-// hide each other's latencies; head_dim 128 needs one SM per CTA.
+// hide each other's latencies.  head_dim 128 needs one SM per CTA; there each
+// query row is split over two softmax warps (key columns 0..63 and 64..127,
+// row maxima and sums exchanged through shared memory) so that every SM
+// sub-partition still runs two softmax warps.
 template <int D>
 struct FwdCfg {
   static constexpr int kChunks = D / 64;               // 64-column (128 B) swizzle atoms along head_dim
   static constexpr int kTileBytes = kBM * D * 2;       // one Q/K/V tile
   static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
+  static constexpr int kSplit = D == 64 ? 1 : 2;       // softmax warps per query row
+  static constexpr int kSoftWarps = 4 * kSplit;
+  static constexpr int kThreads = 64 + 32 * kSoftWarps;
   static constexpr int kQBufs = 1;
   static constexpr int kKvStages = 2;
   static constexpr int kSBufs = D == 64 ? 1 : 2;       // TMEM score buffers
   static constexpr int kPBytes = kBM * kBN * 2;        // P tile (bf16)
-  static constexpr int kSmemData = (kQBufs + 2 * kKvStages) * kTileBytes + kPBytes;
+  static constexpr int kRedBytes = kSplit == 2 ? 2 * 2 * kBM * 4 : 0;  // row exchange [parity][half][row] fp32
+  static constexpr int kBarBytes = kSplit == 2 ? 512 : 256;
+  static constexpr int kSmemData = (kQBufs + 2 * kKvStages) * kTileBytes + kPBytes + kRedBytes;
   // Two CTAs per SM leave no room for alignment slack: the dynamic window is
   // then required to start 1024-byte aligned (checked in the kernel).
   static constexpr bool kAlignSlack = kCtasPerSm == 1;
-  static constexpr int kSmemBytes = kSmemData + 256 /*barriers*/ + (kAlignSlack ? 1024 : 0);
+  static constexpr int kSmemBytes = kSmemData + kBarBytes + (kAlignSlack ? 1024 : 0);
   static constexpr uint32_t kTmemCols = D == 64 ? 256 : 512;  // S buffers, then O
   static constexpr uint32_t kOCol = kSBufs * 128;
 };
@@ -104,10 +111,29 @@ __device__ __forceinline__ float lg2(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, for the share of the softmax exponentials taken off the
+// MUFU unit (which runs at a fraction of the FMA rate).  Range reduction
+// x = n + f, n = round-to-nearest(x) by the 1.5 * 2^23 add (the sum's low
+// mantissa bits then hold n), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial
+// whose coefficients are the minimax fit for relative error on [-1/2, 1/2]
+// (Remez exchange, computed for this kernel: max relative error 7.5e-5, well
+// below the 2^-9 rounding of the bf16 P it feeds); 2^n by adding n to the
+// exponent field.  x is clamped at -126 so the exponent field never
+// underflows: masked scores (-inf) give ~1.2e-38 instead of 0.
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float t = __fadd_rn(x, 12582912.0f);
+  const float f = __fadd_rn(x, -__fadd_rn(t, -12582912.0f));
+  const float q = fmaf(fmaf(fmaf(0.05517166853f, f, 0.24261112511f), f, 0.69326096773f), f, 0.99992805719f);
+  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+}
 
 
-template <int D>
-__global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
+
+// kPoly: of every 8 pairs of exponentials a softmax thread computes, how many
+// go through ex2_poly (FMA pipe) instead of ex2.approx (MUFU).
+template <int D, int kPoly>
+__global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
     fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ FwdParams p) {
   using C = FwdCfg<D>;
   constexpr int KST = C::kKvStages;
@@ -123,7 +149,8 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
   uint8_t* sK = sQ + QB * C::kTileBytes;
   uint8_t* sV = sK + KST * C::kTileBytes;
   uint8_t* sP = sV + KST * C::kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::kPBytes);
+  float* sRed = reinterpret_cast<float*>(sP + C::kPBytes);  // split rows only
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::kPBytes + C::kRedBytes);
   uint64_t* q_full = bars;           // [2]
   uint64_t* q_empty = bars + 2;      // [2]
   uint64_t* k_full = bars + 4;       // [4]
@@ -137,6 +164,7 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
   uint64_t* drain = bars + 26;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 27);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 28);
+  uint64_t* xbar = bars + 29;        // [4] row exchange between the two warps of a lane quarter (split rows)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -154,9 +182,11 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
+      mbar_init(&s_free[i], C::kSoftWarps);
     }
-    mbar_init(p_full, 4);
+    mbar_init(p_full, C::kSoftWarps);
+    if (C::kSplit == 2)
+      for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 2);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -300,15 +330,34 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
     mbar_wait(drain, 0, p.status, 55, nullptr);
   } else if (warp >= 2) {
     // ------------------------------------------------------------ softmax + epilogue
+    constexpr int NC = kBN / C::kSplit;      // key columns per thread
+    constexpr int OC = D / 32 / C::kSplit;   // 32-column O chunks per thread (rescale, epilogue)
+    const int half = (warp - 2) >> 2;        // column half of the row (0 unless split)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int kc0 = half * NC;               // first key column of this thread
     const float sl2 = p.scale_log2;
+    uint32_t xph = 0;                        // row exchanges done (split rows)
+    // Split rows: publish v for the partner warp (other column half, same rows) and
+    // return the partner's value.  Exchange k uses buffer k & 1: a warp rewrites a
+    // buffer only after the partner arrived at the next exchange, i.e. after it
+    // read this one.  Bounded wait; false on timeout / abort.
+    auto exchange = [&](float& v, int site) -> bool {
+      const int par = static_cast<int>(xph & 1u);
+      sRed[(par * 2 + half) * kBM + row] = v;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xbar[quarter]);
+      if (!mbar_wait(&xbar[quarter], xph & 1u, p.status, site, abort_flag)) return false;
+      v = sRed[(par * 2 + (half ^ 1)) * kBM + row];
+      ++xph;
+      return true;
+    };
     int g = 0;
     for (int w = blockIdx.x; w < p.items; w += gridDim.x) {
       int qt, b, h;
       decode(p, w, qt, b, h);
-      float m = -INFINITY, l = 0.f;
+      float m = -INFINITY, l = 0.f;  // split rows: l is this half's partial sum
       bool ok = true;
       for (int j = 0; j <= qt; ++j, ++g) {
         const int sb = g % SB;
@@ -317,42 +366,63 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
           break;
         }
         tc_fence_after();
-        uint32_t r[4][32];
+        uint32_t r[NC / 32][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_base + static_cast<uint32_t>(sb * kBN + c * 32), r[c]);
+        for (int c = 0; c < NC / 32; ++c)
+          tmem_ld_32x32b_x32(tmem + lane_base + static_cast<uint32_t>(sb * kBN + kc0 + c * 32), r[c]);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[sb]);
         if (j == qt) {  // diagonal block: key > query is masked
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < NC / 32; ++c)
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (c * 32 + i > row) r[c][i] = __float_as_uint(-INFINITY);
+              if (kc0 + c * 32 + i > row) r[c][i] = __float_as_uint(-INFINITY);
         }
-        float mx0 = -INFINITY, mx1 = -INFINITY;
+        // Row maximum over eight independent partial maxima (a short dependency chain).
+        float mx8[8];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            mx0 = fmaxf(mx0, __uint_as_float(r[c][i]));
-            mx1 = fmaxf(mx1, __uint_as_float(r[c][i + 1]));
+        for (int c = 0; c < NC / 32; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(r[c][i]));
+        float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                         fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        if constexpr (C::kSplit == 2) {
+          float other = mx;
+          if (!exchange(other, 63)) {
+            ok = false;
+            break;
           }
-        const float mx = fmaxf(mx0, mx1) * sl2;
+          mx = fmaxf(mx, other);
+        }
+        mx *= sl2;
+        // Both halves of a split row see the same m and mx, so they agree on m_use.
         const float m_use = mx > m + kRescaleLog2 ? mx : m;
         const float alpha = ex2(m - m_use);
         float l0 = 0.f, l1 = 0.f;
-        uint32_t pk[64];
+        uint32_t pk[NC / 2];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < NC / 32; ++c)
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
-            const float e0 = ex2(fmaf(__uint_as_float(r[c][i]), sl2, -m_use));
-            const float e1 = ex2(fmaf(__uint_as_float(r[c][i + 1]), sl2, -m_use));
+            const int pair = (c * 32 + i) >> 1;
+            const float x0 = fmaf(__uint_as_float(r[c][i]), sl2, -m_use);
+            const float x1 = fmaf(__uint_as_float(r[c][i + 1]), sl2, -m_use);
+            float e0, e1;
+            if ((pair & 7) < kPoly) {
+              e0 = ex2_poly(x0);
+              e1 = ex2_poly(x1);
+            } else {
+              e0 = ex2(x0);
+              e1 = ex2(x1);
+            }
             l0 += e0;
             l1 += e1;
-            pk[(c * 32 + i) >> 1] = pack_bf16x2(e0, e1);
+            pk[pair] = pack_bf16x2(e0, e1);
           }
         l = l * alpha + (l0 + l1);
         if (j > 0) {
@@ -362,11 +432,12 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
             break;
           }
           tc_fence_after();
+          // Rows of the partner warp make the same decision, so each half rescales its O columns.
           if (__any_sync(0xFFFFFFFFu, m_use != m)) {
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
+            for (int c = 0; c < OC; ++c) {
               uint32_t o[32];
-              const uint32_t ta = tmem + lane_base + C::kOCol + static_cast<uint32_t>(c * 32);
+              const uint32_t ta = tmem + lane_base + C::kOCol + static_cast<uint32_t>((half * OC + c) * 32);
               tmem_ld_32x32b_x32(ta, o);
               tmem_ld_wait();
 #pragma unroll
@@ -378,8 +449,9 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
         }
         m = m_use;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          uint8_t* dst = sP + (k >> 3) * (kBM * 128) + sw128_off(row, k & 7);
+        for (int k = 0; k < NC / 8; ++k) {
+          const int kk = half * (NC / 8) + k;  // 16-byte column group of the 128-key row
+          uint8_t* dst = sP + (kk >> 3) * (kBM * 128) + sw128_off(row, kk & 7);
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(dst)), "r"(pk[4 * k]),
                        "r"(pk[4 * k + 1]), "r"(pk[4 * k + 2]), "r"(pk[4 * k + 3])
                        : "memory");
@@ -390,6 +462,11 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
         if (lane == 0) mbar_arrive(p_full);
       }
       if (!ok) break;
+      if constexpr (C::kSplit == 2) {
+        float other = l;
+        if (!exchange(other, 64)) break;
+        l += other;
+      }
       // Epilogue: O / l straight from TMEM, lse for the backward pass.
       if (!mbar_wait(o_done, static_cast<uint32_t>(g - 1) & 1u, p.status, 62, abort_flag)) break;
       tc_fence_after();
@@ -398,7 +475,8 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
       uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) +
                       (static_cast<long long>(b) * p.S + q) * p.ldo * 2 + static_cast<long long>(h) * p.dr * 2;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int cc = 0; cc < OC; ++cc) {
+        const int c = half * OC + cc;
         if (c * 32 >= p.dr) break;  // uniform: the padded columns are not stored
         uint32_t o[32];
         tmem_ld_32x32b_x32(tmem + lane_base + C::kOCol + static_cast<uint32_t>(c * 32), o);
@@ -416,7 +494,8 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::kCtasPerSm)
           }
         }
       }
-      if (q < p.S) p.lse[(static_cast<long long>(b) * p.H + h) * p.S + q] = (m + lg2(l)) * 0.6931471805599453f;
+      if (half == 0 && q < p.S)
+        p.lse[(static_cast<long long>(b) * p.H + h) * p.S + q] = (m + lg2(l)) * 0.6931471805599453f;
       tc_fence_before();
     }
   }
@@ -1504,6 +1583,20 @@ bool make_map_f32_bshd(CUtensorMap* map, const void* ptr, int B, int S, int H, i
 int g_sms = 0;
 long long* g_trace = nullptr;  // device buffer set by md_attn_trace_enable (analysis only)
 
+// Pairs of every 8 softmax exponentials computed on the FMA pipe (fwd_kernel's
+// kPoly): 0, 2 or 4, from MINIDIST_ATTN_EXP_POLY; default 0.  Measured on B200
+// (fwd, causal, bf16): d 64 16x12x1024 71.2 / 75.4 / 91.7 us, d 128 4x16x2048
+// 108.7 / 107.8 / 113.0 us for 0 / 2 / 4 -- the softmax warps are not bound by
+// the MUFU rate, so the extra FMA-pipe instructions do not pay at these sizes.
+int fwd_poly(int D) {
+  (void)D;
+  static const int env = [] {
+    const char* e = getenv("MINIDIST_ATTN_EXP_POLY");
+    return e && *e ? atoi(e) : -1;
+  }();
+  return env == 2 || env == 4 ? env : 0;
+}
+
 template <int D>
 int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, float* lse, int B, int H, int S,
                   float scale, void* status, cudaStream_t st, int dr = D) {
@@ -1532,12 +1625,14 @@ int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, floa
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = reinterpret_cast<md::Status*>(status);
   p.dr = dr;
-  auto k = md::attn_tc::fwd_kernel<D>;
+  const int poly = fwd_poly(D);
+  auto k = poly == 4 ? md::attn_tc::fwd_kernel<D, 4> : poly == 2 ? md::attn_tc::fwd_kernel<D, 2>
+                                                                 : md::attn_tc::fwd_kernel<D, 0>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
   const int slots = g_sms * C::kCtasPerSm;
   const int grid = p.items < slots ? p.items : slots;
-  md::launch_pdl(k, grid, dim3(md::attn_tc::kThreads), C::kSmemBytes, st, tm, p);
+  md::launch_pdl(k, grid, dim3(C::kThreads), C::kSmemBytes, st, tm, p);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -3,6 +3,9 @@
 from __future__ import annotations
 
 import math
+import os
+import subprocess
+import sys
 
 import pytest
 import torch
@@ -99,6 +102,42 @@ def test_attention_fwd_tc_many_tiles():
     g2 = K.attention_bwd(qkv, y, dy, lse, B, S, H, D, impl="mma")
     nat.check_status()
     assert _rel(g1, g2) < 2e-2
+
+
+_EXP_SPLIT = r"""
+import math
+import torch
+import torch.nn.functional as F
+from minidist.ops import _native as nat
+from minidist.ops import kernels as K
+torch.manual_seed(5)
+for D in (64, 80, 128):
+    B, S, H = 2, 1000, 6
+    qkv = (torch.randn(B * S, 3 * H * D, device="cuda") * 2).bfloat16()
+    y, lse = K.attention_fwd(qkv, B, S, H, D, impl="tc")
+    torch.cuda.synchronize()
+    nat.check_status()
+    q, k, v = (t.transpose(1, 2) for t in qkv.float().view(B, S, H, 3, D).unbind(3))
+    ref = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).reshape(B * S, H * D)
+    s = (q @ k.transpose(-1, -2)) / math.sqrt(D)
+    s = s.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool, device="cuda"), 1), float("-inf"))
+    lse_ref = torch.logsumexp(s, -1)
+    e_y = ((y.float() - ref).abs().max() / ref.abs().max()).item()
+    e_l = ((lse - lse_ref).abs().max() / lse_ref.abs().max()).item()
+    print(D, e_y, e_l)
+    assert e_y < 2e-2 and e_l < 1e-3, (D, e_y, e_l)
+print("ok")
+"""
+
+
+@pytest.mark.parametrize("poly", ["0", "2", "4"])
+def test_attention_fwd_exp_split(poly):
+    """The tcgen05 forward with 0, 2 or 4 of every 8 exponential pairs on the FMA-pipe polynomial
+    (MINIDIST_ATTN_EXP_POLY, read once per process), at head_dim 64, 80 and 128, against fp32."""
+    env = dict(os.environ, MINIDIST_ATTN_EXP_POLY=poly)
+    proc = subprocess.run([sys.executable, "-c", _EXP_SPLIT], env=env, capture_output=True, text=True, timeout=300,
+                          cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    assert proc.returncode == 0 and "ok" in proc.stdout, proc.stdout[-2000:] + proc.stderr[-2000:]
 
 
 @pytest.mark.parametrize("D", [80, 128])
