@@ -1,5 +1,5 @@
 // Causal flash attention forward on the 5th-generation tensor cores (tcgen05),
-// bf16 in / bf16 out, head_dim 64 or 128.
+// bf16 in / bf16 out, head_dim 64 or 128 (80 on zero-padded 128 boxes).
 //
 // Same contract as md_attn_fwd of attention.cu (which dispatches here for
 // these head sizes): Q, K, V are read in place from the QKV projection output
@@ -9,25 +9,32 @@
 // natural-log log-sum-exp of every query row for the backward pass.
 //
 // Persistent kernel (two CTAs per SM for head_dim 64, one for 128), warp-specialised:
-//   warp 0      TMA producer: Q tile (128 queries) and, per key block, K and V
-//               tiles (128 keys) through a 3-D tensor map [B, S, 3*H*D] whose
-//               sequence-end rows read as zero.
+//   warp 0      TMA: Q tiles (128 queries, two buffers: the next work item's Q
+//               loads while this one runs) and, per key block, K and V tiles
+//               (128 keys) through a 3-D tensor map [B, S, 3*H*D] whose
+//               sequence-end rows read as zero.  It also stores each finished
+//               item's output tile, which the softmax warps stage in that
+//               item's (no longer needed) Q buffer, with a bulk tensor store,
+//               and reloads the buffer once the store has read it.
 //   warp 1      MMA issuer (one thread): S = Q K^T into a TMEM score buffer
 //               (128 x 128 fp32; two buffers for head_dim 128), then O += P V
-//               into a TMEM accumulator (128 x D fp32).  The score product of
-//               block g+1 is queued before the P V product of block g (the
-//               softmax warps release the score buffer as soon as it is in
-//               registers), so the tensor core computes scores while the
-//               softmax warps exponentiate.
-//   warps 2..5  softmax: thread t owns query row t (TMEM lane t, 32x32b loads),
-//               so row max and row sum need no shuffles.  Scores come out of
-//               TMEM, exp2 on the MUFU pipe, P goes to shared memory as bf16 in
-//               the 128-byte-swizzled K-major layout the P V product reads.
-//               The running max only moves when it grows by more than 2^8
-//               (factor kRescaleLog2), so the O rescale (TMEM load/scale/store)
-//               is rare after the first blocks; l and O stay consistent since
-//               both use the same stale max.  Final O / l and lse are written
-//               straight from TMEM.
+//               into a TMEM accumulator (128 x D fp32) with P read from TMEM.
+//               The score product of block g+1 is queued before the P V
+//               product of block g (the softmax warps release the score buffer
+//               as soon as it is in registers), so the tensor core computes
+//               scores while the softmax warps exponentiate.
+//   warps 2..   softmax: thread t owns query row t (TMEM lane t, 32x32b loads);
+//               for head_dim 128 two warps share each row (keys 0..63 /
+//               64..127) and exchange row maxima and sums through shared
+//               memory.  Scores come out of TMEM, exp2 on the MUFU pipe, P goes
+//               back to TMEM as bf16 pairs (the A operand of P V: no shared-
+//               memory round trip, no proxy fence).  The running max only moves
+//               when it grows by more than 2^8 (factor kRescaleLog2), so the O
+//               rescale (TMEM load/scale/store) is rare after the first blocks;
+//               l and O stay consistent since both use the same stale max.
+//               The epilogue writes O / l into the 128B-swizzled staging tile
+//               and lse straight to global memory, then moves on to the next
+//               item while warp 0 stores the tile.
 //
 // Work items are (query tile, batch*head) pairs ordered longest-first (the
 // causal tile qt has qt+1 key blocks) and dealt round-robin to the CTAs.
@@ -35,6 +42,7 @@
 // Every mbarrier wait is bounded (md_sm100.cuh); a CTA that gives up records a
 // status, lets the other roles see the abort flag, drains its bulk copies and
 // MMAs, frees TMEM and exits.
+
 #include <cudaTypedefs.h>
 #include <stdlib.h>
 
@@ -47,7 +55,7 @@ constexpr int kBM = 128;   // queries per tile (TMEM lanes)
 constexpr int kBN = 128;   // keys per block
 constexpr float kRescaleLog2 = 8.0f;
 
-// head_dim 64 runs two CTAs per SM (112 KB shared memory, 256 TMEM columns
+// head_dim 64 runs two CTAs per SM (96 KB shared memory, 256 TMEM columns
 // each) so two independent softmax pipelines share every SM sub-partition and
 // hide each other's latencies.  head_dim 128 needs one SM per CTA; there each
 // query row is split over two softmax warps (key columns 0..63 and 64..127,
@@ -56,29 +64,29 @@ constexpr float kRescaleLog2 = 8.0f;
 template <int D>
 struct FwdCfg {
   static constexpr int kChunks = D / 64;               // 64-column (128 B) swizzle atoms along head_dim
-  static constexpr int kTileBytes = kBM * D * 2;       // one Q/K/V tile
+  static constexpr int kTileBytes = kBM * D * 2;       // one Q/K/V (or staged O) tile
   static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
   static constexpr int kSplit = D == 64 ? 1 : 2;       // softmax warps per query row
   static constexpr int kSoftWarps = 4 * kSplit;
   static constexpr int kThreads = 64 + 32 * kSoftWarps;
-  static constexpr int kQBufs = 1;
+  static constexpr int kQBufs = 2;
   static constexpr int kKvStages = 2;
   static constexpr int kSBufs = D == 64 ? 1 : 2;       // TMEM score buffers
-  static constexpr int kPBytes = kBM * kBN * 2;        // P tile (bf16)
   static constexpr int kRedBytes = kSplit == 2 ? 2 * 2 * kBM * 4 : 0;  // row exchange [parity][half][row] fp32
   static constexpr int kBarBytes = kSplit == 2 ? 512 : 256;
-  static constexpr int kSmemData = (kQBufs + 2 * kKvStages) * kTileBytes + kPBytes + kRedBytes;
-  // Two CTAs per SM leave no room for alignment slack: the dynamic window is
-  // then required to start 1024-byte aligned (checked in the kernel).
-  static constexpr bool kAlignSlack = kCtasPerSm == 1;
-  static constexpr int kSmemBytes = kSmemData + kBarBytes + (kAlignSlack ? 1024 : 0);
-  static constexpr uint32_t kTmemCols = D == 64 ? 256 : 512;  // S buffers, then O
+  static constexpr int kSmemData = (kQBufs + 2 * kKvStages) * kTileBytes + kRedBytes;
+  static constexpr int kSmemBytes = kSmemData + kBarBytes + 1024 /*alignment slack*/;
+  // TMEM: score buffers, then O (D columns), then P (128 keys as bf16 pairs: 64 columns).
+  static constexpr uint32_t kTmemCols = D == 64 ? 256 : 512;
   static constexpr uint32_t kOCol = kSBufs * 128;
+  static constexpr uint32_t kPCol = kOCol + D;
+  // P buffers: two where TMEM has room (head_dim 128), so block g+1's P is written
+  // while P V of block g still reads block g's.
+  static constexpr int kPBufs = D == 64 ? 1 : 2;
+  static_assert(kPCol + kPBufs * kBN / 2 <= kTmemCols, "TMEM columns");
 };
 
 struct FwdParams {
-  void* out;
-  long long ldo;
   float* lse;
   int B, H, S;
   int n_qt;       // query tiles per sequence
@@ -86,11 +94,22 @@ struct FwdParams {
   float scale_log2;
   Status* status;
   // Real head dimension dr <= D.  dr < D (d = 80 on the D = 128 kernel): the
-  // tensor map is 4-D [B, S, 3H head slots, dr], so the 64-column boxes read
-  // zeros past dr (they add nothing to QK^T or PV) and only dr output columns
-  // are stored.
+  // tensor maps are 4-D [B, S, head slots, dr], so the 64-column boxes read
+  // zeros past dr (they add nothing to QK^T or PV) and the output store
+  // clips columns past dr.
   int dr;
+  long long* trace;  // optional: CTA 0 records clock64() at pipeline hand-offs, [64 blocks][32]
 };
+
+// Forward pipeline trace (CTA 0, first 64 key blocks; only in the kTrace
+// instantiation).  Slots: 0-5 softmax warp 2 lane 0 (scores ready, scores
+// loaded, row max, exponentials with P written to TMEM, O synchronised /
+// rescaled, P handed to the MMA warp), 6-11 the same for warp 6 (split rows),
+// 12 / 13 MMA issue of S / P V, 14 / 15 TMA issue of K / V.
+#define MD_FTRACE(gg, slot)                                                                      \
+  do {                                                                                          \
+    if (kTrace && blockIdx.x == 0 && (gg) < 64) p.trace[(gg) * 32 + (slot)] = clock64();        \
+  } while (0)
 
 __device__ __forceinline__ void decode(const FwdParams& p, int w, int& qt, int& b, int& h) {
   const int bh_count = p.B * p.H;
@@ -112,14 +131,15 @@ __device__ __forceinline__ float lg2(float x) {
 }
 
 // 2^x on the FMA pipe, for the share of the softmax exponentials taken off the
-// MUFU unit (which runs at a fraction of the FMA rate).  Range reduction
-// x = n + f, n = round-to-nearest(x) by the 1.5 * 2^23 add (the sum's low
-// mantissa bits then hold n), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial
-// whose coefficients are the minimax fit for relative error on [-1/2, 1/2]
-// (Remez exchange, computed for this kernel: max relative error 7.5e-5, well
-// below the 2^-9 rounding of the bf16 P it feeds); 2^n by adding n to the
-// exponent field.  x is clamped at -126 so the exponent field never
-// underflows: masked scores (-inf) give ~1.2e-38 instead of 0.
+// MUFU unit (16 results per clock per SM: the exponentials of a 128 x 128 block
+// alone keep it busy for 1024 cycles).  Range reduction x = n + f with
+// n = round-to-nearest(x) by the 1.5 * 2^23 add (the sum's low mantissa bits
+// then hold n), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose
+// coefficients are the minimax fit for relative error on [-1/2, 1/2] (Remez
+// exchange, computed for this kernel: max relative error 7.5e-5, well below the
+// 2^-9 rounding of the bf16 P it feeds); 2^n by adding n to the exponent field.
+// x is clamped at -126 so the exponent field never underflows: masked scores
+// (-inf) give ~1.2e-38 instead of 0.
 __device__ __forceinline__ float ex2_poly(float x) {
   x = fmaxf(x, -126.0f);
   const float t = __fadd_rn(x, 12582912.0f);
@@ -128,31 +148,27 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
 }
 
-
-
-// kPoly: of every 8 pairs of exponentials a softmax thread computes, how many
-// go through ex2_poly (FMA pipe) instead of ex2.approx (MUFU).
-template <int D, int kPoly>
+// tm: Q/K/V loads ([B, S, 3*H*D], or [B, S, 3H, dr]); to: output stores
+// ([B, S, H*D], or [B, S, H, dr]).  kPoly: of every 8 pairs of exponentials a
+// softmax thread computes, how many go through ex2_poly instead of ex2.approx.
+template <int D, int kPoly, bool kTrace>
 __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
-    fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ FwdParams p) {
+    fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap to,
+               const __grid_constant__ FwdParams p) {
   using C = FwdCfg<D>;
   constexpr int KST = C::kKvStages;
   constexpr int QB = C::kQBufs;
   constexpr int SB = C::kSBufs;
+  constexpr int PB = C::kPBufs;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  if (!C::kAlignSlack && smem != smem_raw) {  // uniform across the CTA
-    if (threadIdx.x == 0) report(p.status, kBadArgument, 39, static_cast<uint32_t>(smem_u32(smem_raw)));
-    return;
-  }
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + QB * C::kTileBytes;
   uint8_t* sV = sK + KST * C::kTileBytes;
-  uint8_t* sP = sV + KST * C::kTileBytes;
-  float* sRed = reinterpret_cast<float*>(sP + C::kPBytes);  // split rows only
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::kPBytes + C::kRedBytes);
+  float* sRed = reinterpret_cast<float*>(sV + KST * C::kTileBytes);  // split rows only
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + KST * C::kTileBytes + C::kRedBytes);
   uint64_t* q_full = bars;           // [2]
-  uint64_t* q_empty = bars + 2;      // [2]
+  uint64_t* o_staged = bars + 2;     // [2] the item's O is in its Q buffer (softmax warps -> warp 0)
   uint64_t* k_full = bars + 4;       // [4]
   uint64_t* k_empty = bars + 8;      // [4]
   uint64_t* v_full = bars + 12;      // [4]
@@ -172,7 +188,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
   if (threadIdx.x == 0) {
     for (int i = 0; i < QB; ++i) {
       mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
+      mbar_init(&o_staged[i], C::kSoftWarps);
     }
     for (int i = 0; i < KST; ++i) {
       mbar_init(&k_full[i], 1);
@@ -192,6 +208,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm);
+    tma_prefetch_desc(&to);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -205,23 +222,47 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
   pdl_trigger();
   pdl_wait();
 
+  const bool map4 = p.dr != D;  // uniform
   if (warp == 0 && lane == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA loads and output stores
     int q_armed[2] = {-1, -1};
     int k_armed[4] = {-1, -1, -1, -1};
     int v_armed[4] = {-1, -1, -1, -1};
-    int g = 0, t = 0;
+    // Store item ti's output tile (staged by the softmax warps in Q buffer ti % QB).
+    auto store_out = [&](int ti) -> bool {
+      const int qb = ti % QB;
+      if (!mbar_wait(&o_staged[qb], static_cast<uint32_t>(ti / QB) & 1u, p.status, 46, abort_flag)) return false;
+      int qt, b, h;
+      decode(p, blockIdx.x + ti * gridDim.x, qt, b, h);
+#pragma unroll
+      for (int c = 0; c < C::kChunks; ++c) {
+        if (c * 64 >= p.dr) break;  // uniform: nothing of this box lies inside the tensor
+        const uint8_t* src = sQ + qb * C::kTileBytes + c * (kBM * 128);
+        if (map4) tma_store_4d(&to, src, c * 64, h, qt * kBM, b);
+        else tma_store_3d(&to, src, h * D + c * 64, qt * kBM, b);
+      }
+      bulk_commit_group();
+      return true;
+    };
+    int g = 0, t = 0, stored = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
       int qt, b, h;
       decode(p, w, qt, b, h);
       const int qb = t % QB;
-      const uint32_t qph = static_cast<uint32_t>(t / QB) & 1u;
-      if (!mbar_wait(&q_empty[qb], qph ^ 1u, p.status, 40, abort_flag)) break;
+      if (t >= QB) {
+        // Buffer qb last held item t-QB: store that item's output, and reload the
+        // buffer once the store has read it.
+        if (!store_out(t - QB)) {
+          ok = false;
+          break;
+        }
+        stored = t - QB + 1;
+        bulk_wait_read_all();
+      }
       mbar_arrive_expect_tx(&q_full[qb], C::kTileBytes);
-      q_armed[qb] = static_cast<int>(qph);
+      q_armed[qb] = static_cast<int>(static_cast<uint32_t>(t / QB) & 1u);
       const int col0 = h * 3 * D;
-      const bool map4 = p.dr != D;  // uniform
 #pragma unroll
       for (int c = 0; c < C::kChunks; ++c) {
         if (map4) tma_load_4d(&tm, &q_full[qb], sQ + qb * C::kTileBytes + c * (kBM * 128), c * 64, 3 * h, qt * kBM, b);
@@ -236,6 +277,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
         }
         mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
         k_armed[st] = static_cast<int>(ph);
+        MD_FTRACE(g, 14);
 #pragma unroll
         for (int c = 0; c < C::kChunks; ++c) {
           if (map4) tma_load_4d(&tm, &k_full[st], sK + st * C::kTileBytes + c * (kBN * 128), c * 64, 3 * h + 1, j * kBN, b);
@@ -247,6 +289,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
         }
         mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
         v_armed[st] = static_cast<int>(ph);
+        MD_FTRACE(g, 15);
 #pragma unroll
         for (int c = 0; c < C::kChunks; ++c) {
           if (map4) tma_load_4d(&tm, &v_full[st], sV + st * C::kTileBytes + c * (kBN * 128), c * 64, 3 * h + 2, j * kBN, b);
@@ -255,7 +298,12 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
         }
       }
     }
-    // No bulk copy into shared memory may still be in flight at exit.
+    // The last items' outputs (skipped after an abort: their tiles were never staged).
+    if (ok)
+      for (int ti = stored; ti < t; ++ti)
+        if (!store_out(ti)) break;
+    // No bulk copy may still be in flight at exit: stores complete, loads landed.
+    bulk_wait_all();
     for (int i = 0; i < QB; ++i)
       if (q_armed[i] >= 0) mbar_wait(&q_full[i], static_cast<uint32_t>(q_armed[i]), p.status, 43, nullptr);
     for (int i = 0; i < KST; ++i) {
@@ -267,27 +315,46 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
     constexpr uint32_t idS = idesc_bf16_f32(kBM, kBN, false, false);
     constexpr uint32_t idO = idesc_bf16_f32(kBM, D, false, true);
     // Base descriptors; an operand at byte offset `off` is base + (off >> 4).
-    const uint64_t dP = sdesc_sw128(smem_u32(sP), 16, 1024);
     const uint64_t dV = sdesc_sw128(smem_u32(sV), kBN * 128, 1024);
     const uint64_t dQ = sdesc_sw128(smem_u32(sQ), 16, 1024);
     const uint64_t dK = sdesc_sw128(smem_u32(sK), 16, 1024);
     constexpr uint32_t kTile16 = C::kTileBytes >> 4;
     int pend = -1;
     bool pend_first = false;
-    // O += P V for block gp (P from shared memory, V MN-major).
+    // O += P V for block gp (P from TMEM, V MN-major from shared memory).
     auto issue_pv = [&](int gp, bool first) -> bool {
       if (!mbar_wait(p_full, static_cast<uint32_t>(gp) & 1u, p.status, 52, abort_flag)) return false;
       const int st = gp % KST;
       if (!mbar_wait(&v_full[st], static_cast<uint32_t>(gp / KST) & 1u, p.status, 53, abort_flag)) return false;
       tc_fence_after();
+      if (lane == 0) MD_FTRACE(gp, 13);
       const uint64_t v0 = dV + st * kTile16;
 #pragma unroll
       for (int kk = 0; kk < kBN / 16; ++kk)
-        umma_bf16_ss_elect(tmem + C::kOCol, dP + (((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4), v0 + kk * 128,
-                           idO, (first && kk == 0) ? 0u : 1u);
+        umma_bf16_ts_elect(tmem + C::kOCol, tmem + C::kPCol + static_cast<uint32_t>((gp % C::kPBufs) * (kBN / 2) + kk * 8),
+                           v0 + kk * 128, idO, (first && kk == 0) ? 0u : 1u);
       umma_commit_elect(o_done);
       umma_commit_elect(&v_empty[st]);
       return true;
+    };
+    // While a P V product is pending, issue whichever comes first: that product (its P
+    // is in TMEM) or the next score product (its K tile and score buffer are free).
+    // Returns 1 when the P V went first, 0 when the scores may go first, -1 on
+    // timeout / abort.
+    auto pv_first = [&](uint64_t* a, uint32_t pa, uint64_t* b2, uint32_t pb) -> int {
+      const uint64_t t0 = globaltimer_ns();
+      for (uint32_t it = 0;; ++it) {
+        if (mbar_test_wait(a, pa) && (b2 == nullptr || mbar_test_wait(b2, pb))) return 0;
+        if (mbar_test_wait(p_full, static_cast<uint32_t>(pend) & 1u)) return issue_pv(pend, pend_first) ? 1 : -1;
+        if ((it & 63u) == 63u) {
+          if (*abort_flag) return -1;
+          if (globaltimer_ns() - t0 > kPipelineTimeoutNs) {
+            report(p.status, kTimeoutPipeline, 56, 0);
+            *abort_flag = 1;
+            return -1;
+          }
+        }
+      }
     };
     int g = 0, t = 0;
     bool ok = true;
@@ -295,17 +362,40 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
       int qt, b, h;
       decode(p, w, qt, b, h);
       const int qb = t % QB;
-      if (!mbar_wait(&q_full[qb], static_cast<uint32_t>(t / QB) & 1u, p.status, 50, abort_flag)) break;
+      const uint32_t qph = static_cast<uint32_t>(t / QB) & 1u;
+      if (pend >= 0) {
+        const int r = pv_first(&q_full[qb], qph, nullptr, 0);
+        if (r < 0) {
+          ok = false;
+          break;
+        }
+        if (r == 1) pend = -1;
+      }
+      if (!mbar_wait(&q_full[qb], qph, p.status, 50, abort_flag)) {
+        ok = false;
+        break;
+      }
       const uint64_t q0 = dQ + qb * kTile16;
       for (int j = 0; j <= qt; ++j, ++g) {
         const int st = g % KST;
         const int sb = g % SB;
-        if (!mbar_wait(&k_full[st], static_cast<uint32_t>(g / KST) & 1u, p.status, 51, abort_flag) ||
-            !mbar_wait(&s_free[sb], (static_cast<uint32_t>(g / SB) & 1u) ^ 1u, p.status, 54, abort_flag)) {
+        const uint32_t kph = static_cast<uint32_t>(g / KST) & 1u;
+        const uint32_t sph = (static_cast<uint32_t>(g / SB) & 1u) ^ 1u;
+        if (pend >= 0) {
+          const int r = pv_first(&k_full[st], kph, &s_free[sb], sph);
+          if (r < 0) {
+            ok = false;
+            break;
+          }
+          if (r == 1) pend = -1;
+        }
+        if (!mbar_wait(&k_full[st], kph, p.status, 51, abort_flag) ||
+            !mbar_wait(&s_free[sb], sph, p.status, 54, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        if (lane == 0) MD_FTRACE(g, 12);
         const uint64_t k0 = dK + st * kTile16;
         const uint32_t sd = tmem + static_cast<uint32_t>(sb * kBN);
 #pragma unroll
@@ -315,7 +405,6 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
         }
         umma_commit_elect(&s_full[sb]);
         umma_commit_elect(&k_empty[st]);
-        if (j == qt) umma_commit_elect(&q_empty[qb]);
         if (pend >= 0 && !issue_pv(pend, pend_first)) {
           ok = false;
           break;
@@ -338,23 +427,26 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int kc0 = half * NC;               // first key column of this thread
     const float sl2 = p.scale_log2;
+    const int tslot = lane == 0 && quarter == 2 ? 6 * half : -1;  // warps 2 and 6 record (kTrace)
     uint32_t xph = 0;                        // row exchanges done (split rows)
-    // Split rows: publish v for the partner warp (other column half, same rows) and
-    // return the partner's value.  Exchange k uses buffer k & 1: a warp rewrites a
-    // buffer only after the partner arrived at the next exchange, i.e. after it
-    // read this one.  Bounded wait; false on timeout / abort.
-    auto exchange = [&](float& v, int site) -> bool {
-      const int par = static_cast<int>(xph & 1u);
-      sRed[(par * 2 + half) * kBM + row] = v;
+    // Split rows: post(v) publishes v for the partner warp (other column half, same
+    // rows); get() returns the partner's value of the same exchange.  Exchange k uses
+    // buffer k & 1: a warp rewrites a buffer only after the partner arrived at the
+    // next exchange, i.e. after it read this one.  Bounded wait; false on timeout /
+    // abort.
+    auto post = [&](float v) {
+      sRed[(static_cast<int>(xph & 1u) * 2 + half) * kBM + row] = v;
       __syncwarp();
       if (lane == 0) mbar_arrive(&xbar[quarter]);
+    };
+    auto get = [&](float& v, int site) -> bool {
       if (!mbar_wait(&xbar[quarter], xph & 1u, p.status, site, abort_flag)) return false;
-      v = sRed[(par * 2 + (half ^ 1)) * kBM + row];
+      v = sRed[(static_cast<int>(xph & 1u) * 2 + (half ^ 1)) * kBM + row];
       ++xph;
       return true;
     };
-    int g = 0;
-    for (int w = blockIdx.x; w < p.items; w += gridDim.x) {
+    int g = 0, t = 0;
+    for (int w = blockIdx.x; w < p.items; w += gridDim.x, ++t) {
       int qt, b, h;
       decode(p, w, qt, b, h);
       float m = -INFINITY, l = 0.f;  // split rows: l is this half's partial sum
@@ -366,6 +458,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
           break;
         }
         tc_fence_after();
+        if (kTrace && tslot >= 0) MD_FTRACE(g, tslot + 0);
         uint32_t r[NC / 32][32];
 #pragma unroll
         for (int c = 0; c < NC / 32; ++c)
@@ -374,6 +467,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[sb]);
+        if (kTrace && tslot >= 0) MD_FTRACE(g, tslot + 1);
         if (j == qt) {  // diagonal block: key > query is masked
 #pragma unroll
           for (int c = 0; c < NC / 32; ++c)
@@ -391,47 +485,97 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
           for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(r[c][i]));
         float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                          fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-        if constexpr (C::kSplit == 2) {
-          float other = mx;
-          if (!exchange(other, 63)) {
-            ok = false;
-            break;
-          }
-          mx = fmaxf(mx, other);
-        }
         mx *= sl2;
-        // Both halves of a split row see the same m and mx, so they agree on m_use.
-        const float m_use = mx > m + kRescaleLog2 ? mx : m;
-        const float alpha = ex2(m - m_use);
-        float l0 = 0.f, l1 = 0.f;
-        uint32_t pk[NC / 2];
-#pragma unroll
-        for (int c = 0; c < NC / 32; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int pair = (c * 32 + i) >> 1;
-            const float x0 = fmaf(__uint_as_float(r[c][i]), sl2, -m_use);
-            const float x1 = fmaf(__uint_as_float(r[c][i + 1]), sl2, -m_use);
-            float e0, e1;
-            if ((pair & 7) < kPoly) {
-              e0 = ex2_poly(x0);
-              e1 = ex2_poly(x1);
-            } else {
-              e0 = ex2(x0);
-              e1 = ex2(x1);
+        // Row maximum across a split row: each half posts its own.  Usually neither half
+        // moves the (stale) running max, so the exponentials start at once with m and the
+        // partner's maximum is read afterwards; in the rare block where it does move the
+        // max the halves agree first (or the exponentials are redone).  Both halves apply
+        // the same rule to the same values, so they use the same m_use.
+        float m_use = m;
+        bool agreed = true;
+        if constexpr (C::kSplit == 2) {
+          post(mx);
+          if (__any_sync(0xFFFFFFFFu, mx > m + kRescaleLog2)) {
+            float other;
+            if (!get(other, 63)) {
+              ok = false;
+              break;
             }
-            l0 += e0;
-            l1 += e1;
-            pk[pair] = pack_bf16x2(e0, e1);
+            mx = fmaxf(mx, other);
+          } else {
+            agreed = false;
           }
+        }
+        if (agreed) m_use = mx > m + kRescaleLog2 ? mx : m;
+        if (kTrace && tslot >= 0) MD_FTRACE(g, tslot + 2);
+        // P V of the previous block must have finished before O is rescaled and, with one
+        // P buffer, before this block's P overwrites the one it reads.
+        auto wait_pv = [&]() -> bool {
+          if (!mbar_wait(o_done, static_cast<uint32_t>(g - 1) & 1u, p.status, 61, abort_flag)) return false;
+          tc_fence_after();
+          return true;
+        };
+        if (PB == 1 && j > 0 && !wait_pv()) {
+          ok = false;
+          break;
+        }
+        // Exponentials, 64 keys at a time; their bf16 pairs go to TMEM (P buffer g % PB,
+        // the A operand of the P V product) as soon as a 32-column group is complete.
+        const uint32_t pcol = tmem + lane_base + C::kPCol + static_cast<uint32_t>((g % PB) * (kBN / 2) + half * (NC / 2));
+        float l0, l1;
+        auto exps = [&](float mu) {
+          l0 = 0.f;
+          l1 = 0.f;
+#pragma unroll
+          for (int k = 0; k < NC / 64; ++k) {
+            uint32_t pq[32];
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+              for (int i = 0; i < 32; i += 2) {
+                const int pair = (cc * 32 + i) >> 1;
+                const float x0 = fmaf(__uint_as_float(r[2 * k + cc][i]), sl2, -mu);
+                const float x1 = fmaf(__uint_as_float(r[2 * k + cc][i + 1]), sl2, -mu);
+                float e0, e1;
+                if ((pair & 7) < kPoly) {
+                  e0 = ex2_poly(x0);
+                  e1 = ex2_poly(x1);
+                } else {
+                  e0 = ex2(x0);
+                  e1 = ex2(x1);
+                }
+                l0 += e0;
+                l1 += e1;
+                pq[pair] = pack_bf16x2(e0, e1);
+              }
+            tmem_st_32x32b_x32(pcol + static_cast<uint32_t>(k * 32), pq);
+          }
+        };
+        exps(m_use);
+        if constexpr (C::kSplit == 2) {
+          if (!agreed) {
+            float other;
+            if (!get(other, 63)) {
+              ok = false;
+              break;
+            }
+            if (__any_sync(0xFFFFFFFFu, other > m + kRescaleLog2)) {
+              // The partner's half moved the max: redo this block's exponentials with it.
+              mx = fmaxf(mx, other);
+              m_use = mx > m + kRescaleLog2 ? mx : m;
+              tmem_st_wait();  // the P columns are rewritten below
+              exps(m_use);
+            }
+          }
+        }
+        const float alpha = ex2(m - m_use);
         l = l * alpha + (l0 + l1);
+        if (kTrace && tslot >= 0) MD_FTRACE(g, tslot + 3);
         if (j > 0) {
-          // P V of the previous block has finished reading P and writing O.
-          if (!mbar_wait(o_done, static_cast<uint32_t>(g - 1) & 1u, p.status, 61, abort_flag)) {
+          if (PB == 2 && !wait_pv()) {
             ok = false;
             break;
           }
-          tc_fence_after();
           // Rows of the partner warp make the same decision, so each half rescales its O columns.
           if (__any_sync(0xFFFFFFFFu, m_use != m)) {
 #pragma unroll
@@ -444,59 +588,53 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
               for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
               tmem_st_32x32b_x32(ta, o);
             }
-            tmem_st_wait();
           }
         }
         m = m_use;
-#pragma unroll
-        for (int k = 0; k < NC / 8; ++k) {
-          const int kk = half * (NC / 8) + k;  // 16-byte column group of the 128-key row
-          uint8_t* dst = sP + (kk >> 3) * (kBM * 128) + sw128_off(row, kk & 7);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(dst)), "r"(pk[4 * k]),
-                       "r"(pk[4 * k + 1]), "r"(pk[4 * k + 2]), "r"(pk[4 * k + 3])
-                       : "memory");
-        }
-        fence_proxy_async_smem();
+        if (kTrace && tslot >= 0) MD_FTRACE(g, tslot + 4);
+        tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full);
+        if (kTrace && tslot >= 0) MD_FTRACE(g, tslot + 5);
       }
       if (!ok) break;
       if constexpr (C::kSplit == 2) {
-        float other = l;
-        if (!exchange(other, 64)) break;
+        float other;
+        post(l);
+        if (!get(other, 64)) break;
         l += other;
       }
-      // Epilogue: O / l straight from TMEM, lse for the backward pass.
+      // Epilogue: O / l from TMEM into the 128B-swizzled staging tile (this item's Q
+      // buffer: every score product of the item has completed), lse to global memory.
       if (!mbar_wait(o_done, static_cast<uint32_t>(g - 1) & 1u, p.status, 62, abort_flag)) break;
       tc_fence_after();
       const int q = qt * kBM + row;
       const float inv_l = 1.0f / l;
-      uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) +
-                      (static_cast<long long>(b) * p.S + q) * p.ldo * 2 + static_cast<long long>(h) * p.dr * 2;
+      uint8_t* stage = sQ + (t % QB) * C::kTileBytes;
 #pragma unroll
       for (int cc = 0; cc < OC; ++cc) {
-        const int c = half * OC + cc;
-        if (c * 32 >= p.dr) break;  // uniform: the padded columns are not stored
+        const int c = half * OC + cc;  // 32-column chunk: atom c / 2, 16-byte groups (c % 2) * 4 + k
         uint32_t o[32];
         tmem_ld_32x32b_x32(tmem + lane_base + C::kOCol + static_cast<uint32_t>(c * 32), o);
         tmem_ld_wait();
-        if (q < p.S) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            if (c * 32 + k * 8 >= p.dr) break;
-            uint4 v;
-            v.x = pack_bf16x2(__uint_as_float(o[8 * k + 0]) * inv_l, __uint_as_float(o[8 * k + 1]) * inv_l);
-            v.y = pack_bf16x2(__uint_as_float(o[8 * k + 2]) * inv_l, __uint_as_float(o[8 * k + 3]) * inv_l);
-            v.z = pack_bf16x2(__uint_as_float(o[8 * k + 4]) * inv_l, __uint_as_float(o[8 * k + 5]) * inv_l);
-            v.w = pack_bf16x2(__uint_as_float(o[8 * k + 6]) * inv_l, __uint_as_float(o[8 * k + 7]) * inv_l);
-            *reinterpret_cast<uint4*>(orow + c * 64 + k * 16) = v;
-          }
+        for (int k = 0; k < 4; ++k) {
+          uint8_t* dst = stage + (c >> 1) * (kBM * 128) + sw128_off(row, (c & 1) * 4 + k);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(dst)),
+                       "r"(pack_bf16x2(__uint_as_float(o[8 * k + 0]) * inv_l, __uint_as_float(o[8 * k + 1]) * inv_l)),
+                       "r"(pack_bf16x2(__uint_as_float(o[8 * k + 2]) * inv_l, __uint_as_float(o[8 * k + 3]) * inv_l)),
+                       "r"(pack_bf16x2(__uint_as_float(o[8 * k + 4]) * inv_l, __uint_as_float(o[8 * k + 5]) * inv_l)),
+                       "r"(pack_bf16x2(__uint_as_float(o[8 * k + 6]) * inv_l, __uint_as_float(o[8 * k + 7]) * inv_l))
+                       : "memory");
         }
       }
       if (half == 0 && q < p.S)
         p.lse[(static_cast<long long>(b) * p.H + h) * p.S + q] = (m + lg2(l)) * 0.6931471805599453f;
+      fence_proxy_async_smem();
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_staged[t % QB]);
     }
   }
 
@@ -505,6 +643,9 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
+
+#undef MD_FTRACE
+
 
 
 // ===========================================================================
@@ -1584,17 +1725,14 @@ int g_sms = 0;
 long long* g_trace = nullptr;  // device buffer set by md_attn_trace_enable (analysis only)
 
 // Pairs of every 8 softmax exponentials computed on the FMA pipe (fwd_kernel's
-// kPoly): 0, 2 or 4, from MINIDIST_ATTN_EXP_POLY; default 0.  Measured on B200
-// (fwd, causal, bf16): d 64 16x12x1024 71.2 / 75.4 / 91.7 us, d 128 4x16x2048
-// 108.7 / 107.8 / 113.0 us for 0 / 2 / 4 -- the softmax warps are not bound by
-// the MUFU rate, so the extra FMA-pipe instructions do not pay at these sizes.
+// kPoly): 0, 2 or 4; MINIDIST_ATTN_EXP_POLY overrides the per-head-size default.
 int fwd_poly(int D) {
-  (void)D;
   static const int env = [] {
     const char* e = getenv("MINIDIST_ATTN_EXP_POLY");
     return e && *e ? atoi(e) : -1;
   }();
-  return env == 2 || env == 4 ? env : 0;
+  if (env == 0 || env == 2 || env == 4) return env;
+  return D == 64 ? 0 : 0;
 }
 
 template <int D>
@@ -1602,11 +1740,15 @@ int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, floa
                   float scale, void* status, cudaStream_t st, int dr = D) {
   using C = md::attn_tc::FwdCfg<D>;
   if (!get_encoder()) return -3;
-  CUtensorMap tm;
+  // Loads read Q/K/V in place; the output tiles are stored through a second map
+  // (rows past S and, for dr < D, columns past dr are clipped by the store).
+  CUtensorMap tm, to;
   if (dr == D) {
-    if (!make_map_bsc(&tm, qkv, B, S, 3LL * H * D, ldq)) return -4;
+    if (!make_map_bsc(&tm, qkv, B, S, 3LL * H * D, ldq) || !make_map_bsc(&to, out, B, S, 1LL * H * D, ldo)) return -4;
   } else {
-    if (dr % 8 || dr > D || !make_map_bshd(&tm, qkv, B, S, 3 * H, dr, ldq)) return -4;
+    if (dr % 8 || dr > D || !make_map_bshd(&tm, qkv, B, S, 3 * H, dr, ldq) ||
+        !make_map_bshd(&to, out, B, S, H, dr, ldo))
+      return -4;
   }
   if (g_sms == 0) {
     int dev = 0;
@@ -1614,8 +1756,6 @@ int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, floa
     cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
   }
   md::attn_tc::FwdParams p;
-  p.out = out;
-  p.ldo = ldo;
   p.lse = lse;
   p.B = B;
   p.H = H;
@@ -1625,14 +1765,17 @@ int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, floa
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = reinterpret_cast<md::Status*>(status);
   p.dr = dr;
+  p.trace = g_trace;
   const int poly = fwd_poly(D);
-  auto k = poly == 4 ? md::attn_tc::fwd_kernel<D, 4> : poly == 2 ? md::attn_tc::fwd_kernel<D, 2>
-                                                                 : md::attn_tc::fwd_kernel<D, 0>;
+  auto k = g_trace != nullptr ? (poly == 2 ? md::attn_tc::fwd_kernel<D, 2, true> : md::attn_tc::fwd_kernel<D, 0, true>)
+           : poly == 4        ? md::attn_tc::fwd_kernel<D, 4, false>
+           : poly == 2        ? md::attn_tc::fwd_kernel<D, 2, false>
+                              : md::attn_tc::fwd_kernel<D, 0, false>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
   const int slots = g_sms * C::kCtasPerSm;
   const int grid = p.items < slots ? p.items : slots;
-  md::launch_pdl(k, grid, dim3(C::kThreads), C::kSmemBytes, st, tm, p);
+  md::launch_pdl(k, grid, dim3(C::kThreads), C::kSmemBytes, st, tm, to, p);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -38,6 +38,8 @@ _SIGS = {
     "md_adamw_chunk": "i:",
     "md_nonfinite": "i:ppipp",
     "md_adamw_entry_bytes": "i:",
+    "md_attn_trace_enable": "i:i",
+    "md_attn_trace_read": "i:p",
 }
 for _n, _s in _SIGS.items():
     nat.declare(_n, _s)
@@ -129,6 +131,23 @@ def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int, D: int, impl: str |
 def attention_bwd_impl() -> str:
     """The attention backward in use: ``"tc"`` (tcgen05, d = 64 / 80 / 128) or ``"mma"``."""
     return _ATTN_BWD
+
+
+def attention_pipeline_trace(fn) -> torch.Tensor:
+    """Run ``fn`` (one tcgen05 attention launch) with the kernel's pipeline trace on and return
+    CTA 0's ``clock64()`` stamps as int64 [64 key blocks, 32 slots] (0 = not recorded).
+
+    Analysis only: the trace costs a global store per stamp.  Slot meanings are listed beside
+    the kernels' MD_FTRACE / MD_TRACE macros."""
+    nat.check(nat.lib().md_attn_trace_enable(1), "md_attn_trace_enable")
+    try:
+        fn()
+        torch.cuda.synchronize()
+        out = torch.zeros(64, 32, dtype=torch.int64)
+        nat.check(nat.lib().md_attn_trace_read(out.data_ptr()), "md_attn_trace_read")
+    finally:
+        nat.lib().md_attn_trace_enable(0)
+    return out
 
 
 def attention_bwd(qkv, out, dout, lse, B: int, S: int, H: int, D: int, dqkv: torch.Tensor | None = None,
