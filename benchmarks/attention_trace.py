@@ -32,6 +32,7 @@ def main(argv=None) -> int:
     p.add_argument("--shape", default="16,12,1024,64", help="B,H,S,D")
     p.add_argument("--skip", type=int, default=2)
     p.add_argument("--json", default=None)
+    p.add_argument("--bwd", action="store_true", help="trace the backward kernel instead (head_dim 64)")
     a = p.parse_args(argv)
     import torch
 
@@ -43,6 +44,8 @@ def main(argv=None) -> int:
     for _ in range(3):
         K.attention_fwd(qkv, B, S, H, D, impl="tc")
     torch.cuda.synchronize()
+    if a.bwd:
+        return _bwd(K, nat, qkv, B, H, S, D, a)
     tr = K.attention_pipeline_trace(lambda: K.attention_fwd(qkv, B, S, H, D, impl="tc")).tolist()
     nat.check_status()
     rows = [r for r in tr if r[0] and r[5]][a.skip:]
@@ -59,6 +62,44 @@ def main(argv=None) -> int:
     out["S issue -> scores ready"] = med([r[0] - r[12] for r in rows if r[0] and r[12]])
     for k, v in out.items():
         print(f"{k:>52}: {v}")
+    if a.json:
+        Path(a.json).write_text(json.dumps({"raw": tr, "summary": out}, indent=1))
+    return 0
+
+
+def _bwd(K, nat, qkv, B, H, S, D, a) -> int:
+    """Backward trace (head_dim 64 kernel).  Compute-warp slots: 1 scores ready, 2 first
+    half of P / dS computed, 3 P / dS buffers free, 16.. P / dS handed to the MMA warp (per
+    warp); MMA slots 12 scores issued, 5 P / dS received, 7 dQ TMEM free, 8 dV issued;
+    9 dQ drained; 11 Q / dO load issued."""
+    import torch
+
+    y, lse = K.attention_fwd(qkv, B, S, H, D, impl="tc")
+    dy = torch.randn_like(y)
+    for _ in range(3):
+        K.attention_bwd(qkv, y, dy, lse, B, S, H, D, impl="tc")
+    torch.cuda.synchronize()
+    tr = K.attention_pipeline_trace(lambda: K.attention_bwd(qkv, y, dy, lse, B, S, H, D, impl="tc")).tolist()
+    nat.check_status()
+    med = lambda xs: statistics.median(xs) if xs else float("nan")  # noqa: E731
+    rows = [(g, r) for g, r in enumerate(tr) if r[1] and r[16]][a.skip:]
+    out = {"shape": [B, H, S, D], "blocks": len(rows)}
+    out["scores ready -> first half computed"] = med([r[2] - r[1] for _, r in rows if r[2]])
+    out["first half -> buffers free"] = med([r[3] - r[2] for _, r in rows if r[3] and r[2]])
+    out["buffers free -> P / dS handed (warp 2)"] = med([r[16] - r[3] for _, r in rows if r[3]])
+    periods = [tr[g + 1][1] - tr[g][1] for g in range(a.skip, 63) if tr[g][1] and tr[g + 1][1]]
+    out["block period (median)"] = med(periods)
+    out["block period (max)"] = max(periods) if periods else float("nan")
+    out["scores issue -> scores ready"] = med([r[1] - r[12] for _, r in rows if r[12]])
+    for k, v in out.items():
+        print(f"{k:>52}: {v}")
+    print("\nper block (cycles from block 0's scores-ready): scores issued, ready, handed, dV issued, dQ drained")
+    base = tr[0][1]
+    for g in range(min(40, len(tr))):
+        r = tr[g]
+        if not r[1]:
+            break
+        print(g, *[(r[i] - base) if r[i] else -1 for i in (12, 1, 16, 8, 9)])
     if a.json:
         Path(a.json).write_text(json.dumps({"raw": tr, "summary": out}, indent=1))
     return 0

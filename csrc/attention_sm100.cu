@@ -130,28 +130,10 @@ __device__ __forceinline__ float lg2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, for the share of the softmax exponentials taken off the
-// MUFU unit (16 results per clock per SM: the exponentials of a 128 x 128 block
-// alone keep it busy for 1024 cycles).  Range reduction x = n + f with
-// n = round-to-nearest(x) by the 1.5 * 2^23 add (the sum's low mantissa bits
-// then hold n), f in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose
-// coefficients are the minimax fit for relative error on [-1/2, 1/2] (Remez
-// exchange, computed for this kernel: max relative error 7.5e-5, well below the
-// 2^-9 rounding of the bf16 P it feeds); 2^n by adding n to the exponent field.
-// x is clamped at -126 so the exponent field never underflows: masked scores
-// (-inf) give ~1.2e-38 instead of 0.
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float t = __fadd_rn(x, 12582912.0f);
-  const float f = __fadd_rn(x, -__fadd_rn(t, -12582912.0f));
-  const float q = fmaf(fmaf(fmaf(0.05517166853f, f, 0.24261112511f), f, 0.69326096773f), f, 0.99992805719f);
-  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
-}
 
 // tm: Q/K/V loads ([B, S, 3*H*D], or [B, S, 3H, dr]); to: output stores
-// ([B, S, H*D], or [B, S, H, dr]).  kPoly: of every 8 pairs of exponentials a
-// softmax thread computes, how many go through ex2_poly instead of ex2.approx.
-template <int D, int kPoly, bool kTrace>
+// ([B, S, H*D], or [B, S, H, dr]).
+template <int D, bool kTrace>
 __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
     fwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap to,
                const __grid_constant__ FwdParams p) {
@@ -533,20 +515,11 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
             for (int cc = 0; cc < 2; ++cc)
 #pragma unroll
               for (int i = 0; i < 32; i += 2) {
-                const int pair = (cc * 32 + i) >> 1;
-                const float x0 = fmaf(__uint_as_float(r[2 * k + cc][i]), sl2, -mu);
-                const float x1 = fmaf(__uint_as_float(r[2 * k + cc][i + 1]), sl2, -mu);
-                float e0, e1;
-                if ((pair & 7) < kPoly) {
-                  e0 = ex2_poly(x0);
-                  e1 = ex2_poly(x1);
-                } else {
-                  e0 = ex2(x0);
-                  e1 = ex2(x1);
-                }
+                const float e0 = ex2(fmaf(__uint_as_float(r[2 * k + cc][i]), sl2, -mu));
+                const float e1 = ex2(fmaf(__uint_as_float(r[2 * k + cc][i + 1]), sl2, -mu));
                 l0 += e0;
                 l1 += e1;
-                pq[pair] = pack_bf16x2(e0, e1);
+                pq[(cc * 32 + i) >> 1] = pack_bf16x2(e0, e1);
               }
             tmem_st_32x32b_x32(pcol + static_cast<uint32_t>(k * 32), pq);
           }
@@ -705,10 +678,11 @@ struct BwdParams {
   long long* trace;    // optional: CTA 0 records clock64() at pipeline hand-offs, [64 blocks][32]
 };
 
-// Pipeline trace for performance analysis (CTA 0, first 64 blocks; no-op unless enabled).
+// Pipeline trace for performance analysis (CTA 0, first 64 blocks; only in the
+// kTrace instantiation).
 #define MD_TRACE(gg, slot)                                                                  \
   do {                                                                                     \
-    if (p.trace != nullptr && blockIdx.x == 0 && (gg) < 64) p.trace[(gg) * 32 + (slot)] = clock64(); \
+    if (kTrace && blockIdx.x == 0 && (gg) < 64) p.trace[(gg) * 32 + (slot)] = clock64();   \
   } while (0)
 
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
@@ -716,7 +690,7 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                : "memory");
 }
 
-template <int D>
+template <int D, bool kTrace>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
                const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ BwdParams p) {
@@ -1724,17 +1698,6 @@ bool make_map_f32_bshd(CUtensorMap* map, const void* ptr, int B, int S, int H, i
 int g_sms = 0;
 long long* g_trace = nullptr;  // device buffer set by md_attn_trace_enable (analysis only)
 
-// Pairs of every 8 softmax exponentials computed on the FMA pipe (fwd_kernel's
-// kPoly): 0, 2 or 4; MINIDIST_ATTN_EXP_POLY overrides the per-head-size default.
-int fwd_poly(int D) {
-  static const int env = [] {
-    const char* e = getenv("MINIDIST_ATTN_EXP_POLY");
-    return e && *e ? atoi(e) : -1;
-  }();
-  if (env == 0 || env == 2 || env == 4) return env;
-  return D == 64 ? 0 : 0;
-}
-
 template <int D>
 int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, float* lse, int B, int H, int S,
                   float scale, void* status, cudaStream_t st, int dr = D) {
@@ -1766,11 +1729,7 @@ int fwd_tc_launch(const void* qkv, long long ldq, void* out, long long ldo, floa
   p.status = reinterpret_cast<md::Status*>(status);
   p.dr = dr;
   p.trace = g_trace;
-  const int poly = fwd_poly(D);
-  auto k = g_trace != nullptr ? (poly == 2 ? md::attn_tc::fwd_kernel<D, 2, true> : md::attn_tc::fwd_kernel<D, 0, true>)
-           : poly == 4        ? md::attn_tc::fwd_kernel<D, 4, false>
-           : poly == 2        ? md::attn_tc::fwd_kernel<D, 2, false>
-                              : md::attn_tc::fwd_kernel<D, 0, false>;
+  auto k = g_trace != nullptr ? md::attn_tc::fwd_kernel<D, true> : md::attn_tc::fwd_kernel<D, false>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
   const int slots = g_sms * C::kCtasPerSm;
@@ -1816,7 +1775,7 @@ int bwd_tc_launch(const void* qkv, long long ldq, const void* dout, long long ld
   p.flags = flags;
   p.status = reinterpret_cast<md::Status*>(status);
   p.trace = g_trace;
-  auto k = md::attn_tc::bwd_kernel<D>;
+  auto k = g_trace != nullptr ? md::attn_tc::bwd_kernel<D, true> : md::attn_tc::bwd_kernel<D, false>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
   const int grid = p.items < g_sms ? p.items : g_sms;
