@@ -628,8 +628,10 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
 // longest-first (tile kt meets nqt - kt query blocks).  Per query block i:
 //   S^T  = K Q_i^T          (TMEM, 128 keys x 128 queries)
 //   dP^T = V dO_i^T         (TMEM)
-//   P^T  = exp(S^T * scale - lse_i),  dS^T = P^T (dP^T - delta_i)   [compute warps, bf16 to smem]
-//   dV  += P^T dO_i,   dK += dS^T Q_i      (TMEM accumulators for the whole item)
+//   P^T  = exp(S^T * scale - lse_i),  dS^T = P^T (dP^T - delta_i)   [compute warps, bf16:
+//                                             P^T to TMEM, dS^T to shared memory]
+//   dV  += P^T dO_i,   dK += dS^T Q_i      (TMEM accumulators for the whole item; dV reads
+//                                             P^T from TMEM as its A operand)
 //   dQ_i = dS K_j                            (TMEM, drained by the dQ warps into an
 //                                             fp32 accumulator with bulk reduce-adds)
 // Roles: warp 0 TMA, warp 1 MMA, warps 2..9 compute (thread = key row; warps
@@ -637,10 +639,15 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
 // share every SM sub-partition), warps 10..13 dQ drain (thread = query row,
 // staged through shared memory into bulk reduce-adds).
 // The tensor core runs the next block's score products as soon as the compute
-// warps hold this block's scores in registers, then (once P^T/dS^T are in
-// shared memory) dK and dQ (which read dS^T; a single buffer, released as
-// soon as they are done), then dV (which reads P^T; double-buffered).  Q/dO tiles stream
-// through three stages so their loads start two blocks ahead.
+// warps hold this block's scores in registers and its Q/dO tile has landed (or,
+// when this block's P^T/dS^T are ready first, right after this block's
+// products), then dK and dQ (which read dS^T; a single buffer, released as
+// soon as they are done), then dV (which reads P^T; the compute warps write the
+// next block's P^T once it has finished).  Q/dO tiles stream through three stages.  K/V are double-buffered: the next item's tiles load while this
+// item runs, and a finished item's dK / dV are staged (bf16, 128B-swizzled) in its own
+// K / V buffers and written by the TMA warp with bulk tensor stores, after which the
+// buffers are reloaded -- so an item boundary costs neither a K/V load nor the compute
+// warps' time for scattered global stores.
 // ===========================================================================
 constexpr int kBwdThreads = 448;
 constexpr int kBwdCompute = 8;  // compute warps
@@ -650,15 +657,18 @@ struct BwdCfg {
   static constexpr int kChunks = D / 64;
   static constexpr int kTileBytes = 128 * D * 2;
   static constexpr int kQStages = 3;
-  static constexpr int kPBytes = 128 * 128 * 2;
-  // K, V | (Q, dO) x stages | P^T x 2 | dS^T | lse, delta x 2 blocks
-  static constexpr int kSmemData = (2 + 2 * kQStages) * kTileBytes + 3 * kPBytes + 2 * 2 * 128 * 4;
+  static constexpr int kPBytes = 128 * 128 * 2;       // dS^T (bf16)
+  static constexpr int kStgBytes = 128 * D * 4;       // dQ staging (fp32, D / 32 boxes [128][32])
+  // (K, V) x 2 | (Q, dO) x stages | dS^T | dQ staging | lse, delta x 2 blocks
+  static constexpr int kSmemData = (4 + 2 * kQStages) * kTileBytes + kPBytes + kStgBytes + 2 * 2 * 128 * 4;
   // No alignment slack fits: the dynamic window must start 1024-byte aligned
   // (checked in the kernel).
   static constexpr int kSmemBytes = kSmemData + 256;
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 256 + D, kColDQ = 256 + 2 * D;
-  static_assert(256 + 3 * D <= 512, "TMEM budget");
+  // P^T (bf16 pairs, 64 columns) is the A operand of dV += P^T dO.
+  static constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 256 + D, kColDQ = 256 + 2 * D,
+                            kColP = 256 + 3 * D;
+  static_assert(256 + 3 * D + 64 <= 512, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -693,7 +703,8 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
 template <int D, bool kTrace>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
-               const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ BwdParams p) {
+               const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ CUtensorMap tmOut,
+               const __grid_constant__ BwdParams p) {
   using C = BwdCfg<D>;
   constexpr int QS = C::kQStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -701,30 +712,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (threadIdx.x == 0) report(p.status, kBadArgument, 69, smem_u32(smem_raw));
     return;
   }
-  uint8_t* sK = smem_raw;
-  uint8_t* sV = sK + C::kTileBytes;
-  uint8_t* sQ = sV + C::kTileBytes;               // [QS]
+  uint8_t* sKV = smem_raw;                        // [2] x (K, V); K of buffer kb at sKV + 2 kb tile
+  uint8_t* sQ = sKV + 4 * C::kTileBytes;          // [QS]
   uint8_t* sdO = sQ + QS * C::kTileBytes;         // [QS]
-  uint8_t* sPt = sdO + QS * C::kTileBytes;        // [2] P^T
-  uint8_t* sdSt = sPt + 2 * C::kPBytes;           // dS^T
-  float* sL = reinterpret_cast<float*>(sdSt + C::kPBytes);  // [2][128] lse (log2 units)
+  uint8_t* sdSt = sdO + QS * C::kTileBytes;       // dS^T
+  uint8_t* sStg = sdSt + C::kPBytes;              // dQ staging
+  float* sL = reinterpret_cast<float*>(sStg + C::kStgBytes);  // [2][128] lse (log2 units)
   float* sDel = sL + 2 * 128;                                   // [2][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 2 * 128);
-  uint64_t* kv_full = bars + 0;
-  uint64_t* kv_empty = bars + 1;
+  static_assert(QS == 3, "barrier slots below are laid out for three Q/dO stages");
+  uint64_t* kv_full = bars + 0;    // [2]
   uint64_t* qd_full = bars + 2;    // [3]
   uint64_t* qd_empty = bars + 5;   // [3]
+  uint64_t* kv_staged = bars + 26; // [2] the item's dK / dV are in its K / V buffers
   uint64_t* sd_full = bars + 8;
   uint64_t* sd_free = bars + 9;
   uint64_t* pds_full = bars + 10;
-  uint64_t* p_free = bars + 11;    // [2] per P^T buffer
+  uint64_t* p_free = bars + 11;    // [2] by block parity: dV of the block has completed
   uint64_t* ds_free = bars + 13;
   uint64_t* dq_full = bars + 14;
   uint64_t* dq_free = bars + 15;
   uint64_t* dkv_free = bars + 16;
   uint64_t* drain = bars + 17;
   uint64_t* stage_bar = bars + 18;  // [2] (slot 20 unused)
-  uint64_t* pst_free = bars + 21;   // [2] P^T buffer free again after the dQ staging
+  uint64_t* pst_free = bars + 21;   // [0]: the dQ staging tile has been read by the reduce-adds (slot 22 unused)
   uint64_t* dq_staged = bars + 23;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 25);
@@ -734,8 +745,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int bhc = p.B * p.H;
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
-    mbar_init(kv_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_staged[i], kBwdCompute);
+    }
     for (int i = 0; i < QS; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
@@ -759,6 +772,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tma_prefetch_desc(&tmQKV);
     tma_prefetch_desc(&tmDO);
     tma_prefetch_desc(&tmDQ);
+    tma_prefetch_desc(&tmOut);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -773,23 +787,47 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   pdl_wait();
 
   if (warp == 0 && lane == 0) {
-    // ------------------------------------------------------------ TMA producer
-    int kv_armed = -1;
+    // ------------------------------------------------------------ TMA loads and dK / dV stores
+    int kv_armed[2] = {-1, -1};
     int q_armed[QS];
     for (int i = 0; i < QS; ++i) q_armed[i] = -1;
-    int g = 0, t = 0;
+    // Store item ti's dK / dV (staged by the compute warps in K / V buffer ti % 2).
+    auto store_dkv = [&](int ti) -> bool {
+      const int kb = ti & 1;
+      if (!mbar_wait(&kv_staged[kb], static_cast<uint32_t>(ti >> 1) & 1u, p.status, 74, abort_flag)) return false;
+      const int w = blockIdx.x + ti * gridDim.x;
+      const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
+      const uint8_t* sk = sKV + 2 * kb * C::kTileBytes;
+#pragma unroll
+      for (int c = 0; c < C::kChunks; ++c) {
+        tma_store_3d(&tmOut, sk + c * 16384, h * 3 * D + D + c * 64, kt * 128, b);
+        tma_store_3d(&tmOut, sk + C::kTileBytes + c * 16384, h * 3 * D + 2 * D + c * 64, kt * 128, b);
+      }
+      bulk_commit_group();
+      return true;
+    };
+    int g = 0, t = 0, stored = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
       const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
-      const uint32_t tph = static_cast<uint32_t>(t) & 1u;
-      if (!mbar_wait(kv_empty, tph ^ 1u, p.status, 70, abort_flag)) break;
-      mbar_arrive_expect_tx(kv_full, 2 * C::kTileBytes);
-      kv_armed = static_cast<int>(tph);
+      const int kb = t & 1;
+      if (t >= 2) {
+        // Buffer kb last held item t-2: store its dK / dV, reload once the store has read them.
+        if (!store_dkv(t - 2)) {
+          ok = false;
+          break;
+        }
+        stored = t - 1;
+        bulk_wait_read_all();
+      }
+      mbar_arrive_expect_tx(&kv_full[kb], 2 * C::kTileBytes);
+      kv_armed[kb] = static_cast<int>(static_cast<uint32_t>(t >> 1) & 1u);
       const int col0 = h * 3 * D;
+      uint8_t* sk = sKV + 2 * kb * C::kTileBytes;
 #pragma unroll
       for (int c = 0; c < C::kChunks; ++c) {
-        tma_load_3d(&tmQKV, kv_full, sK + c * 16384, col0 + D + c * 64, kt * 128, b);
-        tma_load_3d(&tmQKV, kv_full, sV + c * 16384, col0 + 2 * D + c * 64, kt * 128, b);
+        tma_load_3d(&tmQKV, &kv_full[kb], sk + c * 16384, col0 + D + c * 64, kt * 128, b);
+        tma_load_3d(&tmQKV, &kv_full[kb], sk + C::kTileBytes + c * 16384, col0 + 2 * D + c * 64, kt * 128, b);
       }
       for (int i = kt; i < p.n_t; ++i, ++g) {
         const int st = g % QS;
@@ -808,7 +846,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
     }
-    if (kv_armed >= 0) mbar_wait(kv_full, static_cast<uint32_t>(kv_armed), p.status, 72, nullptr);
+    // The last items' dK / dV (skipped after an abort: they were never staged).
+    if (ok)
+      for (int ti = stored; ti < t; ++ti)
+        if (!store_dkv(ti)) break;
+    bulk_wait_all();
+    for (int i = 0; i < 2; ++i)
+      if (kv_armed[i] >= 0) mbar_wait(&kv_full[i], static_cast<uint32_t>(kv_armed[i]), p.status, 72, nullptr);
     for (int i = 0; i < QS; ++i)
       if (q_armed[i] >= 0) mbar_wait(&qd_full[i], static_cast<uint32_t>(q_armed[i]), p.status, 73, nullptr);
   } else if (warp == 1) {
@@ -817,20 +861,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     constexpr uint32_t idKV = idesc_bf16_f32(128, D, false, true);     // dV, dK: B MN-major
     constexpr uint32_t idQ = idesc_bf16_f32(128, D, true, true);       // dQ: A (dS) and B (K) MN-major
     // Base descriptors; an operand at byte offset `off` is base + (off >> 4).
-    const uint64_t dK_k = sdesc_sw128(smem_u32(sK), 16, 1024);
-    const uint64_t dK_mn = sdesc_sw128(smem_u32(sK), 16384, 1024);
-    const uint64_t dV_k = sdesc_sw128(smem_u32(sV), 16, 1024);
+    // K / V buffer kb: + 2 kb (K) or 2 kb + 1 (V) tiles.
+    const uint64_t dK_k0 = sdesc_sw128(smem_u32(sKV), 16, 1024);
+    const uint64_t dK_mn0 = sdesc_sw128(smem_u32(sKV), 16384, 1024);
+    const uint64_t dV_k0 = sdesc_sw128(smem_u32(sKV + C::kTileBytes), 16, 1024);
     const uint64_t dQ_k = sdesc_sw128(smem_u32(sQ), 16, 1024);
     const uint64_t dQ_mn = sdesc_sw128(smem_u32(sQ), 16384, 1024);
     const uint64_t ddO_k = sdesc_sw128(smem_u32(sdO), 16, 1024);
     const uint64_t ddO_mn = sdesc_sw128(smem_u32(sdO), 16384, 1024);
-    const uint64_t dP_k = sdesc_sw128(smem_u32(sPt), 16, 1024);
     const uint64_t ddS_k = sdesc_sw128(smem_u32(sdSt), 16, 1024);
     const uint64_t ddS_mn = sdesc_sw128(smem_u32(sdSt), 16384, 1024);
     constexpr uint32_t kTile16 = C::kTileBytes >> 4;
-    constexpr uint32_t kP16 = C::kPBytes >> 4;
     int g = 0, t = 0;
     bool ok = true;
+    uint64_t dK_k = dK_k0, dK_mn = dK_mn0, dV_k = dV_k0;  // this item's K / V buffer
     // Score products for block gg.
     auto issue_scores = [&](int gg) -> bool {
       const int st = gg % QS;
@@ -852,17 +896,45 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
       const int kt = w / bhc;
       const int n = p.n_t - kt;
-      if (!mbar_wait(kv_full, static_cast<uint32_t>(t) & 1u, p.status, 82, abort_flag)) break;
+      const int kb = t & 1;
+      if (!mbar_wait(&kv_full[kb], static_cast<uint32_t>(t >> 1) & 1u, p.status, 82, abort_flag)) break;
+      dK_k = dK_k0 + 2 * kb * kTile16;
+      dK_mn = dK_mn0 + 2 * kb * kTile16;
+      dV_k = dV_k0 + 2 * kb * kTile16;
       if (!issue_scores(g)) break;
       for (int u = 0; u < n; ++u, ++g) {
         const int st = g % QS;
         const int pb = g & 1;
-        // The next block's score products go first: they only need the
-        // compute warps to have read this block's scores into registers
-        // (mid-block), so they run while the compute warps finish this block.
-        if (u + 1 < n && !issue_scores(g + 1)) {
-          ok = false;
-          break;
+        // The next block's score products normally go first: they only need the compute
+        // warps to have read this block's scores into registers (mid-block) and the next
+        // Q / dO tile, so they run while the compute warps finish this block.  If this
+        // block's P / dS arrive before that tile has landed, its products go first.
+        bool scores_after = false;
+        if (u + 1 < n) {
+          const int st1 = (g + 1) % QS;
+          const uint64_t t0 = globaltimer_ns();
+          for (uint32_t it = 0;; ++it) {
+            if (mbar_test_wait(&qd_full[st1], static_cast<uint32_t>((g + 1) / QS) & 1u) &&
+                mbar_test_wait(sd_free, (static_cast<uint32_t>(g + 1) & 1u) ^ 1u))
+              break;
+            if (mbar_test_wait(pds_full, static_cast<uint32_t>(g) & 1u)) {
+              scores_after = true;
+              break;
+            }
+            if ((it & 63u) == 63u && (*abort_flag || globaltimer_ns() - t0 > kPipelineTimeoutNs)) {
+              if (!*abort_flag) {
+                report(p.status, kTimeoutPipeline, 87, 0);
+                *abort_flag = 1;
+              }
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) break;
+          if (!scores_after && !issue_scores(g + 1)) {
+            ok = false;
+            break;
+          }
         }
         MD_TRACE(g, 6);
         if (!mbar_wait(pds_full, static_cast<uint32_t>(g) & 1u, p.status, 83, abort_flag)) {
@@ -876,7 +948,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         tc_fence_after();
         const uint64_t qmn = dQ_mn + st * kTile16, omn = ddO_mn + st * kTile16;
-        const uint64_t pk = dP_k + pb * kP16;
         const uint32_t acc0 = u > 0 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
@@ -893,16 +964,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_bf16_ss_elect(tmem + C::kColDQ, ddS_mn + kk * 128, dK_mn + kk * 128, idQ, kk > 0 ? 1u : 0u);
         umma_commit_elect(ds_free);
         umma_commit_elect(dq_full);
+        // dV += P^T dO with P^T from TMEM (8 columns per 16 queries).
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_bf16_ss_elect(tmem + C::kColDV, pk + (((kk >> 2) * 16384 + (kk & 3) * 32) >> 4), omn + kk * 128, idKV,
+          umma_bf16_ts_elect(tmem + C::kColDV, tmem + C::kColP + static_cast<uint32_t>(kk * 8), omn + kk * 128, idKV,
                              (acc0 | kk) ? 1u : 0u);
         umma_commit_elect(&qd_empty[st]);
         umma_commit_elect(&p_free[pb]);
         MD_TRACE(g, 8);
+        if (scores_after && !issue_scores(g + 1)) {
+          ok = false;
+          break;
+        }
       }
       if (!ok) break;
-      umma_commit_elect(kv_empty);
     }
     umma_commit_elect(drain);
     mbar_wait(drain, 0, p.status, 86, nullptr);
@@ -956,10 +1031,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       next_block(blockIdx.x, kt0, pre_w, pre_i);
       if (pre_w >= 0) pre = load_raw(pre_w, pre_i);
     }
-    int g = 0;
+    int g = 0, t = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x) {
-      const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
+      const int kt = w / bhc;
       const int n = p.n_t - kt;
       for (int u = 0; u < n; ++u, ++g) {
         if (!mbar_wait(&stage_bar[g & 1], static_cast<uint32_t>(g >> 1) & 1u, p.status, 89, abort_flag)) {
@@ -975,7 +1050,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         if (threadIdx.x == 64) MD_TRACE(g, 1);
         tc_fence_after();
-        uint8_t* sP = sPt + (g & 1) * C::kPBytes + half * 16384;
         uint8_t* sdS = sdSt + half * 16384;
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
@@ -1009,9 +1083,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
           if (c == 0) {
             if (threadIdx.x == 64) MD_TRACE(g, 2);
-            // dV of block g-2 and the dQ staging after it are done with this
-            // P^T buffer; dK/dQ of block g-1 have finished reading dS^T.
-            if ((g >= 2 && !mbar_wait(&pst_free[g & 1], (static_cast<uint32_t>(g >> 1) & 1u) ^ 1u, p.status, 91,
+            // dV of block g-1 has finished reading P^T (TMEM); dK/dQ of block g-1
+            // have finished reading dS^T.
+            if ((g >= 1 && !mbar_wait(&p_free[(g - 1) & 1], static_cast<uint32_t>((g - 1) >> 1) & 1u, p.status, 91,
                                       abort_flag)) ||
                 (g >= 1 && !mbar_wait(ds_free, static_cast<uint32_t>(g - 1) & 1u, p.status, 93, abort_flag))) {
               ok = false;
@@ -1028,18 +1102,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
               if (w2 >= 0) pre = load_raw(w2, i2);
             }
           }
+          // P^T to TMEM (16 columns = these 32 queries), dS^T to shared memory.
+          tc_fence_after();
+          tmem_st_32x32b_x16(tmem + lane_base + C::kColP + static_cast<uint32_t>(half * 32 + c * 16), pp);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint32_t off = sw128_off(krow, c * 4 + k);
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(sP + off)), "r"(pp[4 * k]),
-                         "r"(pp[4 * k + 1]), "r"(pp[4 * k + 2]), "r"(pp[4 * k + 3])
-                         : "memory");
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(sdS + off)), "r"(dd[4 * k]),
                          "r"(dd[4 * k + 1]), "r"(dd[4 * k + 2]), "r"(dd[4 * k + 3])
                          : "memory");
           }
         }
         if (!ok) break;
+        tmem_st_wait();
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
@@ -1049,45 +1124,47 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
       if (!ok) break;
-      // dK (scaled; warps of half 0) and dV (half 1) of this key tile.
-      // dV (the last product of the last block) done: both accumulators final.
+      // dK (scaled; warps of half 0) and dV (half 1) of this key tile, staged as bf16 in
+      // the item's K / V buffer (the 128B-swizzled layout the bulk tensor store reads).
+      // dV (the last product of the last block) done: both accumulators are final and
+      // every product of the item that read K or V has completed.
       if (!mbar_wait(&p_free[(g - 1) & 1], static_cast<uint32_t>((g - 1) >> 1) & 1u, p.status, 92, abort_flag)) break;
       tc_fence_after();
-      const int key = kt * 128 + krow;
       const float sc = half == 0 ? p.scale : 1.f;
       const uint32_t colx = half == 0 ? C::kColDK : C::kColDV;
-      uint8_t* row = reinterpret_cast<uint8_t*>(p.dqkv) +
-                     ((static_cast<long long>(b) * p.S + key) * p.lddq + static_cast<long long>(h) * 3 * D +
-                      (half + 1) * D) * 2;
+      uint8_t* stg = sKV + (2 * (t & 1) + half) * C::kTileBytes;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         tmem_ld_32x32b_x32(tmem + lane_base + colx + c * 32, o);
         tmem_ld_wait();
-        if (key < p.S) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            uint4 v;
-            v.x = pack_bf16x2(__uint_as_float(o[8 * k + 0]) * sc, __uint_as_float(o[8 * k + 1]) * sc);
-            v.y = pack_bf16x2(__uint_as_float(o[8 * k + 2]) * sc, __uint_as_float(o[8 * k + 3]) * sc);
-            v.z = pack_bf16x2(__uint_as_float(o[8 * k + 4]) * sc, __uint_as_float(o[8 * k + 5]) * sc);
-            v.w = pack_bf16x2(__uint_as_float(o[8 * k + 6]) * sc, __uint_as_float(o[8 * k + 7]) * sc);
-            *reinterpret_cast<uint4*>(row + c * 64 + k * 16) = v;
-          }
+        for (int k = 0; k < 4; ++k) {
+          uint8_t* dst = stg + (c >> 1) * 16384 + sw128_off(krow, (c & 1) * 4 + k);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(dst)),
+                       "r"(pack_bf16x2(__uint_as_float(o[8 * k + 0]) * sc, __uint_as_float(o[8 * k + 1]) * sc)),
+                       "r"(pack_bf16x2(__uint_as_float(o[8 * k + 2]) * sc, __uint_as_float(o[8 * k + 3]) * sc)),
+                       "r"(pack_bf16x2(__uint_as_float(o[8 * k + 4]) * sc, __uint_as_float(o[8 * k + 5]) * sc)),
+                       "r"(pack_bf16x2(__uint_as_float(o[8 * k + 6]) * sc, __uint_as_float(o[8 * k + 7]) * sc))
+                       : "memory");
         }
       }
+      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(dkv_free);
+      if (lane == 0) {
+        mbar_arrive(dkv_free);
+        mbar_arrive(&kv_staged[t & 1]);
+      }
+      ++t;
     }
   } else if (warp >= 2 + kBwdCompute) {
     // ------------------------------------------------------------ dQ drain (thread = query row)
-    // dQ_i leaves TMEM into the P^T buffer of its block once dV has consumed
-    // it (fp32, two 128 x 32 sub-tiles with the 128-byte swizzle), then one
-    // bulk tensor reduce-add per sub-tile adds it into the fp32 accumulator in
-    // global memory (the L2 reduces whole lines; rows past the sequence end
-    // are clipped by the tensor map).  The buffer is handed back to the compute
-    // warps once the bulk copies have read it.
+    // dQ_i leaves TMEM into the staging tile (fp32, two 128 x 32 sub-tiles with
+    // the 128-byte swizzle) once the previous block's reduce-adds have read it,
+    // then one bulk tensor reduce-add per sub-tile adds it into the fp32
+    // accumulator in global memory (the L2 reduces whole lines; rows past the
+    // sequence end are clipped by the tensor map).
     const int quarter = warp & 3;
     const int qrow = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
@@ -1110,12 +1187,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(dq_free);
-        // dV of this block has finished reading its P^T buffer.
-        if (!mbar_wait(&p_free[g & 1], static_cast<uint32_t>(g >> 1) & 1u, p.status, 96, abort_flag)) {
+        // The previous block's reduce-adds have read the staging tile.
+        if (g >= 1 && !mbar_wait(&pst_free[0], static_cast<uint32_t>(g - 1) & 1u, p.status, 96, abort_flag)) {
           ok = false;
           break;
         }
-        uint8_t* stg = sPt + (g & 1) * C::kPBytes;
+        uint8_t* stg = sStg;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c)
 #pragma unroll
@@ -1137,7 +1214,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
               bulk_commit_group();
               bulk_wait_read_all();
             }
-            mbar_arrive(&pst_free[g & 1]);
+            mbar_arrive(&pst_free[0]);
           }
         }
         ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
@@ -1745,9 +1822,9 @@ int bwd_tc_launch(const void* qkv, long long ldq, const void* dout, long long ld
                   float scale, void* status, cudaStream_t st) {
   using C = md::attn_tc::BwdCfg<D>;
   if (!get_encoder()) return -3;
-  CUtensorMap tq, tdo, tdq;
+  CUtensorMap tq, tdo, tdq, tout;
   if (!make_map_bsc(&tq, qkv, B, S, 3LL * H * D, ldq) || !make_map_bsc(&tdo, dout, B, S, 1LL * H * D, lddo) ||
-      !make_map_f32_bsc(&tdq, dqacc, B, S, 1LL * H * D, ldacc))
+      !make_map_f32_bsc(&tdq, dqacc, B, S, 1LL * H * D, ldacc) || !make_map_bsc(&tout, dqkv, B, S, 3LL * H * D, lddq))
     return -4;
   if (g_sms == 0) {
     int dev = 0;
@@ -1779,7 +1856,7 @@ int bwd_tc_launch(const void* qkv, long long ldq, const void* dout, long long ld
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
   const int grid = p.items < g_sms ? p.items : g_sms;
-  md::launch_pdl(k, grid, dim3(md::attn_tc::kBwdThreads), C::kSmemBytes, st, tq, tdo, tdq, p);
+  md::launch_pdl(k, grid, dim3(md::attn_tc::kBwdThreads), C::kSmemBytes, st, tq, tdo, tdq, tout, p);
   return static_cast<int>(cudaGetLastError());
 }
 
