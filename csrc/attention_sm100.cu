@@ -1261,13 +1261,14 @@ struct Bwd128Cfg {
   static constexpr int kKTile = 128 * D * 2;                  // K or V tile: 2 chunks [128][64]
   static constexpr int kQTile = kBQ * D * 2;                  // Q or dO tile: 2 chunks [64][64]
   static constexpr int kQChunk = kBQ * 128;                   // 8 KB
-  static constexpr int kQStages = 2;
-  static constexpr int kPBytes = 128 * kBQ * 2;               // P^T / dS^T [128 keys][64 queries]
+  static constexpr int kQStages = 3;
+  static constexpr int kPBytes = 128 * kBQ * 2;               // dS^T [128 keys][64 queries]
   static constexpr int kStgBytes = kBQ * D * 4;               // dQ staging, 4 boxes [64][32] fp32
-  static constexpr int kSmemData = 2 * kKTile + 2 * kQStages * kQTile + 3 * kPBytes + kStgBytes + 2 * 2 * kBQ * 4;
+  static constexpr int kSmemData = 2 * kKTile + 2 * kQStages * kQTile + kPBytes + kStgBytes + 2 * 2 * kBQ * 4;
   static constexpr int kSmemBytes = kSmemData + 256;
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kColS = 0, kColDP = 64, kColDQ = 128, kColDK = 256, kColDV = 384;
+  // P^T (bf16 pairs, 32 columns per buffer, two buffers) is the A operand of dV += P^T dO.
+  static constexpr uint32_t kColS = 0, kColDP = 64, kColDQ = 128, kColP = 192, kColDK = 256, kColDV = 384;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -1288,7 +1289,7 @@ struct Bwd128Params {
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd128_kernel(const __grid_constant__ CUtensorMap tmKV, const __grid_constant__ CUtensorMap tmQ,
                   const __grid_constant__ CUtensorMap tmDO, const __grid_constant__ CUtensorMap tmDQ,
-                  const __grid_constant__ Bwd128Params p) {
+                  const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ Bwd128Params p) {
   using C = Bwd128Cfg;
   constexpr int D = C::D;
   constexpr int QS = C::kQStages;
@@ -1302,30 +1303,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sV = sK + C::kKTile;
   uint8_t* sQ = sV + C::kKTile;                  // [QS]
   uint8_t* sdO = sQ + QS * C::kQTile;            // [QS]
-  uint8_t* sPt = sdO + QS * C::kQTile;           // [2] P^T
-  uint8_t* sdSt = sPt + 2 * C::kPBytes;          // dS^T
+  uint8_t* sdSt = sdO + QS * C::kQTile;          // dS^T
   uint8_t* sStg = sdSt + C::kPBytes;             // dQ staging (fp32)
   float* sL = reinterpret_cast<float*>(sStg + C::kStgBytes);  // [2][64] lse (log2 units)
   float* sDel = sL + 2 * BQ;                                    // [2][64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDel + 2 * BQ);
+  static_assert(QS == 3, "barrier slots below are laid out for three Q/dO stages");
   uint64_t* kv_full = bars + 0;
-  uint64_t* kv_empty = bars + 1;
-  uint64_t* qd_full = bars + 2;    // [2]
-  uint64_t* qd_empty = bars + 4;   // [2]
-  uint64_t* sd_full = bars + 6;
-  uint64_t* sd_free = bars + 7;
-  uint64_t* pds_full = bars + 8;
-  uint64_t* p_free = bars + 9;     // [2] dV done reading P^T buffer
-  uint64_t* ds_free = bars + 11;   // dK and dQ^T done reading dS^T
-  uint64_t* dq_full = bars + 12;
-  uint64_t* dq_free = bars + 13;
-  uint64_t* dkv_free = bars + 14;
-  uint64_t* drain = bars + 15;
-  uint64_t* stage_bar = bars + 16;  // [2]
-  uint64_t* stg_free = bars + 18;   // staging tile read by the bulk reduce-adds
-  uint64_t* dq_staged = bars + 19;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 21);
+  uint64_t* kv_staged = bars + 1;  // the item's dK / dV are in the K / V buffers
+  uint64_t* qd_full = bars + 2;    // [3]
+  uint64_t* qd_empty = bars + 5;   // [3]
+  uint64_t* sd_full = bars + 8;
+  uint64_t* sd_free = bars + 9;
+  uint64_t* pds_full = bars + 10;
+  uint64_t* p_free = bars + 11;    // [2] dV done reading P^T buffer
+  uint64_t* ds_free = bars + 13;   // dK and dQ^T done reading dS^T
+  uint64_t* dq_full = bars + 14;
+  uint64_t* dq_free = bars + 15;
+  uint64_t* dkv_free = bars + 16;
+  uint64_t* drain = bars + 17;
+  uint64_t* stage_bar = bars + 18;  // [2]
+  uint64_t* stg_free = bars + 20;   // staging tile read by the bulk reduce-adds
+  uint64_t* dq_staged = bars + 21;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 23);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1333,7 +1334,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(kv_empty, 1);
+    mbar_init(kv_staged, kBwdCompute);
     for (int i = 0; i < QS; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
@@ -1357,6 +1358,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmDO);
     tma_prefetch_desc(&tmDQ);
+    tma_prefetch_desc(&tmOut);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -1374,12 +1376,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     int kv_armed = -1;
     int q_armed[QS];
     for (int i = 0; i < QS; ++i) q_armed[i] = -1;
+    // Store item ti's dK / dV (staged by the compute warps in the K / V buffers).
+    auto store_dkv = [&](int ti) -> bool {
+      if (!mbar_wait(kv_staged, static_cast<uint32_t>(ti) & 1u, p.status, 164, abort_flag)) return false;
+      const int w = blockIdx.x + ti * gridDim.x;
+      const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        if (c * 64 >= p.dr) break;
+        tma_store_4d(&tmOut, sK + c * 16384, c * 64, 3 * h + 1, kt * 128, b);
+        tma_store_4d(&tmOut, sV + c * 16384, c * 64, 3 * h + 2, kt * 128, b);
+      }
+      bulk_commit_group();
+      return true;
+    };
     int g = 0, t = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x, ++t) {
       const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
       const uint32_t tph = static_cast<uint32_t>(t) & 1u;
-      if (!mbar_wait(kv_empty, tph ^ 1u, p.status, 160, abort_flag)) break;
+      if (t >= 1) {
+        // The previous item's dK / dV leave the K / V buffers before they are reloaded.
+        if (!store_dkv(t - 1)) break;
+        bulk_wait_read_all();
+      }
       mbar_arrive_expect_tx(kv_full, 2 * C::kKTile);
       kv_armed = static_cast<int>(tph);
 #pragma unroll
@@ -1403,6 +1423,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
     }
+    if (ok && t >= 1) store_dkv(t - 1);
+    bulk_wait_all();
     if (kv_armed >= 0) mbar_wait(kv_full, static_cast<uint32_t>(kv_armed), p.status, 162, nullptr);
     for (int i = 0; i < QS; ++i)
       if (q_armed[i] >= 0) mbar_wait(&qd_full[i], static_cast<uint32_t>(q_armed[i]), p.status, 163, nullptr);
@@ -1418,11 +1440,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint64_t dQ_mn = sdesc_sw128(smem_u32(sQ), C::kQChunk, 1024);
     const uint64_t ddO_k = sdesc_sw128(smem_u32(sdO), 16, 1024);
     const uint64_t ddO_mn = sdesc_sw128(smem_u32(sdO), C::kQChunk, 1024);
-    const uint64_t dP_k = sdesc_sw128(smem_u32(sPt), 16, 1024);
     const uint64_t ddS_k = sdesc_sw128(smem_u32(sdSt), 16, 1024);
     const uint64_t ddS_mn = sdesc_sw128(smem_u32(sdSt), 16384, 1024);
     constexpr uint32_t kQT16 = C::kQTile >> 4;
-    constexpr uint32_t kP16 = C::kPBytes >> 4;
     int g = 0, t = 0;
     bool ok = true;
     auto issue_scores = [&](int gg) -> bool {
@@ -1450,9 +1470,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int u = 0; u < n; ++u, ++g) {
         const int st = g % QS;
         const int pb = g & 1;
-        if (u + 1 < n && !issue_scores(g + 1)) {
-          ok = false;
-          break;
+        // The next block's score products go first once their Q / dO tile has landed;
+        // if this block's P / dS arrive before that, this block's products go first.
+        bool scores_after = false;
+        if (u + 1 < n) {
+          const int st1 = (g + 1) % QS;
+          const uint64_t t0 = globaltimer_ns();
+          for (uint32_t it = 0;; ++it) {
+            if (mbar_test_wait(&qd_full[st1], static_cast<uint32_t>((g + 1) / QS) & 1u) &&
+                mbar_test_wait(sd_free, (static_cast<uint32_t>(g + 1) & 1u) ^ 1u))
+              break;
+            if (mbar_test_wait(pds_full, static_cast<uint32_t>(g) & 1u)) {
+              scores_after = true;
+              break;
+            }
+            if ((it & 63u) == 63u && (*abort_flag || globaltimer_ns() - t0 > kPipelineTimeoutNs)) {
+              if (!*abort_flag) {
+                report(p.status, kTimeoutPipeline, 177, 0);
+                *abort_flag = 1;
+              }
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) break;
+          if (!scores_after && !issue_scores(g + 1)) {
+            ok = false;
+            break;
+          }
         }
         if (!mbar_wait(pds_full, static_cast<uint32_t>(g) & 1u, p.status, 173, abort_flag)) {
           ok = false;
@@ -1464,7 +1509,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         tc_fence_after();
         const uint64_t qmn = dQ_mn + st * kQT16, omn = ddO_mn + st * kQT16;
-        const uint64_t pk = dP_k + pb * kP16;
         const uint32_t acc0 = u > 0 ? 1u : 0u;
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)
@@ -1479,14 +1523,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_bf16_ss_elect(tmem + C::kColDQ, dK_mn + kk * 128, ddS_mn + kk * 128, idQT, kk > 0 ? 1u : 0u);
         umma_commit_elect(ds_free);
         umma_commit_elect(dq_full);
+        // dV += P^T dO with P^T from TMEM buffer pb (8 columns per 16 queries).
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)
-          umma_bf16_ss_elect(tmem + C::kColDV, pk + ((kk * 32) >> 4), omn + kk * 128, idKV, (acc0 | kk) ? 1u : 0u);
+          umma_bf16_ts_elect(tmem + C::kColDV, tmem + C::kColP + static_cast<uint32_t>(pb * 32 + kk * 8), omn + kk * 128,
+                             idKV, (acc0 | kk) ? 1u : 0u);
         umma_commit_elect(&qd_empty[st]);
         umma_commit_elect(&p_free[pb]);
+        if (scores_after && !issue_scores(g + 1)) {
+          ok = false;
+          break;
+        }
       }
       if (!ok) break;
-      umma_commit_elect(kv_empty);
     }
     umma_commit_elect(drain);
     mbar_wait(drain, 0, p.status, 176, nullptr);
@@ -1533,7 +1582,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     int g = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < p.items && ok; w += gridDim.x) {
-      const int kt = w / bhc, bh = w % bhc, b = bh / p.H, h = bh % p.H;
+      const int kt = w / bhc;
       const int n = p.n_qb - 2 * kt;
       for (int u = 0; u < n; ++u, ++g) {
         if (!mbar_wait(&stage_bar[g & 1], static_cast<uint32_t>(g >> 1) & 1u, p.status, 179, abort_flag)) {
@@ -1586,54 +1635,55 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           pre_i = i2;
           if (w2 >= 0) pre = load_raw(w2, i2);
         }
-        uint8_t* sP = sPt + (g & 1) * C::kPBytes;
+        // P^T to TMEM buffer g & 1 (16 columns = these 32 queries), dS^T to shared memory.
+        tc_fence_after();
+        tmem_st_32x32b_x16(tmem + lane_base + C::kColP + static_cast<uint32_t>((g & 1) * 32 + half * 16), pp);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const uint32_t off = sw128_off(krow, half * 4 + k);
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(sP + off)), "r"(pp[4 * k]),
-                       "r"(pp[4 * k + 1]), "r"(pp[4 * k + 2]), "r"(pp[4 * k + 3])
-                       : "memory");
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(sdSt + off)), "r"(dd[4 * k]),
                        "r"(dd[4 * k + 1]), "r"(dd[4 * k + 2]), "r"(dd[4 * k + 3])
                        : "memory");
         }
+        tmem_st_wait();
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(pds_full);
       }
       if (!ok) break;
-      // dV of the last block done: dK and dV of this key tile are final.
+      // dV of the last block done: dK and dV of this key tile are final and every product
+      // that read K or V has completed.  Stage them (bf16, the 128B-swizzled layout of the
+      // K / V tiles: half 0 dK into the K buffer, half 1 dV into the V buffer) for the
+      // TMA warp's bulk tensor stores, which clip columns past dr and rows past S.
       if (!mbar_wait(&p_free[(g - 1) & 1], static_cast<uint32_t>((g - 1) >> 1) & 1u, p.status, 183, abort_flag)) break;
       tc_fence_after();
-      const int key = kt * 128 + krow;
       const float sc = half == 0 ? p.scale : 1.f;
       const uint32_t colx = half == 0 ? C::kColDK : C::kColDV;
-      uint8_t* row = reinterpret_cast<uint8_t*>(p.dqkv) +
-                     ((static_cast<long long>(b) * p.S + key) * p.lddq + static_cast<long long>(h) * 3 * p.dr +
-                      (half + 1) * p.dr) * 2;
+      uint8_t* stg = half == 0 ? sK : sV;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
-        if (c * 32 >= p.dr) break;  // uniform
         uint32_t o[32];
         tmem_ld_32x32b_x32(tmem + lane_base + colx + c * 32, o);
         tmem_ld_wait();
-        if (key < p.S) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            if (c * 32 + k * 8 >= p.dr) break;
-            uint4 v;
-            v.x = pack_bf16x2(__uint_as_float(o[8 * k + 0]) * sc, __uint_as_float(o[8 * k + 1]) * sc);
-            v.y = pack_bf16x2(__uint_as_float(o[8 * k + 2]) * sc, __uint_as_float(o[8 * k + 3]) * sc);
-            v.z = pack_bf16x2(__uint_as_float(o[8 * k + 4]) * sc, __uint_as_float(o[8 * k + 5]) * sc);
-            v.w = pack_bf16x2(__uint_as_float(o[8 * k + 6]) * sc, __uint_as_float(o[8 * k + 7]) * sc);
-            *reinterpret_cast<uint4*>(row + c * 64 + k * 16) = v;
-          }
+        for (int k = 0; k < 4; ++k) {
+          uint8_t* dst = stg + (c >> 1) * 16384 + sw128_off(krow, (c & 1) * 4 + k);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(dst)),
+                       "r"(pack_bf16x2(__uint_as_float(o[8 * k + 0]) * sc, __uint_as_float(o[8 * k + 1]) * sc)),
+                       "r"(pack_bf16x2(__uint_as_float(o[8 * k + 2]) * sc, __uint_as_float(o[8 * k + 3]) * sc)),
+                       "r"(pack_bf16x2(__uint_as_float(o[8 * k + 4]) * sc, __uint_as_float(o[8 * k + 5]) * sc)),
+                       "r"(pack_bf16x2(__uint_as_float(o[8 * k + 6]) * sc, __uint_as_float(o[8 * k + 7]) * sc))
+                       : "memory");
         }
       }
+      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(dkv_free);
+      if (lane == 0) {
+        mbar_arrive(dkv_free);
+        mbar_arrive(kv_staged);
+      }
     }
   } else if (warp >= 2 + kBwdCompute) {
     // ------------------------------------------------------------ dQ drain (thread = head-dim row)
@@ -1867,9 +1917,10 @@ int bwd128_tc_launch(const void* qkv, long long ldq, const void* dout, long long
   using C = md::attn_tc::Bwd128Cfg;
   if (!get_encoder()) return -3;
   if (dr % 8 || dr > 128 || dr < 72 || ldacc != static_cast<long long>(H) * dr) return -2;
-  CUtensorMap tkv, tq, tdo, tdq;
+  CUtensorMap tkv, tq, tdo, tdq, tout;
   if (!make_map_bshd(&tkv, qkv, B, S, 3 * H, dr, ldq, 128) || !make_map_bshd(&tq, qkv, B, S, 3 * H, dr, ldq, 64) ||
-      !make_map_bshd(&tdo, dout, B, S, H, dr, lddo, 64) || !make_map_f32_bshd(&tdq, dqacc, B, S, H, dr, ldacc, 64))
+      !make_map_bshd(&tdo, dout, B, S, H, dr, lddo, 64) || !make_map_f32_bshd(&tdq, dqacc, B, S, H, dr, ldacc, 64) ||
+      !make_map_bshd(&tout, dqkv, B, S, 3 * H, dr, lddq, 128))
     return -4;
   if (g_sms == 0) {
     int dev = 0;
@@ -1895,7 +1946,7 @@ int bwd128_tc_launch(const void* qkv, long long ldq, const void* dout, long long
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
   const int grid = p.items < g_sms ? p.items : g_sms;
-  md::launch_pdl(k, grid, dim3(md::attn_tc::kBwdThreads), C::kSmemBytes, st, tkv, tq, tdo, tdq, p);
+  md::launch_pdl(k, grid, dim3(md::attn_tc::kBwdThreads), C::kSmemBytes, st, tkv, tq, tdo, tdq, tout, p);
   return static_cast<int>(cudaGetLastError());
 }
 
