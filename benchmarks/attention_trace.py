@@ -69,8 +69,9 @@ def main(argv=None) -> int:
 
 def _bwd(K, nat, qkv, B, H, S, D, a) -> int:
     """Backward trace (head_dim 64 kernel).  Compute-warp slots: 1 scores ready, 2 first
-    half of P / dS computed, 3 P / dS buffers free, 16.. P / dS handed to the MMA warp (per
-    warp); MMA slots 12 scores issued, 5 P / dS received, 7 dQ TMEM free, 8 dV issued;
+    half of P / dS computed, 3 P / dS buffers free, 4 next block's lse / delta staged, 10
+    first half stored, 13 / 14 second half's score load issued / complete, 15 second half
+    computed, 16.. P / dS handed to the MMA warp (per warp); MMA slots 12 scores issued, 5 P / dS received, 7 dQ TMEM free, 8 dV issued;
     9 dQ drained; 11 Q / dO load issued."""
     import torch
 
@@ -86,6 +87,11 @@ def _bwd(K, nat, qkv, B, H, S, D, a) -> int:
     out = {"shape": [B, H, S, D], "blocks": len(rows)}
     out["scores ready -> first half computed"] = med([r[2] - r[1] for _, r in rows if r[2]])
     out["first half -> buffers free"] = med([r[3] - r[2] for _, r in rows if r[3] and r[2]])
+    out["buffers free -> next lse / delta staged"] = med([r[4] - r[3] for _, r in rows if r[4] and r[3]])
+    out["-> first half P^T / dS^T stored"] = med([r[10] - r[4] for _, r in rows if r[10] and r[4]])
+    out["-> second half scores loaded"] = med([r[14] - r[10] for _, r in rows if r[14] and r[10]])
+    out["-> second half computed"] = med([r[15] - r[14] for _, r in rows if r[15] and r[14]])
+    out["-> P / dS handed (warp 2)"] = med([r[16] - r[15] for _, r in rows if r[15]])
     out["buffers free -> P / dS handed (warp 2)"] = med([r[16] - r[3] for _, r in rows if r[3]])
     periods = [tr[g + 1][1] - tr[g][1] for g in range(a.skip, 63) if tr[g][1] and tr[g + 1][1]]
     out["block period (median)"] = med(periods)

@@ -996,11 +996,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // the start of block g+1, normally already complete).  The load for block
     // g+2 uses a clamped index and is only scaled when stored, so no
     // arithmetic waits on it meanwhile.
-    auto load_raw = [&](int w_, int i_) -> float {
-      const int q = min(i_ * 128 + (ct & 127), p.S - 1);
-      const long long idx = static_cast<long long>(w_ % bhc) * p.S + q;
-      return ct < 128 ? p.lse[idx] : p.delta[idx];
-    };
+    // The prefetch walks this CTA's blocks with a row pointer per item (one integer
+    // division per item, none per block); the value is loaded a block before it is staged.
+    const float* const src = ct < 128 ? p.lse : p.delta;
+    auto row_of = [&](int w_) -> const float* { return src + static_cast<long long>(w_ % bhc) * p.S; };
+    auto load_raw = [&](const float* row, int i_) -> float { return row[min(i_ * 128 + (ct & 127), p.S - 1)]; };
     auto stage = [&](int gg, int i_, float raw) {
       const int q = i_ * 128 + (ct & 127);
       const float v = ct < 128 ? (q < p.S ? raw * 1.4426950408889634f : INFINITY) : (q < p.S ? raw : 0.f);
@@ -1011,25 +1011,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mbar_arrive(&stage_bar[gg & 1]);
       }
     };
-    // The block after (w_, i_) in this CTA's work list: (item, query tile) or w = -1.
-    auto next_block = [&](int w_, int i_, int& wn, int& in) {
+    // Advance (w_, i_, row) to the next block of this CTA's work list (w_ = -1 past the end).
+    auto next_block = [&](int& w_, int& i_, const float*& row) {
       if (i_ + 1 < p.n_t) {
-        wn = w_;
-        in = i_ + 1;
+        ++i_;
       } else if (w_ + static_cast<int>(gridDim.x) < p.items) {
-        wn = w_ + static_cast<int>(gridDim.x);
-        in = wn / bhc;
+        w_ += static_cast<int>(gridDim.x);
+        i_ = w_ / bhc;
+        row = row_of(w_);
       } else {
-        wn = -1;
+        w_ = -1;
       }
     };
     float pre = 0.f;
     int pre_w = -1, pre_i = 0;  // block whose raw value `pre` holds
+    const float* pre_row = src;
     if (static_cast<int>(blockIdx.x) < p.items) {
-      const int kt0 = blockIdx.x / bhc;
-      stage(0, kt0, load_raw(blockIdx.x, kt0));
-      next_block(blockIdx.x, kt0, pre_w, pre_i);
-      if (pre_w >= 0) pre = load_raw(pre_w, pre_i);
+      pre_w = blockIdx.x;
+      pre_i = pre_w / bhc;
+      pre_row = row_of(pre_w);
+      stage(0, pre_i, load_raw(pre_row, pre_i));
+      next_block(pre_w, pre_i, pre_row);
+      pre = load_raw(pre_row, pre_i);  // unconditional (a valid row): no select on the loaded value
     }
     int g = 0, t = 0;
     bool ok = true;
@@ -1067,20 +1070,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             if (lane == 0) mbar_arrive(sd_free);
           }
           uint32_t pp[16], dd[16];
+          float4 l4, d4;  // lse / delta of four queries (one 16-byte broadcast load each)
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
             const int qc = c * 32 + e;  // within this half
-            float p0 = ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -L[qc]));
-            float p1 = ex2(fmaf(__uint_as_float(sv[e + 1]), p.scale_log2, -L[qc + 1]));
+            if ((e & 3) == 0) {
+              l4 = *reinterpret_cast<const float4*>(L + qc);
+              d4 = *reinterpret_cast<const float4*>(Dl + qc);
+            }
+            const float la = (e & 3) ? l4.z : l4.x, lb = (e & 3) ? l4.w : l4.y;
+            const float da = (e & 3) ? d4.z : d4.x, db = (e & 3) ? d4.w : d4.y;
+            float p0 = ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -la));
+            float p1 = ex2(fmaf(__uint_as_float(sv[e + 1]), p.scale_log2, -lb));
             if (u == 0) {  // diagonal block: query < key is masked
               if (half * 64 + qc < krow) p0 = 0.f;
               if (half * 64 + qc + 1 < krow) p1 = 0.f;
             }
-            const float g0 = p0 * (__uint_as_float(dv[e]) - Dl[qc]);
-            const float g1 = p1 * (__uint_as_float(dv[e + 1]) - Dl[qc + 1]);
+            const float g0 = p0 * (__uint_as_float(dv[e]) - da);
+            const float g1 = p1 * (__uint_as_float(dv[e + 1]) - db);
             pp[e >> 1] = pack_bf16x2(p0, p1);
             dd[e >> 1] = pack_bf16x2(g0, g1);
           }
+          if (c == 1 && threadIdx.x == 64) MD_TRACE(g, 15);
           if (c == 0) {
             if (threadIdx.x == 64) MD_TRACE(g, 2);
             // dV of block g-1 has finished reading P^T (TMEM); dK/dQ of block g-1
@@ -1092,15 +1103,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
               break;
             }
             if (threadIdx.x == 64) MD_TRACE(g, 3);
-            // Stage the next block's lse/delta (buffer (g+1) & 1 is free: see above).
-            if (pre_w >= 0) {
-              stage(g + 1, pre_i, pre);
-              int w2, i2;
-              next_block(pre_w, pre_i, w2, i2);
-              pre_w = w2;
-              pre_i = i2;
-              if (w2 >= 0) pre = load_raw(w2, i2);
-            }
           }
           // P^T to TMEM (16 columns = these 32 queries), dS^T to shared memory.
           tc_fence_after();
@@ -1112,6 +1114,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                          "r"(dd[4 * k + 1]), "r"(dd[4 * k + 2]), "r"(dd[4 * k + 3])
                          : "memory");
           }
+          if (c == 0 && threadIdx.x == 64) MD_TRACE(g, 10);
         }
         if (!ok) break;
         tmem_st_wait();
@@ -1122,6 +1125,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           MD_TRACE(g, 16 + warp - 2);
           mbar_arrive(pds_full);
         }
+        // Stage the next block's lse/delta (buffer (g+1) & 1 is free: the wait for dK/dQ
+        // of block g-1 above implies every compute warp has finished block g-1), off the
+        // path to the P/dS hand-off.
+        if (pre_w >= 0) {
+          stage(g + 1, pre_i, pre);
+          next_block(pre_w, pre_i, pre_row);
+          pre = load_raw(pre_row, pre_i);
+        }
+        if (threadIdx.x == 64) MD_TRACE(g, 4);
       }
       if (!ok) break;
       // dK (scaled; warps of half 0) and dV (half 1) of this key tile, staged as bf16 in
@@ -1546,11 +1558,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int krow = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int ct = threadIdx.x - 64;  // 0..255: 0..63 stage lse, 64..127 delta
-    auto load_raw = [&](int w_, int i_) -> float {
-      const int q = min(i_ * BQ + (ct & 63), p.S - 1);
-      const long long idx = static_cast<long long>(w_ % bhc) * p.S + q;
-      return ct < 64 ? p.lse[idx] : (ct < 128 ? p.delta[idx] : 0.f);
-    };
+    // The prefetch walks this CTA's blocks with a row pointer per item (one integer
+    // division per item, none per block); the value is loaded a block before it is staged
+    // (threads 128.. load a value they never stage).
+    const float* const src = ct < 64 ? p.lse : p.delta;
+    auto row_of = [&](int w_) -> const float* { return src + static_cast<long long>(w_ % bhc) * p.S; };
+    auto load_raw = [&](const float* row, int i_) -> float { return row[min(i_ * BQ + (ct & 63), p.S - 1)]; };
     auto stage = [&](int gg, int i_, float raw) {
       if (ct < 128) {
         const int q = i_ * BQ + (ct & 63);
@@ -1560,24 +1573,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&stage_bar[gg & 1]);
     };
-    auto next_block = [&](int w_, int i_, int& wn, int& in) {
+    // Advance (w_, i_, row) to the next block of this CTA's work list (w_ = -1 past the end).
+    auto next_block = [&](int& w_, int& i_, const float*& row) {
       if (i_ + 1 < p.n_qb) {
-        wn = w_;
-        in = i_ + 1;
+        ++i_;
       } else if (w_ + static_cast<int>(gridDim.x) < p.items) {
-        wn = w_ + static_cast<int>(gridDim.x);
-        in = 2 * (wn / bhc);
+        w_ += static_cast<int>(gridDim.x);
+        i_ = 2 * (w_ / bhc);
+        row = row_of(w_);
       } else {
-        wn = -1;
+        w_ = -1;
       }
     };
     float pre = 0.f;
     int pre_w = -1, pre_i = 0;
+    const float* pre_row = src;
     if (static_cast<int>(blockIdx.x) < p.items) {
-      const int i0 = 2 * (static_cast<int>(blockIdx.x) / bhc);
-      stage(0, i0, load_raw(blockIdx.x, i0));
-      next_block(blockIdx.x, i0, pre_w, pre_i);
-      if (pre_w >= 0) pre = load_raw(pre_w, pre_i);
+      pre_w = blockIdx.x;
+      pre_i = 2 * (pre_w / bhc);
+      pre_row = row_of(pre_w);
+      stage(0, pre_i, load_raw(pre_row, pre_i));
+      next_block(pre_w, pre_i, pre_row);
+      pre = load_raw(pre_row, pre_i);  // unconditional (a valid row): no select on the loaded value
     }
     int g = 0;
     bool ok = true;
@@ -1607,16 +1624,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         // Diagonal: query q_abs < key k_abs is masked; only the first two blocks can hold such pairs.
         const int qoff = (2 * kt + u) * BQ + half * 32 - (kt * 128 + krow);  // q_abs - k_abs at column 0
         uint32_t pp[16], dd[16];
+        float4 l4, d4;  // lse / delta of four queries (one 16-byte broadcast load each)
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float p0 = ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -L[e]));
-          float p1 = ex2(fmaf(__uint_as_float(sv[e + 1]), p.scale_log2, -L[e + 1]));
+          if ((e & 3) == 0) {
+            l4 = *reinterpret_cast<const float4*>(L + e);
+            d4 = *reinterpret_cast<const float4*>(Dl + e);
+          }
+          const float la = (e & 3) ? l4.z : l4.x, lb = (e & 3) ? l4.w : l4.y;
+          const float da = (e & 3) ? d4.z : d4.x, db = (e & 3) ? d4.w : d4.y;
+          float p0 = ex2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -la));
+          float p1 = ex2(fmaf(__uint_as_float(sv[e + 1]), p.scale_log2, -lb));
           if (u < 2) {
             if (qoff + e < 0) p0 = 0.f;
             if (qoff + e + 1 < 0) p1 = 0.f;
           }
-          const float g0 = p0 * (__uint_as_float(dv[e]) - Dl[e]);
-          const float g1 = p1 * (__uint_as_float(dv[e + 1]) - Dl[e + 1]);
+          const float g0 = p0 * (__uint_as_float(dv[e]) - da);
+          const float g1 = p1 * (__uint_as_float(dv[e + 1]) - db);
           pp[e >> 1] = pack_bf16x2(p0, p1);
           dd[e >> 1] = pack_bf16x2(g0, g1);
         }
@@ -1626,14 +1650,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             (g >= 1 && !mbar_wait(ds_free, static_cast<uint32_t>(g - 1) & 1u, p.status, 182, abort_flag))) {
           ok = false;
           break;
-        }
-        if (pre_w >= 0) {
-          stage(g + 1, pre_i, pre);
-          int w2, i2;
-          next_block(pre_w, pre_i, w2, i2);
-          pre_w = w2;
-          pre_i = i2;
-          if (w2 >= 0) pre = load_raw(w2, i2);
         }
         // P^T to TMEM buffer g & 1 (16 columns = these 32 queries), dS^T to shared memory.
         tc_fence_after();
@@ -1650,6 +1666,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(pds_full);
+        // Stage the next block's lse/delta (its buffer is free: see the waits above), off
+        // the path to the P/dS hand-off.
+        if (pre_w >= 0) {
+          stage(g + 1, pre_i, pre);
+          next_block(pre_w, pre_i, pre_row);
+          pre = load_raw(pre_row, pre_i);
+        }
       }
       if (!ok) break;
       // dV of the last block done: dK and dV of this key tile are final and every product
