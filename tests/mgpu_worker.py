@@ -457,17 +457,18 @@ def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", rank))
+    checks = {"allreduce": check_allreduce, "gemm_ar": check_gemm_ar, "ddp": check_ddp, "fsdp": check_fsdp,
+              "tp_gpt": check_tp_gpt, "tp_embedding": check_tp_embedding, "graphs": check_graphs,
+              "pipeline": check_pipeline, "composition": check_composition, "fsdp_training": check_fsdp_training}
+    # MGPU_CHECKS=name,name runs a subset (same order); default: all of them.
+    wanted = [c for c in os.environ.get("MGPU_CHECKS", "").split(",") if c] or list(checks)
+    unknown = [c for c in wanted if c not in checks]
+    if unknown:
+        raise SystemExit(f"unknown checks {unknown}; known: {list(checks)}")
     try:
-        check_allreduce(rank, world)
-        check_gemm_ar(rank, world)
-        check_ddp(rank, world)
-        check_fsdp(rank, world)
-        check_tp_gpt(rank, world)
-        check_tp_embedding(rank, world)
-        check_graphs(rank, world)
-        check_pipeline(rank, world)
-        check_composition(rank, world)
-        check_fsdp_training(rank, world)
+        for name in checks:
+            if name in wanted:
+                checks[name](rank, world)
     finally:
         symm.release_all()
         dist.barrier()
