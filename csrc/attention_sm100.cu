@@ -695,10 +695,6 @@ struct BwdParams {
     if (kTrace && blockIdx.x == 0 && (gg) < 64) p.trace[(gg) * 32 + (slot)] = clock64();   \
   } while (0)
 
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
 
 template <int D, bool kTrace>
 __global__ void __launch_bounds__(kBwdThreads, 1)
