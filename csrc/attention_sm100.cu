@@ -1245,23 +1245,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // accumulators = 256 + 3 D TMEM columns, 640 at D = 128 (512 exist).  This
 // kernel walks each 128-key tile's queries in blocks of 64 and computes dQ
 // transposed, dQ^T = K^T dS^T (M = D = 128 rows, N = 64 queries), so
-//   S^T 64 | dP^T 64 | dQ^T 64 | (64 spare) | dK 128 | dV 128  = 512 columns.
+//   S^T 64 | dP^T 64 | dQ^T 64 | P^T 2 x 32 | dK 128 | dV 128  = 512 columns.
 // Per 64-query block i of key tile kt:
 //   S^T  = K Q_i^T,  dP^T = V dO_i^T                 (M 128 keys, N 64)
-//   P^T  = exp(S^T scale - lse_i),  dS^T = P^T (dP^T - delta_i)   [compute warps, bf16 to smem]
-//   dK  += dS^T Q_i,  dV += P^T dO_i                 (M 128 keys, N D, K 64)
+//   P^T  = exp(S^T scale - lse_i),  dS^T = P^T (dP^T - delta_i)   [compute warps, bf16:
+//                                                     P^T to TMEM, dS^T to shared memory]
+//   dK  += dS^T Q_i,  dV += P^T dO_i                 (M 128 keys, N D, K 64; dV reads P^T
+//                                                     from TMEM as its A operand)
 //   dQ_i^T = K^T dS^T                                (M D, N 64, K 128 keys; both operands MN-major)
 // Roles as in the head_dim 64 kernel: warp 0 TMA, warp 1 MMA, warps 2..9
 // compute (thread = key row; warps 2..5 take query columns 0..31 of the
 // block, 6..9 columns 32..63), warps 10..13 drain dQ^T (thread = head-dim
 // row) into a dedicated fp32 staging tile [64 queries][128] (four 128B-
 // swizzled boxes of 32 columns) and one bulk tensor reduce-add per box into
-// the fp32 accumulator.  Two Q/dO stages (the smem budget), P^T double-
-// buffered, dS^T single-buffered; the next block's score products are queued
-// as soon as the compute warps hold the current scores in registers.
+// the fp32 accumulator.  Three Q/dO stages, P^T double-buffered in TMEM,
+// dS^T single-buffered; the MMA warp queues the next block's score products as
+// soon as the compute warps hold the current scores in registers and the next
+// Q/dO tile has landed, or after the current block's products when its P/dS
+// are ready first.  K/V stay single-buffered (shared memory has no room for a
+// second 64 KB pair): an item's dK / dV are staged bf16 in the K / V buffers and
+// written by the TMA warp's bulk tensor stores before it reloads them.
 // Real head_dim dr <= 128: every tensor map is 4-D [B, S, slots, dr], so
-// boxes read zeros past dr and the dQ reduce-add clips there; only dr
-// columns of dK / dV are stored.
+// boxes read zeros past dr and the dQ reduce-add and the dK / dV stores clip
+// there.
 // ===========================================================================
 struct Bwd128Cfg {
   static constexpr int D = 128;
