@@ -643,11 +643,12 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kCtasPerSm)
 // when this block's P^T/dS^T are ready first, right after this block's
 // products), then dK and dQ (which read dS^T; a single buffer, released as
 // soon as they are done), then dV (which reads P^T; the compute warps write the
-// next block's P^T once it has finished).  Q/dO tiles stream through three stages.  K/V are double-buffered: the next item's tiles load while this
-// item runs, and a finished item's dK / dV are staged (bf16, 128B-swizzled) in its own
-// K / V buffers and written by the TMA warp with bulk tensor stores, after which the
-// buffers are reloaded -- so an item boundary costs neither a K/V load nor the compute
-// warps' time for scattered global stores.
+// next block's P^T once it has finished).  Q/dO tiles stream through three
+// stages.  K/V are double-buffered: the next item's tiles load while this item
+// runs, and a finished item's dK / dV are staged (bf16, 128B-swizzled) in its
+// own K / V buffers and written by the TMA warp with bulk tensor stores, after
+// which the buffers are reloaded -- so an item boundary costs neither a K/V
+// load nor the compute warps' time for scattered global stores.
 // ===========================================================================
 constexpr int kBwdThreads = 448;
 constexpr int kBwdCompute = 8;  // compute warps
