@@ -39,6 +39,13 @@ def test_both_arms_same_loss(config, n, port):
     ours = _bench(n, port + 1, "--impl", "ours", "--config", config)
     assert ref["impl"] == "reference" and "impl" not in ours
     for out in (ref, ours):
+        # The driver's contract: one JSON line with these keys on both arms.
+        for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                    "scaling", "vs_baseline", "dtype", "data", "config", "e2e", "gpu_launches"):
+            assert key in out, (key, out)
+        for key in ("model", "global_batch", "seq_len", "parallelism"):
+            assert key in out["config"], (key, out["config"])
+        assert out["metric"] == ref["metric"] and out["higher_is_better"] is True
         assert out["n_gpus"] == n and out["steps"] == 2 and out["warmup"] == 1
         assert out["value"] > 0 and out["e2e"]["value"] > 0
         assert out["config"]["name"] == config
